@@ -1,0 +1,79 @@
+"""Loader for the native crumpet_b200 libraries.
+
+``libcrumpet_b200.so`` (kernels + C ABI) and ``_C.so`` (the ``crumpet_ops``
+torch dispatcher registration) are built in-tree by ``crumpet_b200._build``.
+There is no fallback: if the libraries are missing, every op raises with the
+load error, so a silent CPU or eager path can never stand in for a kernel.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libcrumpet_b200.so"
+EXT_PATH = _PKG / "_C.so"
+
+_load_error: Exception | None = None
+ops = None
+
+try:
+    torch.ops.load_library(str(EXT_PATH))
+    ops = torch.ops.crumpet_ops
+except Exception as exc:  # pragma: no cover - exercised only without a build
+    _load_error = exc
+
+
+def available() -> bool:
+    return ops is not None
+
+
+def require():
+    """Return ``torch.ops.crumpet_ops`` or raise the reason it is unavailable."""
+    if ops is None:
+        raise RuntimeError(
+            "crumpet_b200 native kernels are not built or failed to load "
+            f"({EXT_PATH}): {_load_error!r}. Run `python -m crumpet_b200._build`."
+        )
+    return ops
+
+
+_capi = None
+
+
+def capi() -> ctypes.CDLL:
+    """The C ABI library (include/crumpet_b200.h) opened through ctypes."""
+    global _capi
+    if _capi is None:
+        lib = ctypes.CDLL(str(LIB_PATH))
+        i64, vp, i32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
+        copy_args = [vp, vp, i32] + [i64] * 11 + [vp]
+        for name in (
+            "crumpet_fused_shift_partition_3d",
+            "crumpet_fused_unshift_unpartition_3d",
+            "crumpet_fused_shift_partition_3d_backward",
+            "crumpet_fused_unshift_unpartition_3d_backward",
+        ):
+            getattr(lib, name).argtypes = copy_args
+            getattr(lib, name).restype = i32
+        lib.crumpet_compute_attn_mask_3d.argtypes = [vp, i32] + [i64] * 9 + [vp]
+        lib.crumpet_compute_attn_mask_3d.restype = i32
+        lib.crumpet_fused_swin_attention.argtypes = [
+            vp, vp, vp, vp, vp, vp, i64, vp, i32, i64, i64, i64, i64, ctypes.c_float, vp,
+        ]
+        lib.crumpet_fused_swin_attention.restype = i32
+        lib.crumpet_last_error.argtypes = []
+        lib.crumpet_last_error.restype = ctypes.c_char_p
+        lib.crumpet_abi_version.argtypes = []
+        lib.crumpet_abi_version.restype = i32
+        lib.crumpet_device_status.argtypes = [i32]
+        lib.crumpet_device_status.restype = i32
+        _capi = lib
+    return _capi
+
+
+def last_error() -> str:
+    return capi().crumpet_last_error().decode()

@@ -1,0 +1,636 @@
+// crumpet_b200: fused 3D Swin window attention for sm_100a (B200).
+//
+// Computes, per window b and head h (head_dim 16, N <= 384 tokens),
+//   out[b,h] = softmax(q k^T * scale + bias[h] + mask[b % nmask]) v
+// with fp32 scores and softmax -- the function of the reference Triton kernel
+// torch-ext/crumpet/fused_attention.py:48-146 (eager form: MONAI WindowAttention,
+// as described in torch-ext/crumpet/monai_patch.py:117-198).
+//
+// Design (one persistent CTA per SM, 12 warps):
+//   * A tile is 128 query rows of one (window, head).  Two independent tile
+//     pipelines ("work groups", WG) run per CTA; each has a TMA warp, an MMA
+//     warp and 4 softmax warps (one thread per query row = one TMEM lane).
+//   * TMA loads Q (128 rows) and all K, V rows of the (window, head) into
+//     shared memory with 32-byte swizzle; rows past N are zero-filled by TMA.
+//   * The key axis is processed in chunks of 64.  The MMA warp issues
+//     S_c = Q K_c^T (tcgen05.mma, M=128, K=16, fp32 accumulators in TMEM); the
+//     softmax warps pull S_c into registers, add the relative-position bias
+//     (shared-memory tile, reused for every window of the CTA) and the mask,
+//     take the chunk maximum m_c, write P_c = exp(x - m_c) back to TMEM as
+//     fp16/bf16, and the MMA warp accumulates O_c = P_c V_c with P read from
+//     TMEM.  Every chunk keeps its own O_c, m_c and l_c = sum(P_c), so no
+//     rescaling happens inside the loop; the epilogue combines them exactly:
+//       out = sum_c e^(m_c - m) O_c / sum_c e^(m_c - m) l_c,  m = max_c m_c.
+//   * Work: CTAs are split into groups, one per (head, query-tile) pair, and
+//     walk the windows in lock step, so the CTAs that need the same K/V rows
+//     (the other query tiles and heads of a window) read them close together
+//     in time and hit L2.
+// Every wait is bounded (2 s of %globaltimer); on expiry the kernel records an
+// error in g_device_error, drains its in-flight copies and MMAs, frees TMEM and
+// returns.
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace crumpet {
+
+__device__ int g_device_error;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kHD = 16;       // head dimension
+constexpr int kBM = 128;      // query rows per tile (UMMA M)
+constexpr int kCH = 64;       // key chunk
+constexpr int kNumWG = 2;     // independent tile pipelines per CTA
+constexpr int kStages = 2;    // Q/K/V stages per WG
+constexpr int kThreads = (kNumWG * 2 + kNumWG * 4) * 32;  // 384
+constexpr int kRowBytes = kHD * 2;
+constexpr int kBarsPerWG = 2 * kStages + 7;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemPerWG = 256;
+
+template <int NPAD>
+struct Cfg {
+  static_assert(NPAD % 32 == 0 && NPAD <= 384, "NPAD must be a multiple of 32, at most 384");
+  static constexpr int NKB = (NPAD + 127) / 128;      // 128-row TMA boxes for K and V
+  static constexpr int NCH = (NPAD + kCH - 1) / kCH;  // key chunks
+  static constexpr int LAST_W = NPAD - (NCH - 1) * kCH;
+  static constexpr int BSTRIDE = NPAD + 8;            // bias tile row stride (elements)
+  static constexpr int Q_BYTES = kBM * kRowBytes;
+  static constexpr int KV_BYTES = NKB * 128 * kRowBytes;
+  static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
+  static constexpr int BIAS_BYTES = kBM * BSTRIDE * 2;
+  static constexpr int TM_S = 0;
+  static constexpr int TM_P = kCH;
+  static constexpr int TM_O = kCH + kCH / 2;
+  static_assert(TM_O + NCH * kHD <= int(kTmemPerWG), "TMEM budget");
+  static constexpr int SMEM_BYTES =
+      1024 + kNumWG * kStages * STAGE_BYTES + BIAS_BYTES + kNumWG * kBarsPerWG * 8 + 64;
+};
+
+struct KParams {
+  const uint16_t* bias;      // [H, N, N]
+  const uint16_t* mask;      // [mask_windows, N, N] or null
+  const uint8_t* boundary;   // [B] or null
+  uint16_t* out;
+  long long out_sb, out_sh, out_sn;
+  int B, H, N, MT, P, mask_windows;
+  float scale;
+};
+
+// Work list of one CTA: `pair_count` (head, query-tile) pairs starting at
+// pair_begin with stride pair_step; inside each pair the windows
+// win_begin, win_begin + win_step, ...  Window k of that list goes to WG k % 2.
+struct Sched {
+  int pair_begin, pair_step, pair_count, win_begin, win_step;
+};
+
+__device__ __forceinline__ Sched make_sched(int P) {
+  const int G = gridDim.x, c = blockIdx.x;
+  Sched s{0, 1, 0, 0, 1};
+  if (P <= G) {
+    const int S = G / P;
+    if (c < P * S) {
+      s.pair_begin = c / S;
+      s.pair_count = 1;
+      s.win_begin = c % S;
+      s.win_step = S;
+    }
+  } else {
+    s.pair_begin = c;
+    s.pair_step = G;
+    s.pair_count = (P - c + G - 1) / G;
+  }
+  return s;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float to_f32(uint16_t h) {
+  if constexpr (BF16) {
+    return __uint_as_float(uint32_t(h) << 16);
+  } else {
+    return __half2float(__ushort_as_half(h));
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Waits on a barrier ignoring the abort flag (used only while draining).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+}
+
+template <int NPAD, bool BF16, bool HAS_MASK>
+__global__ void __launch_bounds__(kThreads, 1)
+window_attention_kernel(const __grid_constant__ CUtensorMap tq,
+                        const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const KParams p) {
+  using C = Cfg<NPAD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint16_t* bias_s = reinterpret_cast<uint16_t*>(smem + kNumWG * kStages * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kNumWG * kStages * C::STAGE_BYTES +
+                                               C::BIAS_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumWG * kBarsPerWG);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Sched sc = make_sched(p.P);
+  if (sc.pair_count == 0) return;  // uniform for the CTA
+
+  // Barrier block of WG w: [load_full x kStages][load_empty x kStages]
+  //                        [s_full][s_empty][p_full][p_empty][o_full][o_empty][drain]
+  auto bar = [&](int w, int i) { return bars + w * kBarsPerWG + i; };
+  constexpr int kLF = 0, kLE = kStages, kSF = 2 * kStages, kSE = kSF + 1, kPF = kSF + 2,
+                kPE = kSF + 3, kOF = kSF + 4, kOE = kSF + 5, kDR = kSF + 6;
+
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < kNumWG; ++w) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(bar(w, kLF + s), 1);
+        mbar_init(bar(w, kLE + s), 1);
+      }
+      mbar_init(bar(w, kSF), 1);
+      mbar_init(bar(w, kSE), 4);
+      mbar_init(bar(w, kPF), 4);
+      mbar_init(bar(w, kPE), 1);
+      mbar_init(bar(w, kOF), 1);
+      mbar_init(bar(w, kOE), 4);
+      mbar_init(bar(w, kDR), 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 2 * kNumWG) {
+    const int w = warp >> 1;
+    if ((warp & 1) == 0) {
+      // ------------------------------------------------------------ TMA warp
+      if (lane == 0) {
+        tma_prefetch_map(&tq);
+        tma_prefetch_map(&tk);
+        tma_prefetch_map(&tv);
+        uint32_t it = 0;
+        bool ok = true;
+        for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
+          const int pair = sc.pair_begin + pi * sc.pair_step;
+          const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
+          for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok;
+               b += kNumWG * sc.win_step) {
+            const int st = int(it % kStages);
+            const uint32_t ph = (it / kStages) & 1u;
+            if (!mbar_wait(bar(w, kLE + st), ph ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sb = smem + (w * kStages + st) * C::STAGE_BYTES;
+            uint64_t* full = bar(w, kLF + st);
+            mbar_arrive_expect_tx(full, C::STAGE_BYTES);
+            tma_load_4d(sb, &tq, full, 0, mt * kBM, h, b);
+#pragma unroll
+            for (int kb = 0; kb < C::NKB; ++kb) {
+              tma_load_4d(sb + C::Q_BYTES + kb * 128 * kRowBytes, &tk, full, 0, kb * 128, h, b);
+              tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + kb * 128 * kRowBytes, &tv, full, 0,
+                          kb * 128, h, b);
+            }
+            ++it;
+          }
+        }
+        // Drain: every stage's most recent load must have landed before exit.
+        for (uint32_t s = 0; s < kStages; ++s) {
+          if (it > s) {
+            const uint32_t last = ((it - 1 - s) / kStages) * kStages + s;  // last use of stage s
+            drain_wait(bar(w, kLF + int(s)), (last / kStages) & 1u);
+          }
+        }
+      }
+    } else {
+      // ------------------------------------------------------------ MMA warp
+      if (lane == 0) {
+        const uint32_t tS = tmem_base + w * kTmemPerWG + C::TM_S;
+        const uint32_t tP = tmem_base + w * kTmemPerWG + C::TM_P;
+        const uint32_t tO = tmem_base + w * kTmemPerWG + C::TM_O;
+        uint32_t it = 0, n_se = 0, n_pf = 0, n_oe = 0;
+        bool ok = true;
+        auto issue_pv = [&](int c, uint32_t v_addr) -> bool {
+          if (!mbar_wait(bar(w, kPF), n_pf & 1u, abort_flag)) return false;
+          ++n_pf;
+          tc_fence_after();
+          if (c == 0) {
+            if (!mbar_wait(bar(w, kOE), (n_oe & 1u) ^ 1u, abort_flag)) return false;
+            ++n_oe;
+            tc_fence_after();
+          }
+          const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
+          constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, BF16, true);
+          for (int k = 0; k < width / 16; ++k) {
+            const uint64_t vdesc =
+                smem_desc(v_addr + uint32_t(c * kCH + k * 16) * kRowBytes, 0, 256, kLayoutSW32);
+            umma_ts(tO + uint32_t(c * kHD), tP + uint32_t(k * 8), vdesc, idesc_pv,
+                    k > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(w, kPE));
+          return true;
+        };
+        for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
+          for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok;
+               b += kNumWG * sc.win_step) {
+            const int st = int(it % kStages);
+            const uint32_t ph = (it / kStages) & 1u;
+            if (!mbar_wait(bar(w, kLF + st), ph, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sb = smem_u32(smem + (w * kStages + st) * C::STAGE_BYTES);
+            const uint32_t q_addr = sb;
+            const uint32_t k_addr = sb + C::Q_BYTES;
+            const uint32_t v_addr = sb + C::Q_BYTES + C::KV_BYTES;
+            const uint64_t qdesc = smem_desc(q_addr, 16, 256, kLayoutSW32);
+            for (int c = 0; c < C::NCH && ok; ++c) {
+              if (!mbar_wait(bar(w, kSE), (n_se & 1u) ^ 1u, abort_flag)) {
+                ok = false;
+                break;
+              }
+              ++n_se;
+              tc_fence_after();
+              const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
+              const uint64_t kdesc =
+                  smem_desc(k_addr + uint32_t(c * kCH) * kRowBytes, 16, 256, kLayoutSW32);
+              umma_ss(tS, qdesc, kdesc, idesc_f16(kBM, width, BF16, false), 0u);
+              umma_commit(bar(w, kSF));
+              if (c > 0 && !issue_pv(c - 1, v_addr)) ok = false;
+            }
+            if (ok && !issue_pv(C::NCH - 1, v_addr)) ok = false;
+            if (!ok) break;
+            umma_commit(bar(w, kOF));
+            umma_commit(bar(w, kLE + st));
+            ++it;
+          }
+        }
+        // Drain: all MMAs issued by this thread complete before TMEM is freed.
+        umma_commit(bar(w, kDR));
+        drain_wait(bar(w, kDR), 0);
+      }
+    }
+  } else {
+    // -------------------------------------------------------- softmax warps
+    const int sw = warp - 2 * kNumWG;  // 0 .. 4*kNumWG-1
+    const int w = sw >> 2;
+    const int quarter = warp & 3;      // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const int tid_sm = threadIdx.x - 2 * kNumWG * 32;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + w * kTmemPerWG + C::TM_S;
+    const uint32_t tP = tmem_base + lane_off + w * kTmemPerWG + C::TM_P;
+    const uint32_t tO = tmem_base + lane_off + w * kTmemPerWG + C::TM_O;
+    const float kLog2e = 1.4426950408889634f;
+    const float kNegInf = __int_as_float(0xff800000);
+    uint32_t n_sf = 0, n_pe = 0, n_of = 0;
+    bool ok = true;
+
+    for (int pi = 0; pi < sc.pair_count; ++pi) {
+      const int pair = sc.pair_begin + pi * sc.pair_step;
+      const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
+      // Relative-position bias rows of this (head, query tile): one load per CTA
+      // and pair, shared by every window and both WGs.
+      named_bar_sync(1, kNumWG * 128);
+      for (int e = tid_sm; e < kBM * NPAD; e += kNumWG * 128) {
+        const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
+        const int grow = mt * kBM + r;
+        uint16_t val = 0;
+        if (grow < p.N && col < p.N) val = p.bias[(size_t(h) * p.N + grow) * p.N + col];
+        bias_s[r * C::BSTRIDE + col] = val;
+      }
+      named_bar_sync(1, kNumWG * 128);
+      if (!ok) continue;
+
+      const int qrow = mt * kBM + row;
+      const bool valid = qrow < p.N;
+      const uint16_t* brow = bias_s + row * C::BSTRIDE;
+
+      for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok; b += kNumWG * sc.win_step) {
+        bool use_mask = false;
+        const uint16_t* mrow = nullptr;
+        if constexpr (HAS_MASK) {
+          use_mask = (p.boundary == nullptr) || (p.boundary[b] != 0);
+          const int mw = b % p.mask_windows;
+          mrow = p.mask + (size_t(mw) * p.N + (valid ? qrow : 0)) * p.N;
+        }
+        float mc[C::NCH], lc[C::NCH];
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) {
+          const int W = (c < C::NCH - 1) ? kCH : C::LAST_W;
+          if (!mbar_wait(bar(w, kSF), n_sf & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ++n_sf;
+          tc_fence_after();
+          uint32_t s[kCH];
+          tmem_ld32(tS, s);
+          if (W > 32) tmem_ld32(tS + 32, s + 32);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(w, kSE));
+
+          float x[kCH];
+#pragma unroll
+          for (int j = 0; j < kCH; j += 8) {
+            if (j < W) {
+              const uint4 bv = *reinterpret_cast<const uint4*>(brow + c * kCH + j);
+              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                x[j + 2 * t] = fmaf(__uint_as_float(s[j + 2 * t]), p.scale,
+                                    to_f32<BF16>(uint16_t(bw[t] & 0xFFFFu)));
+                x[j + 2 * t + 1] = fmaf(__uint_as_float(s[j + 2 * t + 1]), p.scale,
+                                        to_f32<BF16>(uint16_t(bw[t] >> 16)));
+              }
+            }
+          }
+          if constexpr (HAS_MASK) {
+            if (use_mask && valid) {
+#pragma unroll
+              for (int j = 0; j < kCH; ++j) {
+                if (j < W) {
+                  const int col = c * kCH + j;
+                  if (c < C::NCH - 1 || col < p.N) x[j] += to_f32<BF16>(mrow[col]);
+                }
+              }
+            }
+          }
+          if (c == C::NCH - 1) {
+#pragma unroll
+            for (int j = 0; j < kCH; ++j) {
+              if (j < W && c * kCH + j >= p.N) x[j] = kNegInf;
+            }
+          }
+          float m = kNegInf;
+#pragma unroll
+          for (int j = 0; j < kCH; ++j) {
+            if (j < W) m = fmaxf(m, x[j]);
+          }
+          const float mref = (m == kNegInf) ? 0.f : m;
+          const float moff = mref * kLog2e;
+          float l = 0.f;
+          uint32_t pk[kCH / 2];
+#pragma unroll
+          for (int j = 0; j < kCH; j += 2) {
+            if (j < W) {
+              const float e0 = fast_ex2(fmaf(x[j], kLog2e, -moff));
+              const float e1 = fast_ex2(fmaf(x[j + 1], kLog2e, -moff));
+              l += e0 + e1;
+              pk[j / 2] = pack2<BF16>(e0, e1);
+            }
+          }
+          mc[c] = m;
+          lc[c] = l;
+          // P buffer must be free: PV of the previous chunk has completed.
+          if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ++n_pe;
+          tc_fence_after();
+          tmem_st16(tP, pk);
+          if (W > 32) tmem_st16(tP + 16, pk + 16);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(w, kPF));
+        }
+        if (!ok) break;
+
+        // ---- epilogue: combine the per-chunk partial outputs
+        if (!mbar_wait(bar(w, kOF), n_of & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ++n_of;
+        tc_fence_after();
+        uint32_t o[C::NCH][kHD];
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) tmem_ld16(tO + uint32_t(c * kHD), o[c]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(w, kOE));
+
+        float mmax = kNegInf;
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) mmax = fmaxf(mmax, mc[c]);
+        float acc[kHD];
+#pragma unroll
+        for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
+        float L = 0.f;
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) {
+          const float wc = (mc[c] == kNegInf) ? 0.f : fast_ex2((mc[c] - mmax) * kLog2e);
+          L = fmaf(wc, lc[c], L);
+#pragma unroll
+          for (int d = 0; d < kHD; ++d) acc[d] = fmaf(wc, __uint_as_float(o[c][d]), acc[d]);
+        }
+        if (valid) {
+          const float inv = 1.f / L;
+          uint32_t packed[kHD / 2];
+#pragma unroll
+          for (int d = 0; d < kHD; d += 2) packed[d / 2] = pack2<BF16>(acc[d] * inv, acc[d + 1] * inv);
+          uint16_t* dst = p.out + b * p.out_sb + h * p.out_sh + qrow * p.out_sn;
+          stg(reinterpret_cast<uint4*>(dst),
+              make_uint4(packed[0], packed[1], packed[2], packed[3]));
+          stg(reinterpret_cast<uint4*>(dst + 8),
+              make_uint4(packed[4], packed[5], packed[6], packed[7]));
+        }
+      }
+    }
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_device_error, 1);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 4D map {head_dim, N, H, B} over q/k/v with a 128-row box and 32-byte swizzle.
+int make_qkv_map(CUtensorMap* map, const void* base, const AttnArgs& a) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[4] = {cuuint64_t(a.head_dim), cuuint64_t(a.N), cuuint64_t(a.H),
+                              cuuint64_t(a.B)};
+  const cuuint64_t strides[3] = {cuuint64_t(a.qkv_stride_n) * 2, cuuint64_t(a.qkv_stride_h) * 2,
+                                 cuuint64_t(a.qkv_stride_b) * 2};
+  const cuuint32_t box[4] = {cuuint32_t(kHD), 128u, 1u, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      a.dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(kErrInvalid, "cuTensorMapEncodeTiled rejected q/k/v");
+  return kOk;
+}
+
+int num_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+template <int NPAD, bool BF16, bool HAS_MASK>
+int launch_impl(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+                const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
+  using C = Cfg<NPAD>;
+  auto kern = window_attention_kernel<NPAD, BF16, HAS_MASK>;
+  static bool configured[64] = {false};  // per device; attribute is per function
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) return set_cuda_error(e, "attention smem attribute");
+    configured[dev] = true;
+  }
+  kern<<<num_sms(), kThreads, C::SMEM_BYTES, stream>>>(tq, tk, tv, kp);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "attention launch");
+  return kOk;
+}
+
+template <int NPAD>
+int dispatch_npad(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+                  const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
+  const bool bf = a.dtype == kBF16;
+  const bool m = a.mask != nullptr;
+  if (bf) {
+    return m ? launch_impl<NPAD, true, true>(a, tq, tk, tv, kp, stream)
+             : launch_impl<NPAD, true, false>(a, tq, tk, tv, kp, stream);
+  }
+  return m ? launch_impl<NPAD, false, true>(a, tq, tk, tv, kp, stream)
+           : launch_impl<NPAD, false, false>(a, tq, tk, tv, kp, stream);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
+  if (a.dtype != kF16 && a.dtype != kBF16)
+    return set_error(kErrUnsupported, "fused_swin_attention supports float16 and bfloat16");
+  if (a.head_dim != kHD) return set_error(kErrUnsupported, "fused_swin_attention requires head_dim 16");
+  if (a.N < 1 || a.N > 384) return set_error(kErrUnsupported, "fused_swin_attention supports 1 <= N <= 384");
+  if (a.B < 0 || a.H < 1) return set_error(kErrInvalid, "B must be >= 0 and H >= 1");
+  if (a.B == 0) return kOk;
+  if (a.B > 0x7fffffff || a.H > 0xffff) return set_error(kErrInvalid, "B or H too large");
+  if (!a.q || !a.k || !a.v || !a.out || !a.bias)
+    return set_error(kErrInvalid, "null tensor pointer");
+  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(a.out))
+    return set_error(kErrInvalid, "q, k, v and out must be 16-byte aligned");
+  if ((a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 != 0 ||
+      (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 != 0)
+    return set_error(kErrInvalid, "q/k/v/out strides must be multiples of 8 elements");
+  if (a.mask && a.mask_windows < 1) return set_error(kErrInvalid, "mask_windows must be >= 1");
+
+  CUtensorMap tq, tk, tv;
+  if (int e = make_qkv_map(&tq, a.q, a)) return e;
+  if (int e = make_qkv_map(&tk, a.k, a)) return e;
+  if (int e = make_qkv_map(&tv, a.v, a)) return e;
+
+  KParams kp{};
+  kp.bias = static_cast<const uint16_t*>(a.bias);
+  kp.mask = static_cast<const uint16_t*>(a.mask);
+  kp.boundary = a.boundary;
+  kp.out = static_cast<uint16_t*>(a.out);
+  kp.out_sb = a.out_stride_b;
+  kp.out_sh = a.out_stride_h;
+  kp.out_sn = a.out_stride_n;
+  kp.B = int(a.B);
+  kp.H = int(a.H);
+  kp.N = int(a.N);
+  kp.MT = int((a.N + kBM - 1) / kBM);
+  kp.P = kp.H * kp.MT;
+  kp.mask_windows = a.mask ? int(a.mask_windows) : 1;
+  kp.scale = a.scale;
+
+  const int n32 = int((a.N + 31) / 32) * 32;
+  if (n32 <= 64) return dispatch_npad<64>(a, tq, tk, tv, kp, stream);
+  if (n32 <= 128) return dispatch_npad<128>(a, tq, tk, tv, kp, stream);
+  if (n32 <= 224) return dispatch_npad<224>(a, tq, tk, tv, kp, stream);
+  if (n32 <= 352) return dispatch_npad<352>(a, tq, tk, tv, kp, stream);
+  return dispatch_npad<384>(a, tq, tk, tv, kp, stream);
+}
+
+int read_device_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace crumpet

@@ -1,0 +1,164 @@
+// crumpet_b200: the C ABI (declared in include/crumpet_b200.h).
+//
+// Every entry point validates its arguments the way the reference's Python
+// wrappers and C++ ops do (torch-ext/crumpet/__init__.py:89-123,
+// cuda/attn_mask_3d.cu:143), launches on the caller's stream, never allocates
+// and never synchronises.  Failures return a non-zero status and leave a
+// message for crumpet_last_error().
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/crumpet_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace crumpet {
+
+namespace {
+thread_local char g_last_error[512] = {0};
+}
+
+int set_error(int code, const char* msg) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
+  return code;
+}
+
+int set_cuda_error(cudaError_t err, const char* where) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", where, cudaGetErrorString(err));
+  return kErrCuda;
+}
+
+namespace {
+
+int check_dtype(int dtype) {
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16)
+    return set_error(kErrInvalid, "CRUMPET supports float32, float16 and bfloat16");
+  return kOk;
+}
+
+// Mirrors _validate_shape (torch-ext/crumpet/__init__.py:98-117).
+int check_window_shape(int64_t D, int64_t H, int64_t W, int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                       int64_t ss_d, int64_t ss_h, int64_t ss_w) {
+  if (D <= 0 || H <= 0 || W <= 0) return set_error(kErrInvalid, "D, H and W must be positive");
+  if (ws_d <= 0 || ws_h <= 0 || ws_w <= 0)
+    return set_error(kErrInvalid, "window_size values must be positive");
+  if (D % ws_d || H % ws_h || W % ws_w)
+    return set_error(kErrInvalid,
+                     "standalone CRUMPET kernels require D, H and W to be divisible by window_size");
+  const int64_t ss[3] = {ss_d, ss_h, ss_w};
+  const int64_t ws[3] = {ws_d, ws_h, ws_w};
+  for (int a = 0; a < 3; ++a) {
+    if (ss[a] < 0 || ss[a] >= ws[a]) {
+      char buf[96];
+      std::snprintf(buf, sizeof(buf), "shift_size[%d] must satisfy 0 <= shift < window_size[%d]", a,
+                    a);
+      return set_error(kErrInvalid, buf);
+    }
+  }
+  // 32-bit index arithmetic inside one window and one volume slice.
+  if (D * H * W >= (int64_t(1) << 31)) return set_error(kErrInvalid, "D*H*W must be below 2^31");
+  return kOk;
+}
+
+int window_copy(bool forward, void* out, const void* in, int dtype, int64_t B, int64_t D, int64_t H,
+                int64_t W, int64_t C, int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                int64_t ss_h, int64_t ss_w, void* stream) {
+  if (int e = check_dtype(dtype)) return e;
+  if (int e = check_window_shape(D, H, W, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w)) return e;
+  if (B < 0 || C < 0) return set_error(kErrInvalid, "B and C must be non-negative");
+  if (B == 0 || C == 0) return kOk;  // empty output: nothing to do
+  if (out == nullptr || in == nullptr) return set_error(kErrInvalid, "null tensor pointer");
+  const ShapeArgs s{B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w};
+  return launch_window_copy(forward, out, in, s, dtype, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace crumpet
+
+using namespace crumpet;
+
+extern "C" {
+
+const char* crumpet_last_error(void) { return g_last_error; }
+
+int crumpet_abi_version(void) { return CRUMPET_ABI_VERSION; }
+
+int crumpet_fused_shift_partition_3d(void* output, const void* x, int dtype, int64_t B, int64_t D,
+                                     int64_t H, int64_t W, int64_t C, int64_t ws_d, int64_t ws_h,
+                                     int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                     void* stream) {
+  return window_copy(true, output, x, dtype, B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w,
+                     stream);
+}
+
+int crumpet_fused_unshift_unpartition_3d(void* output, const void* windows, int dtype, int64_t B,
+                                         int64_t D, int64_t H, int64_t W, int64_t C, int64_t ws_d,
+                                         int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                         int64_t ss_w, void* stream) {
+  return window_copy(false, output, windows, dtype, B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h,
+                     ss_w, stream);
+}
+
+int crumpet_fused_shift_partition_3d_backward(void* grad_x, const void* grad_windows, int dtype,
+                                              int64_t B, int64_t D, int64_t H, int64_t W,
+                                              int64_t C, int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                                              int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                              void* stream) {
+  return window_copy(false, grad_x, grad_windows, dtype, B, D, H, W, C, ws_d, ws_h, ws_w, ss_d,
+                     ss_h, ss_w, stream);
+}
+
+int crumpet_fused_unshift_unpartition_3d_backward(void* grad_windows, const void* grad_x,
+                                                  int dtype, int64_t B, int64_t D, int64_t H,
+                                                  int64_t W, int64_t C, int64_t ws_d, int64_t ws_h,
+                                                  int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                                  int64_t ss_w, void* stream) {
+  return window_copy(true, grad_windows, grad_x, dtype, B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h,
+                     ss_w, stream);
+}
+
+int crumpet_compute_attn_mask_3d(void* output, int dtype, int64_t D, int64_t H, int64_t W,
+                                 int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                 int64_t ss_h, int64_t ss_w, void* stream) {
+  if (int e = check_dtype(dtype)) return e;
+  if (int e = check_window_shape(D, H, W, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w)) return e;
+  if (output == nullptr) return set_error(kErrInvalid, "null tensor pointer");
+  return launch_attn_mask(output, D, H, W, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w, dtype,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int crumpet_fused_swin_attention(void* out, const void* q, const void* k, const void* v,
+                                 const void* rel_bias, const void* mask, int64_t mask_windows,
+                                 const uint8_t* boundary, int dtype, int64_t B, int64_t H,
+                                 int64_t N, int64_t head_dim, float scale, void* stream) {
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.qkv_stride_n = head_dim;
+  a.qkv_stride_h = N * head_dim;
+  a.qkv_stride_b = H * N * head_dim;
+  a.out = out;
+  a.out_stride_n = head_dim;
+  a.out_stride_h = N * head_dim;
+  a.out_stride_b = H * N * head_dim;
+  a.bias = rel_bias;
+  a.mask = mask;
+  a.mask_windows = mask_windows;
+  a.boundary = boundary;
+  a.B = B;
+  a.H = H;
+  a.N = N;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.dtype = dtype;
+  return launch_window_attention(a, static_cast<cudaStream_t>(stream));
+}
+
+int crumpet_device_status(int clear) {
+  const int v = read_device_error(clear != 0);
+  if (v < 0) return set_error(kErrCuda, "could not read the device error word");
+  return v;
+}
+
+}  // extern "C"

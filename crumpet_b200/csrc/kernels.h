@@ -1,0 +1,60 @@
+// crumpet_b200: internal launcher interface between the C ABI (capi.cu) and
+// the kernel translation units.  Nothing here is exported.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace crumpet {
+
+enum Status : int {
+  kOk = 0,
+  kErrInvalid = 1,
+  kErrCuda = 2,
+  kErrUnsupported = 3,
+  kErrDevice = 4,
+};
+
+// Records a message for crumpet_last_error() and returns `code`.
+int set_error(int code, const char* msg);
+int set_cuda_error(cudaError_t err, const char* where);
+
+struct ShapeArgs {
+  int64_t B, D, H, W, C;
+  int64_t ws_d, ws_h, ws_w;
+  int64_t ss_d, ss_h, ss_w;
+};
+
+int launch_window_copy(bool forward, void* out, const void* in, const ShapeArgs& s, int dtype,
+                       cudaStream_t stream);
+
+int launch_attn_mask(void* out, int64_t D, int64_t H, int64_t W, int64_t ws_d, int64_t ws_h,
+                     int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype,
+                     cudaStream_t stream);
+
+// Window attention: out = softmax(q k^T * scale + bias[h] + mask[b mod nmask]) v.
+struct AttnArgs {
+  // q/k/v addressing: element (b, h, n, d) lives at
+  //   base + b*stride_b + h*stride_h + n*stride_n + d     (elements)
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t qkv_stride_b, qkv_stride_h, qkv_stride_n;
+  void* out;
+  int64_t out_stride_b, out_stride_h, out_stride_n;
+  const void* bias;        // [H, N, N] contiguous, same dtype as q
+  const void* mask;        // [mask_windows, N, N] contiguous or nullptr
+  int64_t mask_windows;    // window b uses mask[b % mask_windows]
+  const uint8_t* boundary; // [B] or nullptr (nullptr + mask => every window masked)
+  int64_t B, H, N, head_dim;
+  float scale;
+  int dtype;               // kF16 or kBF16
+};
+
+int launch_window_attention(const AttnArgs& a, cudaStream_t stream);
+
+// Device-side error word written by kernels whose bounded waits expired.
+// Reads it (synchronously); clears it when `clear`.  Returns -1 on failure.
+int read_device_error(bool clear);
+
+}  // namespace crumpet

@@ -1,0 +1,202 @@
+// crumpet_b200: torch dispatcher registration of the crumpet_ops namespace.
+//
+// Same op names, schemas and tags as the reference registration
+// (torch-ext/torch_binding.cpp:9-39), CUDA implementations only, plus
+// fused_swin_attention, which the reference exposes only as a Python/Triton
+// function (torch-ext/crumpet/fused_attention.py:149-226).  Every impl checks
+// the tensors, takes the current stream and calls the C ABI in
+// libcrumpet_b200.so; ops never allocate (outputs are preallocated `Tensor!`).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "crumpet_b200.h"
+
+namespace {
+
+const std::vector<at::Tag> kTags = {at::Tag::pt2_compliant_tag,
+                                    at::Tag::needs_fixed_stride_order};
+
+int dtype_code(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat:
+      return CRUMPET_DTYPE_F32;
+    case at::kHalf:
+      return CRUMPET_DTYPE_F16;
+    case at::kBFloat16:
+      return CRUMPET_DTYPE_BF16;
+    default:
+      TORCH_CHECK_TYPE(false, "CRUMPET supports torch.float32, torch.float16 and torch.bfloat16");
+  }
+  return -1;
+}
+
+void check_rc(int rc) { TORCH_CHECK(rc == CRUMPET_OK, "crumpet_b200: ", crumpet_last_error()); }
+
+void* cur_stream(const at::Tensor& t) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void check_cuda_contig(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+int64_t num_windows(int64_t D, int64_t H, int64_t W, int64_t wd, int64_t wh, int64_t ww) {
+  TORCH_CHECK(wd > 0 && wh > 0 && ww > 0, "window_size values must be positive");
+  return (D / wd) * (H / wh) * (W / ww);
+}
+
+void compute_attn_mask_3d(at::Tensor& output, int64_t D, int64_t H, int64_t W, int64_t ws_d,
+                          int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w) {
+  check_cuda_contig(output, "output");
+  const c10::cuda::CUDAGuard guard(output.device());
+  if (output.numel() == 0) return;
+  const int64_t vol = ws_d * ws_h * ws_w;
+  const int64_t nw = num_windows(D, H, W, ws_d, ws_h, ws_w);
+  TORCH_CHECK(output.dim() == 3 && output.size(0) == nw && output.size(1) == vol &&
+                  output.size(2) == vol,
+              "output must have shape [num_windows, volume, volume]");
+  check_rc(crumpet_compute_attn_mask_3d(output.data_ptr(), dtype_code(output), D, H, W, ws_d, ws_h,
+                                        ws_w, ss_d, ss_h, ss_w, cur_stream(output)));
+}
+
+void fused_shift_partition_3d(at::Tensor& output, const at::Tensor& x, int64_t ws_d, int64_t ws_h,
+                              int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(output, "output");
+  TORCH_CHECK(x.dim() == 5, "x must have shape [B, D, H, W, C]");
+  TORCH_CHECK(output.scalar_type() == x.scalar_type(), "output and x dtypes differ");
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (output.numel() == 0) return;
+  const int64_t B = x.size(0), D = x.size(1), H = x.size(2), W = x.size(3), C = x.size(4);
+  const int64_t nw = num_windows(D, H, W, ws_d, ws_h, ws_w);
+  TORCH_CHECK(output.dim() == 3 && output.size(0) == B * nw &&
+                  output.size(1) == ws_d * ws_h * ws_w && output.size(2) == C,
+              "output must have shape [B * num_windows, volume, C]");
+  check_rc(crumpet_fused_shift_partition_3d(output.data_ptr(), x.data_ptr(), dtype_code(x), B, D,
+                                            H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w,
+                                            cur_stream(x)));
+}
+
+void fused_unshift_unpartition_3d(at::Tensor& output, const at::Tensor& windows, int64_t B,
+                                  int64_t D, int64_t H, int64_t W, int64_t C, int64_t ws_d,
+                                  int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                  int64_t ss_w) {
+  check_cuda_contig(windows, "windows");
+  check_cuda_contig(output, "output");
+  TORCH_CHECK(output.scalar_type() == windows.scalar_type(), "output and windows dtypes differ");
+  const c10::cuda::CUDAGuard guard(windows.device());
+  if (output.numel() == 0) return;
+  const int64_t nw = num_windows(D, H, W, ws_d, ws_h, ws_w);
+  TORCH_CHECK(windows.dim() == 3 && windows.size(0) == B * nw &&
+                  windows.size(1) == ws_d * ws_h * ws_w && windows.size(2) == C,
+              "windows must have shape [B * num_windows, volume, C]");
+  TORCH_CHECK(output.numel() == B * D * H * W * C, "output must have B*D*H*W*C elements");
+  check_rc(crumpet_fused_unshift_unpartition_3d(output.data_ptr(), windows.data_ptr(),
+                                                dtype_code(windows), B, D, H, W, C, ws_d, ws_h,
+                                                ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
+}
+
+// Gradient of the partition is the unpartition (reference:
+// cuda/unshift_unpartition_3d.cu:320-348).
+void fused_shift_partition_3d_backward(at::Tensor& grad_x, const at::Tensor& grad_windows,
+                                       int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                                       int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                       int64_t ss_h, int64_t ss_w) {
+  fused_unshift_unpartition_3d(grad_x, grad_windows, B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h,
+                               ss_w);
+}
+
+// Gradient of the unpartition is the partition (reference:
+// cuda/shift_partition_3d.cu:349-367).
+void fused_unshift_unpartition_3d_backward(at::Tensor& grad_windows, const at::Tensor& grad_x,
+                                           int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                           int64_t ss_h, int64_t ss_w) {
+  fused_shift_partition_3d(grad_windows, grad_x, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w);
+}
+
+void fused_swin_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor& k,
+                          const at::Tensor& v, const at::Tensor& rel_bias,
+                          const c10::optional<at::Tensor>& mask,
+                          const c10::optional<at::Tensor>& boundary, double scale) {
+  check_cuda_contig(out, "out");
+  check_cuda_contig(q, "q");
+  check_cuda_contig(k, "k");
+  check_cuda_contig(v, "v");
+  check_cuda_contig(rel_bias, "relative_position_bias");
+  TORCH_CHECK(q.dim() == 4 && q.sizes() == k.sizes() && q.sizes() == v.sizes() &&
+                  q.sizes() == out.sizes(),
+              "q, k, v and out must share the shape [B, H, N, head_dim]");
+  const int64_t B = q.size(0), H = q.size(1), N = q.size(2), Dh = q.size(3);
+  TORCH_CHECK(rel_bias.dim() == 3 && rel_bias.size(0) == H && rel_bias.size(1) == N &&
+                  rel_bias.size(2) == N,
+              "relative_position_bias must have shape [H, N, N]");
+  const auto st = q.scalar_type();
+  TORCH_CHECK(k.scalar_type() == st && v.scalar_type() == st && out.scalar_type() == st &&
+                  rel_bias.scalar_type() == st,
+              "q, k, v, out and relative_position_bias must share one dtype");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const void* mask_ptr = nullptr;
+  int64_t mask_windows = 0;
+  if (mask.has_value() && mask->defined()) {
+    check_cuda_contig(*mask, "mask");
+    TORCH_CHECK(mask->dim() == 3 && mask->size(1) == N && mask->size(2) == N,
+                "mask must have shape [num_windows, N, N]");
+    TORCH_CHECK(mask->scalar_type() == st, "mask must have the dtype of q");
+    mask_windows = mask->size(0);
+    TORCH_CHECK(mask_windows >= 1 && B % mask_windows == 0,
+                "mask windows must divide the batch of windows");
+    mask_ptr = mask->data_ptr();
+  }
+  const uint8_t* bnd = nullptr;
+  if (boundary.has_value() && boundary->defined()) {
+    check_cuda_contig(*boundary, "boundary");
+    TORCH_CHECK(boundary->scalar_type() == at::kByte && boundary->numel() == B,
+                "boundary must be a uint8 tensor of B elements");
+    bnd = boundary->data_ptr<uint8_t>();
+  }
+  check_rc(crumpet_fused_swin_attention(out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                        rel_bias.data_ptr(), mask_ptr, mask_windows, bnd,
+                                        dtype_code(q), B, H, N, Dh, static_cast<float>(scale),
+                                        cur_stream(q)));
+}
+
+}  // namespace
+
+TORCH_LIBRARY(crumpet_ops, ops) {
+  ops.def(
+      "compute_attn_mask_3d(Tensor! output, int D, int H, int W, int ws_d, int ws_h, int ws_w, "
+      "int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "fused_shift_partition_3d(Tensor! output, Tensor x, int ws_d, int ws_h, int ws_w, int ss_d, "
+      "int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "fused_shift_partition_3d_backward(Tensor! grad_x, Tensor grad_windows, int B, int D, int H, "
+      "int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "fused_unshift_unpartition_3d(Tensor! output, Tensor windows, int B, int D, int H, int W, "
+      "int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "fused_unshift_unpartition_3d_backward(Tensor! grad_windows, Tensor grad_x, int ws_d, "
+      "int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "fused_swin_attention(Tensor! out, Tensor q, Tensor k, Tensor v, Tensor rel_bias, "
+      "Tensor? mask, Tensor? boundary, float scale) -> ()",
+      kTags);
+}
+
+TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
+  ops.impl("compute_attn_mask_3d", &compute_attn_mask_3d);
+  ops.impl("fused_shift_partition_3d", &fused_shift_partition_3d);
+  ops.impl("fused_shift_partition_3d_backward", &fused_shift_partition_3d_backward);
+  ops.impl("fused_unshift_unpartition_3d", &fused_unshift_unpartition_3d);
+  ops.impl("fused_unshift_unpartition_3d_backward", &fused_unshift_unpartition_3d_backward);
+  ops.impl("fused_swin_attention", &fused_swin_attention);
+}

@@ -1,0 +1,72 @@
+"""Fused 3D Swin window attention (hand-written sm_100a kernel).
+
+Python entry point with the signature of the reference Triton launcher
+(torch-ext/crumpet/fused_attention.py:149-226):
+
+    fused_swin_attention(q, k, v, relative_position_bias, mask, boundary=None,
+                         scale=None, block_m=64, block_n=32) -> out
+
+``q``, ``k``, ``v``: ``[B, H, N, head_dim]`` (B = batch * windows);
+``relative_position_bias``: ``[H, N, N]``; ``mask``: ``[num_windows, N, N]``
+(window ``b`` uses ``mask[b % num_windows]``, which covers the reference's
+``mask.shape[0] in (1, B)`` cases and MONAI's sliding-window tiling without a
+``repeat``) or ``None``; ``boundary``: per-window flag, mask rows are read only
+where it is non-zero.  ``block_m`` / ``block_n`` are accepted for API
+compatibility and ignored: the tile shape is fixed by the tcgen05 design
+(128 query rows x 64-key chunks).  fp16 and bf16, head_dim 16, N <= 384.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _ops as _native
+
+
+def fused_swin_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    relative_position_bias: torch.Tensor,
+    mask: torch.Tensor | None,
+    boundary: torch.Tensor | None = None,
+    scale: float | None = None,
+    block_m: int = 64,
+    block_n: int = 32,
+) -> torch.Tensor:
+    del block_m, block_n  # tile shape is fixed by the kernel design
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("fused_swin_attention runs on CUDA tensors only")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("Q/K/V shape mismatch")
+    if q.ndim != 4:
+        raise ValueError("q, k and v must have shape [B, H, N, head_dim]")
+    B, H, N, D = (int(s) for s in q.shape)
+    if tuple(relative_position_bias.shape) != (H, N, N):
+        raise ValueError(f"relative_position_bias must have shape {(H, N, N)}")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("fused_swin_attention supports torch.float16 and torch.bfloat16")
+    if D != 16:
+        raise ValueError("fused_swin_attention requires head_dim 16")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    bias = relative_position_bias.to(q.dtype).contiguous()
+    mask_t = None
+    bnd = None
+    if mask is not None:
+        if mask.ndim != 3 or tuple(mask.shape[1:]) != (N, N):
+            raise ValueError(f"mask must have shape [num_windows, {N}, {N}]")
+        if B % int(mask.shape[0]) != 0:
+            raise ValueError(f"mask shape {int(mask.shape[0])} incompatible with B={B}")
+        mask_t = mask.to(q.dtype).contiguous()
+        if boundary is not None:
+            bnd = boundary if boundary.dtype == torch.uint8 else boundary.to(torch.uint8)
+            bnd = bnd.contiguous()
+    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    _native.require().fused_swin_attention(
+        out, q.contiguous(), k.contiguous(), v.contiguous(), bias, mask_t, bnd, float(scale)
+    )
+    return out
+
+
+__all__ = ["fused_swin_attention"]

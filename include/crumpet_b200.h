@@ -1,0 +1,143 @@
+/*
+ * crumpet_b200 — C ABI of the B200 (sm_100a) shifted-window kernels.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*, i.e. cudaStream_t;
+ * NULL = legacy default stream).  No entry point allocates device memory or
+ * synchronises the device; all of them launch asynchronously on `stream` and
+ * return CRUMPET_OK or an error status, with a message in crumpet_last_error().
+ * Tensors are dense and C-contiguous unless a stride argument says otherwise.
+ *
+ * Each entry point names the reference interface it replaces
+ * (chrisvoncsefalvay/crumpet, path:line).  The torch dispatcher ops in
+ * crumpet_b200/csrc/torch_binding.cpp are thin adapters over these functions.
+ */
+#ifndef CRUMPET_B200_H_
+#define CRUMPET_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CRUMPET_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define CRUMPET_API __attribute__((visibility("default")))
+#else
+#define CRUMPET_API
+#endif
+
+/* Element types. */
+#define CRUMPET_DTYPE_F32 0
+#define CRUMPET_DTYPE_F16 1
+#define CRUMPET_DTYPE_BF16 2
+
+/* Status codes. */
+#define CRUMPET_OK 0
+#define CRUMPET_ERR_INVALID 1     /* bad shape, size, dtype or pointer */
+#define CRUMPET_ERR_CUDA 2        /* a CUDA runtime call or launch failed */
+#define CRUMPET_ERR_UNSUPPORTED 3 /* valid request this build does not handle */
+#define CRUMPET_ERR_DEVICE 4      /* a kernel reported a device-side error */
+
+/* Message of the last failing call on this host thread ("" if none). */
+CRUMPET_API const char* crumpet_last_error(void);
+
+/* Returns CRUMPET_ABI_VERSION. */
+CRUMPET_API int crumpet_abi_version(void);
+
+/*
+ * Cyclic roll by -ss over (D,H,W) followed by the 3D window partition.
+ *   x      [B, D, H, W, C]                 (dtype)
+ *   output [B * nW, ws_d*ws_h*ws_w, C]     nW = (D/ws_d)(H/ws_h)(W/ws_w)
+ * Requires D, H, W divisible by the window and 0 <= ss < ws per axis.
+ * Replaces op crumpet_ops::fused_shift_partition_3d
+ *   (torch-ext/torch_binding.cpp:20-22, torch-ext/torch_binding.h:19-27,
+ *    cuda/shift_partition_3d.cu:318-347).  Shapes are explicit here because
+ *    the C ABI carries no tensor metadata.
+ */
+CRUMPET_API int crumpet_fused_shift_partition_3d(void* output, const void* x, int dtype, int64_t B, int64_t D,
+                                     int64_t H, int64_t W, int64_t C, int64_t ws_d, int64_t ws_h,
+                                     int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                     void* stream);
+
+/*
+ * Window reverse followed by a cyclic roll by +ss: the exact inverse of
+ * crumpet_fused_shift_partition_3d.
+ *   windows [B * nW, ws_d*ws_h*ws_w, C]  ->  output [B, D, H, W, C]
+ * Replaces op crumpet_ops::fused_unshift_unpartition_3d
+ *   (torch-ext/torch_binding.cpp:26-28, torch-ext/torch_binding.h:43-56,
+ *    cuda/unshift_unpartition_3d.cu:284-318).
+ */
+CRUMPET_API int crumpet_fused_unshift_unpartition_3d(void* output, const void* windows, int dtype, int64_t B,
+                                         int64_t D, int64_t H, int64_t W, int64_t C, int64_t ws_d,
+                                         int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                         int64_t ss_w, void* stream);
+
+/*
+ * Gradient of the partition: grad_x = unshift_unpartition(grad_windows).
+ * Replaces op crumpet_ops::fused_shift_partition_3d_backward
+ *   (torch-ext/torch_binding.cpp:23-25, cuda/unshift_unpartition_3d.cu:320-348).
+ */
+CRUMPET_API int crumpet_fused_shift_partition_3d_backward(void* grad_x, const void* grad_windows, int dtype,
+                                              int64_t B, int64_t D, int64_t H, int64_t W,
+                                              int64_t C, int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                                              int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                              void* stream);
+
+/*
+ * Gradient of the unpartition: grad_windows = shift_partition(grad_x).
+ * Replaces op crumpet_ops::fused_unshift_unpartition_3d_backward
+ *   (torch-ext/torch_binding.cpp:29-31, cuda/shift_partition_3d.cu:349-367).
+ */
+CRUMPET_API int crumpet_fused_unshift_unpartition_3d_backward(void* grad_windows, const void* grad_x,
+                                                  int dtype, int64_t B, int64_t D, int64_t H,
+                                                  int64_t W, int64_t C, int64_t ws_d, int64_t ws_h,
+                                                  int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                                  int64_t ss_w, void* stream);
+
+/*
+ * Shifted-window attention mask, output [nW, N, N] with N = ws_d*ws_h*ws_w <= 1024:
+ * -100 where two tokens of a window come from different roll regions, else 0
+ * (all zeros when every shift is zero).
+ * Replaces op crumpet_ops::compute_attn_mask_3d
+ *   (torch-ext/torch_binding.cpp:17-19, torch-ext/torch_binding.h:8-17,
+ *    cuda/attn_mask_3d.cu:127-168).
+ */
+CRUMPET_API int crumpet_compute_attn_mask_3d(void* output, int dtype, int64_t D, int64_t H, int64_t W,
+                                 int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                 int64_t ss_h, int64_t ss_w, void* stream);
+
+/*
+ * Fused window attention, per window b and head h:
+ *   out[b,h] = softmax(q[b,h] k[b,h]^T * scale + rel_bias[h] + mask[b % mask_windows]) v[b,h]
+ * with fp32 accumulation and softmax.  q, k, v, out: [B, H, N, head_dim];
+ * rel_bias: [H, N, N]; mask: [mask_windows, N, N] or NULL; boundary: uint8 [B]
+ * or NULL.  When boundary is given, mask rows are read only for windows with
+ * boundary[b] != 0 (the others are treated as unmasked); when it is NULL and a
+ * mask is given, every window reads its mask.  dtype: F16 or BF16 (all tensors
+ * share it); head_dim == 16; 1 <= N <= 384.
+ * Replaces crumpet.fused_attention.fused_swin_attention
+ *   (torch-ext/crumpet/fused_attention.py:149-226; kernel :48-146), which the
+ *   reference exposes only as a Python/Triton function.
+ */
+CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const void* k, const void* v,
+                                 const void* rel_bias, const void* mask, int64_t mask_windows,
+                                 const uint8_t* boundary, int dtype, int64_t B, int64_t H,
+                                 int64_t N, int64_t head_dim, float scale, void* stream);
+
+/*
+ * Device error word: non-zero once a kernel of this library gave up on a
+ * bounded wait (it then drained its work, freed its tensor memory and
+ * returned without completing its output).  Reading it synchronises with the
+ * device; `clear` != 0 resets it.  Returns the word (0 = healthy) or a negative
+ * value / CRUMPET_ERR_CUDA when it cannot be read.  No reference counterpart:
+ * the reference kernels contain no waits.
+ */
+CRUMPET_API int crumpet_device_status(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CRUMPET_B200_H_ */

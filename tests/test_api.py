@@ -1,0 +1,154 @@
+"""Host-side behaviour that needs no GPU: the C ABI library, op registration,
+argument validation, meta shapes and the mask cache (ports of the reference's
+tests/test_padding.py, test_fake_tensor.py, test_cache.py)."""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import crumpet_b200 as crumpet
+from crumpet_b200 import _ops
+from crumpet_b200.cache import clear_mask_cache, get_or_compute_mask, make_mask_key, mask_cache_info
+from helpers import header_functions
+
+REFERENCE_SCHEMAS = {
+    "compute_attn_mask_3d": "crumpet_ops::compute_attn_mask_3d(Tensor($0! -> ) output, int D, int H, int W, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+    "fused_shift_partition_3d": "crumpet_ops::fused_shift_partition_3d(Tensor($0! -> ) output, Tensor x, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+    "fused_shift_partition_3d_backward": "crumpet_ops::fused_shift_partition_3d_backward(Tensor($0! -> ) grad_x, Tensor grad_windows, int B, int D, int H, int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+    "fused_unshift_unpartition_3d": "crumpet_ops::fused_unshift_unpartition_3d(Tensor($0! -> ) output, Tensor windows, int B, int D, int H, int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+    "fused_unshift_unpartition_3d_backward": "crumpet_ops::fused_unshift_unpartition_3d_backward(Tensor($0! -> ) grad_windows, Tensor grad_x, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+}
+
+
+def test_capi_library_exports_every_declared_symbol():
+    lib = _ops.capi()
+    names = header_functions()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.crumpet_abi_version() == 1
+
+
+def test_capi_rejects_bad_arguments_without_touching_the_device():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    # D not divisible by the window
+    rc = lib.crumpet_fused_shift_partition_3d(null, null, 1, 1, 15, 14, 14, 4, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "divisible" in _ops.last_error()
+    # shift >= window
+    rc = lib.crumpet_fused_unshift_unpartition_3d(null, null, 1, 1, 14, 14, 14, 4, 7, 7, 7, 7, 0, 0, null)
+    assert rc == 1 and "shift_size[0]" in _ops.last_error()
+    # unknown dtype
+    rc = lib.crumpet_compute_attn_mask_3d(null, 7, 14, 14, 14, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "float32" in _ops.last_error()
+    # empty batch is a no-op
+    rc = lib.crumpet_fused_shift_partition_3d(null, null, 1, 0, 14, 14, 14, 4, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 0
+    # attention: unsupported head_dim / N, and an empty batch
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 343, 32, 0.25, null)
+    assert rc == 3 and "head_dim" in _ops.last_error()
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 1000, 16, 0.25, null)
+    assert rc == 3
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 0, 4, 3, 343, 16, 0.25, null)
+    assert rc == 3 and "float16" in _ops.last_error()
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 0, 3, 343, 16, 0.25, null)
+    assert rc == 0
+
+
+def test_dispatcher_ops_keep_reference_schemas():
+    ops = _ops.require()
+    for name, schema in REFERENCE_SCHEMAS.items():
+        assert str(getattr(ops, name).default._schema) == schema
+    tags = ops.fused_shift_partition_3d.default.tags
+    assert torch.Tag.pt2_compliant_tag in tags and torch.Tag.needs_fixed_stride_order in tags
+    assert "Tensor? mask" in str(ops.fused_swin_attention.default._schema)
+
+
+def test_invalid_divisibility_fails_clearly():
+    x = torch.randn((1, 15, 14, 14, 4))
+    with pytest.raises(ValueError, match="divisible"):
+        crumpet.fused_shift_partition_3d(x, (7, 7, 7), (3, 3, 3))
+
+
+def test_invalid_shift_fails_clearly():
+    x = torch.randn((1, 14, 14, 14, 4))
+    with pytest.raises(ValueError, match="shift_size"):
+        crumpet.fused_shift_partition_3d(x, (7, 7, 7), (7, 0, 0))
+
+
+def test_bad_dtype_and_shape_errors():
+    with pytest.raises(TypeError):
+        crumpet.fused_shift_partition_3d(torch.zeros((1, 4, 4, 4, 2), dtype=torch.int32), (2, 2, 2), (1, 1, 1))
+    with pytest.raises(ValueError, match="exactly three"):
+        crumpet.fused_shift_partition_3d(torch.zeros((1, 4, 4, 4, 2)), (2, 2), (1, 1, 1))
+    with pytest.raises(ValueError, match="windows must have shape"):
+        crumpet.fused_unshift_unpartition_3d(torch.zeros((7, 8, 2)), 1, 4, 4, 4, 2, (2, 2, 2), (1, 1, 1))
+
+
+def test_cpu_tensors_have_no_fallback():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.fused_shift_partition_3d(torch.zeros((1, 4, 4, 4, 2)), (2, 2, 2), (1, 1, 1))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.compute_attn_mask_3d(4, 4, 4, (2, 2, 2), (1, 1, 1), torch.float32, "cpu")
+
+
+def test_meta_shape_propagation():
+    x = torch.empty((2, 14, 14, 14, 48), device="meta", dtype=torch.float16)
+    windows = crumpet.fused_shift_partition_3d(x, (7, 7, 7), (3, 3, 3))
+    assert windows.shape == (16, 343, 48)
+    restored = crumpet.fused_unshift_unpartition_3d(windows, 2, 14, 14, 14, 48, (7, 7, 7), (3, 3, 3))
+    assert restored.shape == x.shape
+    mask = crumpet.compute_attn_mask_3d(14, 14, 14, (7, 7, 7), (3, 3, 3), torch.float16, "meta")
+    assert mask.shape == (8, 343, 343)
+
+
+def test_cache_hit_and_miss():
+    clear_mask_cache()
+    calls = {"n": 0}
+    key = make_mask_key(14, 14, 14, (7, 7, 7), (3, 3, 3), torch.float32, "cpu")
+
+    def compute():
+        calls["n"] += 1
+        return torch.zeros((1,), dtype=torch.float32)
+
+    a = get_or_compute_mask(key, compute)
+    b = get_or_compute_mask(key, compute)
+    assert a is b and calls["n"] == 1
+    assert mask_cache_info()["entries"] == 1
+
+
+def test_cache_disabled(monkeypatch):
+    clear_mask_cache()
+    monkeypatch.setenv("CRUMPET_DISABLE_MASK_CACHE", "1")
+    key = make_mask_key(14, 14, 14, (7, 7, 7), (3, 3, 3), torch.float32, "cpu")
+    a = get_or_compute_mask(key, lambda: torch.zeros((1,)))
+    b = get_or_compute_mask(key, lambda: torch.ones((1,)))
+    assert not torch.equal(a, b)
+
+
+def test_cache_byte_cap(monkeypatch):
+    clear_mask_cache()
+    monkeypatch.setenv("CRUMPET_MASK_CACHE_MAX_BYTES", "1")
+    key = make_mask_key(14, 14, 14, (7, 7, 7), (3, 3, 3), torch.float32, "cpu")
+    get_or_compute_mask(key, lambda: torch.zeros((2,), dtype=torch.float32))
+    assert mask_cache_info()["entries"] == 0
+
+
+def test_cache_lru_eviction(monkeypatch):
+    clear_mask_cache()
+    monkeypatch.setenv("CRUMPET_MASK_CACHE_SIZE", "2")
+    keys = [make_mask_key(d, 14, 14, (7, 7, 7), (3, 3, 3), torch.float32, "cpu") for d in (7, 14, 21)]
+    for key in keys:
+        get_or_compute_mask(key, lambda: torch.zeros((4,)))
+    info = mask_cache_info()
+    assert info["entries"] == 2 and info["bytes"] == 32
+
+
+def test_reference_functions_round_trip_on_cpu():
+    x = torch.randn((2, 8, 8, 8, 3))
+    w = crumpet.unfused_shift_partition_3d_reference(x, (4, 4, 4), (2, 2, 2))
+    back = crumpet.unfused_unshift_unpartition_3d_reference(w, 2, 8, 8, 8, 3, (4, 4, 4), (2, 2, 2))
+    assert torch.equal(back, x)
