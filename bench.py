@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""End-to-end benchmark: Swin UNETR 96^3 sliding-window inference, ROIs/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: MONAI-architecture Swin UNETR (in 1, out 14,
+feature 48, depths 2,2,2,2, heads 3,6,12,24, window 7, patch 2), random init
+(seed 0), fp16 autocast, sliding-window inference with 96^3 ROIs at 0.5
+overlap over a synthetic 1x1x512x512x224 volume of uniform[-1000, 1000]
+intensities scaled to [0, 1]: 400 ROIs per step, batches of 4, arg-max
+segmentation.  A step is one full volume.  With N GPUs (torchrun, one process
+per GPU) the ROI batches are dealt round-robin to the ranks and one NCCL
+reduce merges the accumulators on rank 0 (total work fixed: strong scaling).
+
+``value``: ROIs/s with the volume resident in HBM and the segmentation left
+on the device, CUDA-event timed, max over ranks.  ``e2e``: the same with the
+volume copied from pinned host memory and the segmentation copied back inside
+every step.  The 3.3 GB accumulator and 235 MB volume exceed L2, so no flush is
+needed between steps.  Also reported: live timing of the fused attention
+kernel inside the timed region (roofline), stand-alone per-kernel HBM GB/s at
+the BASELINE stage-0 sizes, clocks sampled during the timed region, and the
+CPU eager baseline (the unpatched network on the host cores).
+
+``--impl reference``: times the reference path on the CPU -- the eager,
+unpatched network (torch.roll / window partition / eager attention, i.e. the
+MONAI code path crumpet patches) on one ROI per step with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Swin UNETR 96³ ROIs/s (fp16, 1/2/4/8 B200); per-kernel HBM GB/s vs peak"
+UNIT = "ROIs/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                  "source": "fallback"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--sw-batch", type=int, default=4)
+    ap.add_argument("--volume", type=int, nargs=3, default=(512, 512, 224))
+    ap.add_argument("--roi", type=int, default=96)
+    ap.add_argument("--overlap", type=float, default=0.5)
+    ap.add_argument("--skip-kernels", action="store_true", help="omit stand-alone kernel timings")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
+    return ap.parse_args()
+
+
+def load_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        data["source"] = "measured"
+        return data
+    return dict(FALLBACK_PEAKS)
+
+
+def build_model(device):
+    import torch
+
+    from crumpet_b200.swin_unetr import SwinUNETR
+
+    torch.manual_seed(0)
+    model = SwinUNETR(in_channels=1, out_channels=14, feature_size=48, depths=(2, 2, 2, 2),
+                      num_heads=(3, 6, 12, 24))
+    return model.to(device).eval()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.gpu_ids = gpu_ids
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={','.join(str(i) for i in self.gpu_ids)}",
+                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.tmp.flush()
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def visible_gpu_ids(world: int) -> list[int]:
+    env = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if env:
+        ids = [int(x) for x in env.split(",") if x.strip().isdigit()]
+        if ids:
+            return ids[:world]
+    return list(range(world))
+
+
+def time_kernels(device, peaks) -> dict:
+    """Stand-alone kernel timings at the BASELINE stage-0 sizes (configs 2 and 3)."""
+    import torch
+
+    import crumpet_b200 as crumpet
+
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)
+
+    def timed(fn, iters=20, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iters):
+            flush.zero_()  # evict L2 (126 MB) between iterations
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        return statistics.median(times)
+
+    hbm = peaks["hbm_gbs"]
+    res = {}
+    g = torch.Generator(device=device).manual_seed(2)
+    x = torch.randn((1, 98, 98, 98, 48), device=device, generator=g).half()
+    ws, ss = (7, 7, 7), (3, 3, 3)
+    win = crumpet.fused_shift_partition_3d(x, ws, ss)
+    nbytes = 2 * x.numel() * x.element_size()
+    ms = timed(lambda: crumpet.fused_shift_partition_3d(x, ws, ss))
+    res["fused_shift_partition_3d"] = {"config": "[1,98,98,98,48] fp16 ws7 ss3", "ms": ms,
+                                       "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                       "frac_hbm": nbytes / ms / 1e6 / hbm}
+    ms = timed(lambda: crumpet.fused_unshift_unpartition_3d(win, 1, 98, 98, 98, 48, ws, ss))
+    res["fused_unshift_unpartition_3d"] = {"config": "[2744,343,48] fp16 ws7 ss3", "ms": ms,
+                                           "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                           "frac_hbm": nbytes / ms / 1e6 / hbm}
+    mask = torch.empty((2744, 343, 343), dtype=torch.float16, device=device)
+    ops = crumpet._ops.require()
+    ms = timed(lambda: ops.compute_attn_mask_3d(mask, 98, 98, 98, *ws, *ss))
+    mbytes = mask.numel() * 2
+    res["compute_attn_mask_3d"] = {"config": "[2744,343,343] fp16 (write-only)", "ms": ms,
+                                   "bytes": mbytes, "gbs": mbytes / ms / 1e6,
+                                   "frac_hbm": mbytes / ms / 1e6 / hbm}
+    B, H, N = 2744, 3, 343
+    w_qkv = torch.randn((3 * 48, 48), device=device, generator=g) * 0.02
+    qkv = torch.nn.functional.linear(win.float(), w_qkv).half()
+    qkv = qkv.reshape(B, N, 3, H, 16).permute(2, 0, 3, 1, 4)
+    q, k, v = (t.contiguous() for t in qkv)
+    table = torch.randn((13 ** 3, H), device=device, generator=g) * 0.02
+    coords = torch.stack(torch.meshgrid(*(torch.arange(7),) * 3, indexing="ij")).flatten(1)
+    rel = (coords[:, :, None] - coords[:, None, :]) + 6
+    index = (rel[0] * 169 + rel[1] * 13 + rel[2]).to(device)
+    bias = table[index.reshape(-1)].reshape(N, N, H).permute(2, 0, 1).contiguous().half()
+    bnd = (mask.view(B, -1).abs().amax(1) > 0).to(torch.uint8)
+    ms = timed(lambda: crumpet.fused_swin_attention(q, k, v, bias, mask, bnd), iters=10)
+    abytes = 4 * B * H * N * 16 * 2 + H * N * N * 2 + int(bnd.sum()) * N * N * 2
+    flops = 4 * B * H * N * N * 16
+    res["fused_swin_attention"] = {"config": "2744x3x343x16 fp16, mask+boundary", "ms": ms,
+                                   "bytes": abytes, "gbs": abytes / ms / 1e6,
+                                   "frac_hbm": abytes / ms / 1e6 / hbm,
+                                   "tflops": flops / ms / 1e9,
+                                   "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
+                                   "gexp_s": B * H * N * N / ms / 1e6}
+    del flush
+    return res
+
+
+def cpu_baseline(roi: int, budget_s: float = 12.0) -> dict:
+    """The unpatched eager network on the host cores: ROIs/s on a bounded sample."""
+    import torch
+
+    from crumpet_b200.swin_unetr import SwinUNETR
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = SwinUNETR(1, 14, 48).eval()
+    x = torch.rand((1, 1, roi, roi, roi))
+    with torch.no_grad():
+        model(x)  # allocator warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            model(x)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s or n >= 8:
+                break
+    return {"value": n / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} ROI(s) of {roi}^3 through the unpatched eager network, fp32, "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from crumpet_b200.swin_unetr import SwinUNETR
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = SwinUNETR(1, 14, 48).eval()
+    x = torch.rand((1, 1, args.roi, args.roi, args.roi))
+    times = []
+    with torch.no_grad():
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            model(x)
+            dt = time.perf_counter() - t0
+            if i >= args.warmup:
+                times.append(dt)
+    total = sum(times)
+    value = len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "swin_unetr_sliding_window_rois", "roi": [args.roi] * 3,
+                   "feature_size": 48, "step": "one ROI forward (bounded CPU sample)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"1 ROI per step, unpatched eager network, fp32, {threads} threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import crumpet_b200 as crumpet
+    from crumpet_b200 import monai_patch, profiling, swin_unetr
+    from crumpet_b200.inferer import SlidingWindowInferer, roi_grid, synthetic_volume
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    peaks = load_peaks()
+
+    model = build_model(device)
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    inferer = SlidingWindowInferer(model, (args.roi,) * 3, args.sw_batch, args.overlap, 14,
+                                   torch.float16, rank, world)
+    spatial = tuple(args.volume)
+    n_rois = len(roi_grid(spatial, (args.roi,) * 3, args.overlap))
+    host = synthetic_volume((1, 1, *spatial)).pin_memory()
+    vol = host.to(device)
+    seg_host = torch.empty(spatial, dtype=torch.uint8).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        inferer.segment(vol)
+    torch.cuda.synchronize()
+
+    # ---- timed region 1: volume resident in HBM
+    launches0 = profiling.total_launches()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(visible_gpu_ids(world) if rank == 0 else []) as clocks, \
+            profiling.KernelTimer() as ktimer:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            inferer.segment(vol)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    dev_ms = max_over_ranks(start.elapsed_time(end))
+    launches = profiling.total_launches() - launches0
+    clock = clocks.summary() if rank == 0 else None
+    attn = ktimer.summary()
+
+    # ---- timed region 2: host buffers in, segmentation out (the public call)
+    barrier()
+    torch.cuda.synchronize()
+    s2 = torch.cuda.Event(enable_timing=True)
+    e2 = torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        vol.copy_(host, non_blocking=True)
+        seg = inferer.segment(vol)
+        if seg is not None:
+            seg_host.copy_(seg, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+
+    total_launches = launches
+    if world > 1:
+        t = torch.tensor([launches], dtype=torch.int64, device=device)
+        dist.all_reduce(t)
+        total_launches = int(t.item())
+
+    kernels = None
+    if rank == 0 and not args.skip_kernels:
+        kernels = time_kernels(device, peaks)
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.roi)
+
+    if rank == 0:
+        value = n_rois * args.steps / (dev_ms / 1000.0)
+        e2e_value = n_rois * args.steps / (e2e_ms / 1000.0)
+        roofline = None
+        if attn.get("launches"):
+            gbs = attn["bytes"] / attn["avg_ms"] / 1e6
+            tflops = attn["flops"] / attn["avg_ms"] / 1e9
+            f_hbm = gbs / peaks["hbm_gbs"]
+            f_tc = tflops / peaks["bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks else "bf16_tflops"]
+            sm_mhz = (clock or {}).get("sm_mhz") or 1965.0
+            exp_peak = 16 * 148 * sm_mhz * 1e6  # MUFU ex2 lanes per SM per clock
+            exp_rate = attn["exps"] / (attn["avg_ms"] / 1e3)
+            hbm_side = f_hbm >= f_tc
+            roofline = {
+                "kernel": "window_attention_kernel (fused_swin_attention)",
+                "bound": "hbm" if hbm_side else "tensor",
+                "achieved": gbs if hbm_side else tflops,
+                "peak": peaks["hbm_gbs"] if hbm_side else peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
+                "unit": "GB/s" if hbm_side else "TFLOP/s",
+                "frac": f_hbm if hbm_side else f_tc,
+                "peak_source": peaks["source"],
+                "traffic": None,
+                "launches_timed": attn["launches"],
+                "avg_launch_ms": attn["avg_ms"],
+                "algorithmic_bytes_per_launch": attn["bytes"],
+                "flops_per_launch": attn["flops"],
+                "tensor_tflops": tflops, "tensor_frac": f_tc,
+                "hbm_gbs": gbs, "hbm_frac": f_hbm,
+                "exp": {"achieved_gexp_s": exp_rate / 1e9, "peak_gexp_s": exp_peak / 1e9,
+                        "frac": exp_rate / exp_peak,
+                        "note": "softmax exponentials on the SFU (16/clk/SM at the sampled SM clock)"},
+            }
+            traffic_file = ROOT / "profiles" / "attention_traffic.json"
+            if traffic_file.exists():
+                tr = json.loads(traffic_file.read_text())
+                roofline["traffic"] = tr.get("e2e_avg_dram_bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "swin_unetr_sliding_window", "volume": list(spatial),
+                       "roi": [args.roi] * 3, "overlap": args.overlap, "sw_batch": args.sw_batch,
+                       "rois_per_step": n_rois, "feature_size": 48, "depths": [2, 2, 2, 2],
+                       "heads": [3, 6, 12, 24], "window": 7, "classes": 14,
+                       "parallelism": f"roi-shard x{world}",
+                       "l2": "inputs larger than L2 (235 MB volume, 3.3 GB fp32 accumulator)"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": host.numel() * host.element_size() * world,
+                    "d2h_bytes_per_step": seg_host.numel()},
+            "gpu_launches": total_launches,
+            "clocks": clock,
+            "roofline": roofline,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+    crumpet.unpatch_monai_swin_unetr()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -24,6 +24,7 @@ from typing import Sequence
 import torch
 
 from . import _ops as _native
+from . import profiling as _prof
 from .cache import clear_mask_cache, get_or_compute_mask, make_mask_key, mask_cache_info
 from .reference import (
     compute_attn_mask_3d_reference,
@@ -148,6 +149,7 @@ def compute_attn_mask_3d(
         out = torch.empty((num_windows, volume, volume), dtype=dtype, device=dev)
         with _nvtx_range("crumpet.compute_attn_mask_3d"):
             _native.require().compute_attn_mask_3d(out, D, H, W, *window_size, *shift_size)
+            _prof.count("compute_attn_mask_3d")
         return out
 
     return get_or_compute_mask(make_mask_key(D, H, W, window_size, shift_size, dtype, dev), compute)
@@ -221,6 +223,7 @@ def fused_shift_partition_3d(
             return _ShiftPartitionFn.apply(x, window_size, shift_size)
         out = torch.empty((B * num_windows, volume, C), dtype=x.dtype, device=x.device)
         _native.require().fused_shift_partition_3d(out, x.contiguous(), *window_size, *shift_size)
+        _prof.count("fused_shift_partition_3d")
         return out
 
 
@@ -256,6 +259,7 @@ def fused_unshift_unpartition_3d(
         _native.require().fused_unshift_unpartition_3d(
             out, windows.contiguous(), B, D, H, W, C, *window_size, *shift_size
         )
+        _prof.count("fused_unshift_unpartition_3d")
         return out
 
 

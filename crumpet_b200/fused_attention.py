@@ -21,6 +21,7 @@ from __future__ import annotations
 import torch
 
 from . import _ops as _native
+from . import profiling as _prof
 
 
 def fused_swin_attention(
@@ -63,9 +64,23 @@ def fused_swin_attention(
             bnd = boundary if boundary.dtype == torch.uint8 else boundary.to(torch.uint8)
             bnd = bnd.contiguous()
     out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    _native.require().fused_swin_attention(
-        out, q.contiguous(), k.contiguous(), v.contiguous(), bias, mask_t, bnd, float(scale)
-    )
+    ops = _native.require()
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    token = None
+    if _prof._active:
+        esize = q.element_size()
+        masked = 0 if mask_t is None else (B if bnd is None else bnd)
+        token = _prof.attention_begin({
+            # algorithmic bytes: q, k, v, out, the bias once, plus the mask rows
+            # of masked windows (resolved when the timer is summarised)
+            "bytes": 4 * B * H * N * D * esize + H * N * N * esize,
+            "mask_bytes": (masked, N * N * esize),
+            "flops": 4 * B * H * N * N * D,
+            "exps": B * H * N * N,
+        })
+    ops.fused_swin_attention(out, q, k, v, bias, mask_t, bnd, float(scale))
+    _prof.count("fused_swin_attention")
+    _prof.attention_end(token)
     return out
 
 

@@ -1,0 +1,125 @@
+"""Sliding-window ROI inference for Swin UNETR, sharded by ROI across GPUs.
+
+Semantics of MONAI's ``sliding_window_inference`` with ``mode="constant"``
+(the driver of the reference's end-to-end runs, torch-ext/crumpet/demo_btcv.py:98-129):
+ROIs of ``roi_size`` at a stride of ``int(roi * (1 - overlap))`` per axis, the
+last ROI of every axis clamped to end at the volume edge, ``sw_batch_size``
+ROIs per forward, predictions summed into a float32 accumulator and divided
+by the per-voxel ROI count.
+
+Multi-GPU: one process per GPU.  ROI batches are dealt round-robin to ranks
+(rank r runs batches r, r + world, ...); each rank accumulates its own
+predictions, and the only collective is one NCCL sum-reduce of the
+accumulator onto rank 0 at the end, which then normalises and takes the
+arg-max.  There is no inter-GPU traffic inside the model.
+"""
+
+from __future__ import annotations
+
+import itertools
+from typing import Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def axis_starts(size: int, roi: int, overlap: float) -> list[int]:
+    """Start offsets of the ROIs along one axis."""
+    if size <= roi:
+        return [0]
+    interval = max(int(roi * (1.0 - overlap)), 1)
+    count = -(-(size - roi) // interval) + 1
+    return [min(i * interval, size - roi) for i in range(count)]
+
+
+def roi_grid(spatial: Sequence[int], roi: Sequence[int], overlap: float) -> list[tuple[int, int, int]]:
+    starts = [axis_starts(s, r, overlap) for s, r in zip(spatial, roi)]
+    return list(itertools.product(*starts))
+
+
+class SlidingWindowInferer:
+    """Runs ``model`` over a ``[1, C_in, D, H, W]`` volume in ROI batches.
+
+    ``rank``/``world`` select this process's share of the ROI batches (a
+    single-process run is rank 0 of 1).  ``autocast_dtype`` wraps every
+    forward in ``torch.autocast`` (fp16 in the benchmark, as in the
+    reference's runs).
+    """
+
+    def __init__(self, model: torch.nn.Module, roi_size=(96, 96, 96), sw_batch_size: int = 4,
+                 overlap: float = 0.5, num_classes: int = 14,
+                 autocast_dtype: torch.dtype | None = torch.float16, rank: int = 0, world: int = 1,
+                 group=None):
+        self.model = model
+        self.roi = tuple(int(r) for r in roi_size)
+        self.sw_batch = int(sw_batch_size)
+        self.overlap = float(overlap)
+        self.num_classes = int(num_classes)
+        self.autocast_dtype = autocast_dtype
+        self.rank = rank
+        self.world = world
+        self.group = group
+        self._count_cache: dict = {}
+
+    def rois(self, spatial) -> list[tuple[int, int, int]]:
+        return roi_grid(spatial, self.roi, self.overlap)
+
+    def my_batches(self, spatial) -> list[list[tuple[int, int, int]]]:
+        starts = self.rois(spatial)
+        batches = [starts[i:i + self.sw_batch] for i in range(0, len(starts), self.sw_batch)]
+        return batches[self.rank::self.world]
+
+    def _count_map(self, spatial, device) -> torch.Tensor:
+        key = (tuple(spatial), device)
+        if key not in self._count_cache:
+            cnt = torch.zeros((1, 1, *spatial), dtype=torch.float32, device=device)
+            rd, rh, rw = self.roi
+            for z, y, x in self.rois(spatial):
+                cnt[..., z:z + rd, y:y + rh, x:x + rw] += 1.0
+            self._count_cache[key] = cnt
+        return self._count_cache[key]
+
+    @torch.no_grad()
+    def accumulate(self, volume: torch.Tensor) -> tuple[torch.Tensor, int]:
+        """This rank's summed predictions [1, classes, D, H, W] (fp32) and its ROI count."""
+        spatial = tuple(int(s) for s in volume.shape[2:])
+        rd, rh, rw = self.roi
+        acc = torch.zeros((1, self.num_classes, *spatial), dtype=torch.float32, device=volume.device)
+        done = 0
+        for batch in self.my_batches(spatial):
+            window = torch.cat([volume[..., z:z + rd, y:y + rh, x:x + rw] for z, y, x in batch])
+            if self.autocast_dtype is not None:
+                with torch.autocast("cuda", dtype=self.autocast_dtype):
+                    pred = self.model(window)
+            else:
+                pred = self.model(window)
+            for i, (z, y, x) in enumerate(batch):
+                acc[0, :, z:z + rd, y:y + rh, x:x + rw] += pred[i].float()
+            done += len(batch)
+        return acc, done
+
+    @torch.no_grad()
+    def logits(self, volume: torch.Tensor) -> torch.Tensor | None:
+        """Averaged logits on rank 0 (None on other ranks)."""
+        acc, _ = self.accumulate(volume)
+        if self.world > 1:
+            dist.reduce(acc, dst=0, op=dist.ReduceOp.SUM, group=self.group)
+            if self.rank != 0:
+                return None
+        return acc / self._count_map(tuple(acc.shape[2:]), acc.device)
+
+    @torch.no_grad()
+    def segment(self, volume: torch.Tensor) -> torch.Tensor | None:
+        """uint8 label map [D, H, W] on rank 0 (None on other ranks)."""
+        logits = self.logits(volume)
+        if logits is None:
+            return None
+        # The positive count normaliser does not change the arg-max.
+        return logits[0].argmax(dim=0).to(torch.uint8)
+
+
+def synthetic_volume(shape=(1, 1, 512, 512, 224), seed: int = 0) -> torch.Tensor:
+    """Uniform [-1000, 1000] intensities clipped and scaled to [0, 1] (CPU, fp32)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand(shape, generator=g) * 2000.0 - 1000.0
+    return ((x.clamp(-1000.0, 1000.0) + 1000.0) / 2000.0).contiguous()

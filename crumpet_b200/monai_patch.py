@@ -1,0 +1,195 @@
+"""Reversible patch of MONAI-architecture Swin UNETR blocks onto crumpet_b200.
+
+Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
+``patch_monai_swin_unetr`` replaces
+
+* ``SwinTransformerBlock.forward_part1``: LayerNorm -> pad -> fused roll +
+  partition -> attention -> fused unpartition + reverse roll -> crop
+  (reference :72-114);
+* ``BasicLayer.forward``: channels-last permute, the cached shifted-window mask
+  from ``compute_attn_mask_3d`` on the padded grid, blocks, downsample
+  (reference :201-232);
+* ``WindowAttention.forward``: qkv Linear -> fused tcgen05 window attention ->
+  proj Linear (reference :117-198), falling back to the module's own eager
+  forward in training, with attention dropout, for head_dim != 16 or for
+  fp32 activations;
+
+returns True when it installs the patch and False when it is already active;
+``unpatch_monai_swin_unetr`` restores the originals.  It raises RuntimeError
+when the target module lacks one of the patched names.
+
+``swin_module`` selects the module to patch: MONAI's
+``monai.networks.nets.swin_unetr`` by default (as in the reference), or
+``crumpet_b200.swin_unetr``, the bundled MONAI-architecture network.
+
+Differences from the reference glue, all of them removals of work: the mask
+is never tiled with ``repeat`` (the kernel indexes it modulo the number of
+windows), and the per-window boundary flags are derived once per mask from
+the window geometry instead of an ``abs().amax()`` scan of the whole mask on
+every attention call.
+"""
+
+from __future__ import annotations
+
+import functools
+import os
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+
+from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpartition_3d
+from .fused_attention import fused_swin_attention
+
+_STATE: dict[str, Any] = {}
+_BOUNDARY_ATTR = "_crumpet_boundary"
+
+
+def _fused_attn_enabled() -> bool:
+    """Opt out of the fused attention with CRUMPET_DISABLE_FUSED_ATTN=1."""
+    return os.environ.get("CRUMPET_DISABLE_FUSED_ATTN", "0") != "1"
+
+
+def _load_swin(swin_module):
+    if swin_module is None:
+        try:
+            import monai.networks.nets.swin_unetr as swin_module  # type: ignore
+        except Exception as exc:
+            raise RuntimeError("MONAI Swin UNETR is not importable") from exc
+    for name in ("SwinTransformerBlock", "BasicLayer", "WindowAttention", "get_window_size"):
+        if not hasattr(swin_module, name):
+            raise RuntimeError(f"{swin_module.__name__} is missing {name}")
+    return swin_module
+
+
+def _as_triple(value) -> tuple[int, int, int]:
+    if len(value) != 3:
+        raise RuntimeError("crumpet_b200 MONAI patch only supports 3D Swin blocks")
+    return tuple(int(v) for v in value)  # type: ignore[return-value]
+
+
+def boundary_flags(dims, window_size, shift_size, device) -> torch.Tensor:
+    """uint8 [nW]: 1 for windows whose shifted mask has a -100 entry.
+
+    A window's mask is non-zero exactly when it is the last window along an
+    axis with a non-zero shift (the roll seam); this is the closed form of
+    the reference's ``mask.abs().amax(dim=1) > 0`` (monai_patch.py:177-178).
+    """
+    nd, nh, nw_ = (dims[a] // window_size[a] for a in range(3))
+    idx = [torch.arange(n) for n in (nd, nh, nw_)]
+    last = [(i == n - 1) & (shift_size[a] > 0) for a, (i, n) in enumerate(zip(idx, (nd, nh, nw_)))]
+    flags = last[0][:, None, None] | last[1][None, :, None] | last[2][None, None, :]
+    return flags.reshape(-1).to(torch.uint8).to(device, non_blocking=True)
+
+
+def _patched_forward_part1(original, swin):
+    @functools.wraps(original)
+    def forward_part1(self, x, mask_matrix):
+        if x.dim() != 5:
+            return original(self, x, mask_matrix)
+        x = self.norm1(x)
+        b, d, h, w, c = x.shape
+        window_size, shift_size = swin.get_window_size((d, h, w), self.window_size, self.shift_size)
+        window_size = _as_triple(window_size)
+        shift_size = _as_triple(shift_size)
+        pad_d = (window_size[0] - d % window_size[0]) % window_size[0]
+        pad_h = (window_size[1] - h % window_size[1]) % window_size[1]
+        pad_w = (window_size[2] - w % window_size[2]) % window_size[2]
+        x = F.pad(x, (0, 0, 0, pad_w, 0, pad_h, 0, pad_d))
+        _, dp, hp, wp, _ = x.shape
+        attn_mask = mask_matrix if any(s > 0 for s in shift_size) else None
+        x_windows = fused_shift_partition_3d(x, window_size, shift_size)
+        attn_windows = self.attn(x_windows, mask=attn_mask)
+        x = fused_unshift_unpartition_3d(attn_windows, b, dp, hp, wp, c, window_size, shift_size)
+        if pad_d or pad_h or pad_w:
+            x = x[:, :d, :h, :w, :].contiguous()
+        return x
+
+    return forward_part1
+
+
+def _patched_window_attention_forward(original):
+    @functools.wraps(original)
+    def forward(self, x, mask):
+        if self.training or self.attn_drop.p != 0.0 or not _fused_attn_enabled():
+            return original(self, x, mask)
+        b, n, c = x.shape
+        heads = self.num_heads
+        head_dim = c // heads
+        qkv = self.qkv(x)
+        if head_dim != 16 or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
+            return original(self, x, mask)
+        qkv = qkv.reshape(b, n, 3, heads, head_dim).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        index = self.relative_position_index[:n, :n].reshape(-1)
+        rel_bias = self.relative_position_bias_table[index].reshape(n, n, -1)
+        rel_bias = rel_bias.permute(2, 0, 1).contiguous().to(qkv.dtype)
+        boundary = None
+        if mask is not None:
+            flags = getattr(mask, _BOUNDARY_ATTR, None)
+            if flags is None:
+                flags = (mask.reshape(mask.shape[0], -1).abs().amax(dim=1) > 0).to(torch.uint8)
+            boundary = flags.repeat(b // mask.shape[0]) if b != mask.shape[0] else flags
+            mask = mask.to(qkv.dtype)
+        out = fused_swin_attention(q.contiguous(), k.contiguous(), v.contiguous(), rel_bias, mask,
+                                   boundary, scale=self.scale)
+        out = out.transpose(1, 2).reshape(b, n, c)
+        return self.proj_drop(self.proj(out))
+
+    return forward
+
+
+def _patched_basic_layer_forward(original, swin):
+    @functools.wraps(original)
+    def forward(self, x):
+        if x.dim() != 5:
+            return original(self, x)
+        b, c, d, h, w = x.shape
+        window_size, shift_size = swin.get_window_size((d, h, w), self.window_size, self.shift_size)
+        window_size = _as_triple(window_size)
+        shift_size = _as_triple(shift_size)
+        x = x.permute(0, 2, 3, 4, 1).contiguous()
+        dims = tuple(-(-s // ws) * ws for s, ws in zip((d, h, w), window_size))
+        attn_mask = compute_attn_mask_3d(*dims, window_size, shift_size, x.dtype, x.device)
+        if getattr(attn_mask, _BOUNDARY_ATTR, None) is None:
+            setattr(attn_mask, _BOUNDARY_ATTR, boundary_flags(dims, window_size, shift_size, x.device))
+        for blk in self.blocks:
+            x = blk(x, attn_mask)
+        x = x.view(b, d, h, w, -1)
+        if self.downsample is not None:
+            x = self.downsample(x)
+        return x.permute(0, 4, 1, 2, 3).contiguous()
+
+    return forward
+
+
+def patch_monai_swin_unetr(swin_module=None) -> bool:
+    """Install the patch; True on the installing call, False if already active."""
+    if _STATE.get("patched"):
+        return False
+    swin = _load_swin(swin_module)
+    _STATE.update(
+        patched=True,
+        swin=swin,
+        forward_part1=swin.SwinTransformerBlock.forward_part1,
+        basic_layer_forward=swin.BasicLayer.forward,
+    )
+    swin.SwinTransformerBlock.forward_part1 = _patched_forward_part1(_STATE["forward_part1"], swin)
+    swin.BasicLayer.forward = _patched_basic_layer_forward(_STATE["basic_layer_forward"], swin)
+    if _fused_attn_enabled():
+        _STATE["window_attention_forward"] = swin.WindowAttention.forward
+        swin.WindowAttention.forward = _patched_window_attention_forward(swin.WindowAttention.forward)
+    return True
+
+
+def unpatch_monai_swin_unetr() -> bool:
+    """Restore the original methods; True if a patch was removed."""
+    if not _STATE.get("patched"):
+        return False
+    swin = _STATE["swin"]
+    swin.SwinTransformerBlock.forward_part1 = _STATE["forward_part1"]
+    swin.BasicLayer.forward = _STATE["basic_layer_forward"]
+    if "window_attention_forward" in _STATE:
+        swin.WindowAttention.forward = _STATE["window_attention_forward"]
+    _STATE.clear()
+    return True

@@ -1,0 +1,69 @@
+"""Patched vs eager Swin UNETR on the GPU under fp16 autocast (BASELINE config 5
+criteria: segmentation arg-max agreement >= 99.9 %; logits within fp16
+tolerance), and a Swin block at BASELINE config 1 geometry."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import crumpet_b200 as crumpet
+from crumpet_b200 import profiling, swin_unetr
+from crumpet_b200.inferer import SlidingWindowInferer
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(model, x, patched):
+    if patched:
+        crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.float16):
+            return model(x).float()
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+
+
+def test_shifted_block_matches_eager(cuda_device):
+    torch.manual_seed(0)
+    blk = swin_unetr.SwinTransformerBlock(48, 3, (7, 7, 7), (3, 3, 3)).to(cuda_device).eval()
+    with torch.no_grad():
+        blk.attn.relative_position_bias_table.normal_(0, 0.02)
+    x = torch.randn((1, 28, 28, 28, 48), device=cuda_device)
+    mask = swin_unetr.compute_mask((28, 28, 28), (7, 7, 7), (3, 3, 3), cuda_device)
+    before = profiling.total_launches()
+    patched = _run(lambda t: blk(t, crumpet.compute_attn_mask_3d(28, 28, 28, (7, 7, 7), (3, 3, 3),
+                                                               torch.float16, cuda_device)), x, True)
+    assert profiling.counters["fused_swin_attention"] > 0
+    assert profiling.total_launches() - before >= 3
+    eager = _run(lambda t: blk(t, mask), x, False)
+    assert (patched - eager).abs().max().item() < 2e-2
+
+
+def test_network_argmax_agreement_one_batch(cuda_device):
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    x = torch.rand((2, 1, 96, 96, 96), device=cuda_device)
+    patched = _run(model, x, True)
+    eager = _run(model, x, False)
+    agree = (patched.argmax(1) == eager.argmax(1)).float().mean().item()
+    assert agree >= 0.999, agree
+    assert (patched - eager).abs().max().item() < 5e-2
+
+
+def test_sliding_window_patched_vs_eager(cuda_device):
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    vol = torch.rand((1, 1, 128, 128, 96), device=cuda_device)
+    inf = SlidingWindowInferer(model, (96, 96, 96), 2, 0.5, 14, torch.float16)
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        seg_p = inf.segment(vol)
+        logit_p = inf.logits(vol)
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+    seg_e = inf.segment(vol)
+    logit_e = inf.logits(vol)
+    agree = (seg_p == seg_e).float().mean().item()
+    assert agree >= 0.999, agree
+    assert (logit_p - logit_e).abs().max().item() < 5e-2

@@ -1,0 +1,96 @@
+"""Patch / unpatch contract, the bundled MONAI-architecture network and the ROI
+driver, on the CPU (reference tests/test_monai_patch.py, plus the pieces the
+end-to-end run relies on)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import crumpet_b200 as crumpet
+from crumpet_b200 import monai_patch, swin_unetr
+from crumpet_b200.inferer import SlidingWindowInferer, axis_starts, roi_grid
+from oracle import mechanics as OM
+
+
+def test_patch_unpatch_repeated_safe():
+    originals = (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.BasicLayer.forward,
+                 swin_unetr.WindowAttention.forward)
+    assert crumpet.patch_monai_swin_unetr(swin_unetr) is True
+    assert crumpet.patch_monai_swin_unetr(swin_unetr) is False
+    assert swin_unetr.WindowAttention.forward is not originals[2]
+    assert crumpet.unpatch_monai_swin_unetr() is True
+    assert crumpet.unpatch_monai_swin_unetr() is False
+    assert (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.BasicLayer.forward,
+            swin_unetr.WindowAttention.forward) == originals
+
+
+def test_patch_without_monai_raises():
+    try:
+        import monai  # noqa: F401
+    except ImportError:
+        with pytest.raises(RuntimeError, match="MONAI"):
+            crumpet.patch_monai_swin_unetr()
+    else:
+        pytest.skip("MONAI is installed")
+
+
+def test_fused_attention_opt_out(monkeypatch):
+    monkeypatch.setenv("CRUMPET_DISABLE_FUSED_ATTN", "1")
+    original = swin_unetr.WindowAttention.forward
+    assert crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        assert swin_unetr.WindowAttention.forward is original
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+
+
+def test_swin_unetr_shapes_and_parameter_count():
+    model = swin_unetr.SwinUNETR(1, 14, 48)
+    assert sum(p.numel() for p in model.parameters()) == 62_187_296
+    small = swin_unetr.SwinUNETR(1, 3, 12, depths=(1, 1, 1, 1)).eval()
+    with torch.no_grad():
+        out = small(torch.rand((1, 1, 64, 64, 64)))
+    assert out.shape == (1, 3, 64, 64, 64)
+
+
+def test_eager_mask_matches_oracle():
+    m = swin_unetr.compute_mask((14, 14, 14), (7, 7, 7), (3, 3, 3), "cpu")
+    assert np.array_equal(m.numpy(), OM.attn_mask(14, 14, 14, (7, 7, 7), (3, 3, 3)))
+
+
+@pytest.mark.parametrize("dims,ws,ss", [((49, 49, 49), (7, 7, 7), (3, 3, 3)),
+                                         ((28, 28, 28), (7, 7, 7), (3, 3, 3)),
+                                         ((14, 21, 7), (7, 7, 7), (3, 0, 2)),
+                                         ((6, 6, 6), (6, 6, 6), (0, 0, 0))])
+def test_boundary_flags_closed_form(dims, ws, ss):
+    mask = OM.attn_mask(*dims, ws, ss)
+    want = (np.abs(mask).reshape(mask.shape[0], -1).max(axis=1) > 0).astype(np.uint8)
+    got = monai_patch.boundary_flags(dims, ws, ss, "cpu").numpy()
+    assert np.array_equal(got, want)
+
+
+def test_roi_grid_matches_config():
+    assert axis_starts(512, 96, 0.5) == [0, 48, 96, 144, 192, 240, 288, 336, 384, 416]
+    assert axis_starts(224, 96, 0.5) == [0, 48, 96, 128]
+    assert len(roi_grid((512, 512, 224), (96, 96, 96), 0.5)) == 400
+    assert axis_starts(64, 96, 0.5) == [0]
+
+
+def test_roi_sharding_partitions_the_batches():
+    inf = [SlidingWindowInferer(None, (96,) * 3, 4, 0.5, rank=r, world=3) for r in range(3)]
+    seen = [roi for i in inf for b in i.my_batches((512, 512, 224)) for roi in b]
+    assert len(seen) == 400 and len(set(seen)) == 400
+
+
+def test_sliding_window_eager_cpu_matches_single_forward():
+    # a volume equal to one ROI: the sliding-window result is the plain forward
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 3, 12, depths=(1, 1, 1, 1)).eval()
+    x = torch.rand((1, 1, 64, 64, 64))
+    inf = SlidingWindowInferer(model, (64, 64, 64), 1, 0.5, num_classes=3, autocast_dtype=None)
+    with torch.no_grad():
+        got = inf.logits(x)
+        want = model(x)
+    assert torch.allclose(got, want)
