@@ -1,7 +1,7 @@
 // crumpet_b200: fused 3D Swin window attention for sm_100a (B200).
 //
 // Computes, per window b and head h (head_dim 16, N <= 384 tokens),
-//   out[b,h] = softmax(q k^T * scale + bias[h] + mask[b % nmask]) v
+//   out[b,h] = softmax(q k^T * scale + bias[h] + mask) v
 // with fp32 scores and softmax -- the function of the reference Triton kernel
 // torch-ext/crumpet/fused_attention.py:48-146 (eager form: MONAI WindowAttention,
 // as described in torch-ext/crumpet/monai_patch.py:117-198).
@@ -12,24 +12,38 @@
 //     warp and 4 softmax warps (one thread per query row = one TMEM lane).
 //   * TMA loads Q (128 rows) and all K, V rows of the (window, head) into
 //     shared memory with 32-byte swizzle; rows past N are zero-filled by TMA.
+//     Two address layouts share the kernel: separate q/k/v [B, H, N, 16]
+//     tensors, or the packed qkv Linear output [B, N, 3, H, 16].
 //   * The key axis is processed in chunks of 64.  The MMA warp issues
 //     S_c = Q K_c^T (tcgen05.mma, M=128, K=16, fp32 accumulators in TMEM); the
 //     softmax warps pull S_c into registers, add the relative-position bias
-//     (shared-memory tile, reused for every window of the CTA) and the mask,
-//     take the chunk maximum m_c, write P_c = exp(x - m_c) back to TMEM as
-//     fp16/bf16, and the MMA warp accumulates O_c = P_c V_c with P read from
-//     TMEM.  Every chunk keeps its own O_c, m_c and l_c = sum(P_c), so no
-//     rescaling happens inside the loop; the epilogue combines them exactly:
+//     (a shared-memory tile per (head, query tile), reused for every window of
+//     the CTA) and the mask, take the chunk maximum m_c, write
+//     P_c = exp(x - m_c) back to TMEM as fp16/bf16, and the MMA warp
+//     accumulates O_c = P_c V_c with P read from TMEM.  Every chunk keeps its
+//     own O_c, m_c and l_c = sum(P_c) (m_c, l_c parked in TMEM), so nothing is
+//     rescaled inside the loop; the epilogue combines them exactly:
 //       out = sum_c e^(m_c - m) O_c / sum_c e^(m_c - m) l_c,  m = max_c m_c.
+//   * Bias: a dense [H, N, N] tensor, or gathered in-kernel from MONAI's
+//     relative-position table [T, H] and index [Nc, Nc] (sliced [:N, :N]).
+//   * Mask: none; dense [nW, N, N] (window b uses mask[b % nW], rows read only
+//     for windows flagged in `boundary`), read with aligned 32-bit loads and
+//     added to the bias in half2; or analytic: the shifted-window mask
+//     recomputed on chip from the window geometry (a 3-bit roll-side code per
+//     token and a 3-bit "last window on this axis" flag per window; entries
+//     whose codes differ on a flagged axis get -inf, the exact limit of the
+//     reference's -100: e^-100 underflows to 0 in fp32 either way).
 //   * Work: CTAs are split into groups, one per (head, query-tile) pair, and
 //     walk the windows in lock step, so the CTAs that need the same K/V rows
 //     (the other query tiles and heads of a window) read them close together
-//     in time and hit L2.
+//     in time and hit L2.  Warps whose 32 query rows all lie past N skip the
+//     math of a tile (their P rows only feed output rows that are discarded).
 // Every wait is bounded (2 s of %globaltimer); on expiry the kernel records an
 // error in g_device_error, drains its in-flight copies and MMAs, frees TMEM and
 // returns.
 #include <cstdio>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -53,6 +67,7 @@ constexpr int kRowBytes = kHD * 2;
 constexpr int kBarsPerWG = 2 * kStages + 7;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemPerWG = 256;
+constexpr float kLog2e = 1.4426950408889634f;
 
 template <int NPAD>
 struct Cfg {
@@ -65,21 +80,37 @@ struct Cfg {
   static constexpr int KV_BYTES = NKB * 128 * kRowBytes;
   static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
   static constexpr int BIAS_BYTES = kBM * BSTRIDE * 2;
+  static constexpr int PLANE_BYTES = 3 * NCH * 8;     // analytic-mask code planes
+  // TMEM columns of one WG: S chunk, P chunk, per-chunk O, per-chunk (m, l).
   static constexpr int TM_S = 0;
   static constexpr int TM_P = kCH;
   static constexpr int TM_O = kCH + kCH / 2;
-  static_assert(TM_O + NCH * kHD <= int(kTmemPerWG), "TMEM budget");
-  static constexpr int SMEM_BYTES =
-      1024 + kNumWG * kStages * STAGE_BYTES + BIAS_BYTES + kNumWG * kBarsPerWG * 8 + 64;
+  static constexpr int TM_STAT = TM_O + NCH * kHD;
+  static_assert(TM_STAT + 16 <= int(kTmemPerWG), "TMEM budget");
+  static constexpr int SMEM_BYTES = 1024 + kNumWG * kStages * STAGE_BYTES + BIAS_BYTES +
+                                    PLANE_BYTES + kNumWG * kBarsPerWG * 8 + 64;
 };
 
+enum MaskMode : int { kMaskNone = 0, kMaskDense = 1, kMaskAnalytic = 2 };
+
 struct KParams {
-  const uint16_t* bias;      // [H, N, N]
-  const uint16_t* mask;      // [mask_windows, N, N] or null
-  const uint8_t* boundary;   // [B] or null
+  // bias: dense [H, N, N] in the element type, or table [T, H] + index [Nc, Nc]
+  const uint16_t* bias;
+  const void* table;
+  const long long* index;
+  int index_stride;
+  int bias_from_table;
+  int table_f32;
+  // dense mask
+  const uint16_t* mask;
+  const uint8_t* boundary;
+  int mask_windows;
+  // analytic mask: windows per axis and window / shift sizes of the token grid
+  int nwd, nwh, nww, wsd, wsh, wsw, ssd, ssh, ssw;
+  // output
   uint16_t* out;
   long long out_sb, out_sh, out_sn;
-  int B, H, N, MT, P, mask_windows;
+  int B, H, N, MT, P;
   float scale;
 };
 
@@ -119,12 +150,51 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed fp32 pair arithmetic (sm_100 f32x2).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 template <bool BF16>
-__device__ __forceinline__ float to_f32(uint16_t h) {
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
   if constexpr (BF16) {
-    return __uint_as_float(uint32_t(h) << 16);
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
   } else {
-    return __half2float(__ushort_as_half(h));
+    __half2 h = *reinterpret_cast<const __half2*>(&w);
+    return __half22float2(h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t add_pairs(uint32_t a, uint32_t b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 r = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  } else {
+    __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
 }
 
@@ -139,6 +209,27 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+template <bool BF16>
+__device__ __forceinline__ uint16_t f32_to_elem(float v) {
+  if constexpr (BF16) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  } else {
+    return __half_as_ushort(__float2half_rn(v));
+  }
+}
+
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, uint32_t a, uint32_t b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(a),
+               "r"(b)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // Waits on a barrier ignoring the abort flag (used only while draining).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
@@ -147,7 +238,18 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-template <int NPAD, bool BF16, bool HAS_MASK>
+// Roll-side code of token t: bit a set when its local coordinate on axis a is
+// at or past ws_a - ss_a (the seam of the cyclic roll inside a last window).
+__device__ __forceinline__ uint32_t token_code(const KParams& p, int t) {
+  const int lw = t % p.wsw;
+  const int t2 = t / p.wsw;
+  const int lh = t2 % p.wsh;
+  const int ld = t2 / p.wsh;
+  return uint32_t(ld >= p.wsd - p.ssd) | (uint32_t(lh >= p.wsh - p.ssh) << 1) |
+         (uint32_t(lw >= p.wsw - p.ssw) << 2);
+}
+
+template <int NPAD, bool BF16, int MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 window_attention_kernel(const __grid_constant__ CUtensorMap tq,
                         const __grid_constant__ CUtensorMap tk,
@@ -157,8 +259,9 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint16_t* bias_s = reinterpret_cast<uint16_t*>(smem + kNumWG * kStages * C::STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kNumWG * kStages * C::STAGE_BYTES +
-                                               C::BIAS_BYTES);
+  uint64_t* planes = reinterpret_cast<uint64_t*>(smem + kNumWG * kStages * C::STAGE_BYTES +
+                                                 C::BIAS_BYTES);
+  uint64_t* bars = planes + 3 * C::NCH;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumWG * kBarsPerWG);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -189,6 +292,18 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     }
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if constexpr (MASK == kMaskAnalytic) {
+    // Code planes: bit j of plane[a][c] = bit a of the code of token c*64 + j.
+    if (threadIdx.x < 3 * C::NCH) {
+      const int a = threadIdx.x / C::NCH, c = threadIdx.x % C::NCH;
+      uint64_t bits = 0;
+      for (int j = 0; j < kCH; ++j) {
+        const int t = c * kCH + j;
+        if (t < p.N && ((token_code(p, t) >> a) & 1u)) bits |= uint64_t(1) << j;
+      }
+      planes[a * C::NCH + c] = bits;
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -321,8 +436,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     const uint32_t tS = tmem_base + lane_off + w * kTmemPerWG + C::TM_S;
     const uint32_t tP = tmem_base + lane_off + w * kTmemPerWG + C::TM_P;
     const uint32_t tO = tmem_base + lane_off + w * kTmemPerWG + C::TM_O;
-    const float kLog2e = 1.4426950408889634f;
+    const uint32_t tStat = tmem_base + lane_off + w * kTmemPerWG + C::TM_STAT;
     const float kNegInf = __int_as_float(0xff800000);
+    const float2 scale2 = make_float2(p.scale, p.scale);
+    const float2 log2e2 = make_float2(kLog2e, kLog2e);
     uint32_t n_sf = 0, n_pe = 0, n_of = 0;
     bool ok = true;
 
@@ -336,7 +453,18 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
         const int grow = mt * kBM + r;
         uint16_t val = 0;
-        if (grow < p.N && col < p.N) val = p.bias[(size_t(h) * p.N + grow) * p.N + col];
+        if (grow < p.N && col < p.N) {
+          if (p.bias_from_table) {
+            const long long idx = p.index[(long long)grow * p.index_stride + col];
+            if (p.table_f32) {
+              val = f32_to_elem<BF16>(static_cast<const float*>(p.table)[idx * p.H + h]);
+            } else {
+              val = static_cast<const uint16_t*>(p.table)[idx * p.H + h];
+            }
+          } else {
+            val = p.bias[(size_t(h) * p.N + grow) * p.N + col];
+          }
+        }
         bias_s[r * C::BSTRIDE + col] = val;
       }
       named_bar_sync(1, kNumWG * 128);
@@ -344,100 +472,156 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
 
       const int qrow = mt * kBM + row;
       const bool valid = qrow < p.N;
+      const bool warp_live = (mt * kBM + quarter * 32) < p.N;  // uniform per warp
       const uint16_t* brow = bias_s + row * C::BSTRIDE;
+      uint32_t code_i = 0;
+      if constexpr (MASK == kMaskAnalytic) code_i = valid ? token_code(p, qrow) : 0u;
 
       for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok; b += kNumWG * sc.win_step) {
-        bool use_mask = false;
+        // ---- per-tile mask state
+        bool use_dense = false;
         const uint16_t* mrow = nullptr;
-        if constexpr (HAS_MASK) {
-          use_mask = (p.boundary == nullptr) || (p.boundary[b] != 0);
+        uint32_t am = 0;
+        if constexpr (MASK == kMaskDense) {
+          use_dense = (p.boundary == nullptr) || (p.boundary[b] != 0);
           const int mw = b % p.mask_windows;
           mrow = p.mask + (size_t(mw) * p.N + (valid ? qrow : 0)) * p.N;
         }
-        float mc[C::NCH], lc[C::NCH];
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c) {
-          const int W = (c < C::NCH - 1) ? kCH : C::LAST_W;
-          if (!mbar_wait(bar(w, kSF), n_sf & 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
+        if constexpr (MASK == kMaskAnalytic) {
+          const int wi = b % (p.nwd * p.nwh * p.nww);
+          const int iw = wi % p.nww, t = wi / p.nww;
+          const int ih = t % p.nwh, id = t / p.nwh;
+          am = uint32_t(p.ssd != 0 && id == p.nwd - 1) |
+               (uint32_t(p.ssh != 0 && ih == p.nwh - 1) << 1) |
+               (uint32_t(p.ssw != 0 && iw == p.nww - 1) << 2);
+        }
+
+        // One chunk of W keys (W = 64, or the ragged last chunk).
+        auto chunk = [&](auto w_tag, auto tail_tag, int c) -> bool {
+          constexpr int W = decltype(w_tag)::value;
+          constexpr bool kTail = decltype(tail_tag)::value;
+          if (!mbar_wait(bar(w, kSF), n_sf & 1u, abort_flag)) return false;
           ++n_sf;
           tc_fence_after();
-          uint32_t s[kCH];
+          if (!warp_live) {
+            // No valid row in this warp: keep the barrier protocol, skip the math.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(w, kSE));
+            if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) return false;
+            ++n_pe;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(w, kPF));
+            return true;
+          }
+          uint32_t s[W];
           tmem_ld32(tS, s);
-          if (W > 32) tmem_ld32(tS + 32, s + 32);
+          if constexpr (W > 32) tmem_ld32(tS + 32, s + 32);
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(w, kSE));
 
-          float x[kCH];
+          // bias pairs for the W keys (16-byte shared loads)
+          uint32_t bw[W / 2];
 #pragma unroll
-          for (int j = 0; j < kCH; j += 8) {
-            if (j < W) {
-              const uint4 bv = *reinterpret_cast<const uint4*>(brow + c * kCH + j);
-              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                x[j + 2 * t] = fmaf(__uint_as_float(s[j + 2 * t]), p.scale,
-                                    to_f32<BF16>(uint16_t(bw[t] & 0xFFFFu)));
-                x[j + 2 * t + 1] = fmaf(__uint_as_float(s[j + 2 * t + 1]), p.scale,
-                                        to_f32<BF16>(uint16_t(bw[t] >> 16)));
-              }
-            }
+          for (int q = 0; q < W / 8; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4*>(brow + c * kCH + 8 * q);
+            bw[4 * q + 0] = v.x;
+            bw[4 * q + 1] = v.y;
+            bw[4 * q + 2] = v.z;
+            bw[4 * q + 3] = v.w;
           }
-          if constexpr (HAS_MASK) {
-            if (use_mask && valid) {
+          const int valid_cols = p.N - c * kCH;
+          if constexpr (MASK == kMaskDense) {
+            if (use_dense && valid) {
+              // mask row slice: aligned 32-bit words, re-paired when the row
+              // starts on an odd element, added to the bias pairs in half2.
+              const uintptr_t addr = reinterpret_cast<uintptr_t>(mrow + c * kCH);
+              const uint32_t odd = uint32_t(addr >> 1) & 1u;
+              const uint32_t* wp = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+              uint32_t mw[W / 2 + 1];
 #pragma unroll
-              for (int j = 0; j < kCH; ++j) {
-                if (j < W) {
-                  const int col = c * kCH + j;
-                  if (c < C::NCH - 1 || col < p.N) x[j] += to_f32<BF16>(mrow[col]);
+              for (int k = 0; k <= W / 2; ++k) {
+                // word k holds elements 2k - odd and 2k - odd + 1 of the slice
+                // (only the last chunk can run past the row end)
+                if constexpr (kTail) {
+                  mw[k] = (2 * k - int(odd) < valid_cols) ? ldg_u32(wp + k) : 0u;
+                } else {
+                  mw[k] = ldg_u32(wp + k);
                 }
               }
+              const uint32_t sel = odd ? 0x5432u : 0x3210u;
+#pragma unroll
+              for (int k = 0; k < W / 2; ++k) {
+                bw[k] = add_pairs<BF16>(bw[k], __byte_perm(mw[k], mw[k + 1], sel));
+              }
             }
           }
-          if (c == C::NCH - 1) {
+          float x[W];
 #pragma unroll
-            for (int j = 0; j < kCH; ++j) {
-              if (j < W && c * kCH + j >= p.N) x[j] = kNegInf;
+          for (int k = 0; k < W / 2; ++k) {
+            const float2 r = ffma2(make_float2(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])),
+                                   scale2, unpack2<BF16>(bw[k]));
+            x[2 * k] = r.x;
+            x[2 * k + 1] = r.y;
+          }
+          if constexpr (MASK == kMaskAnalytic) {
+            if (am != 0) {
+              uint64_t pen = 0;
+#pragma unroll
+              for (int a = 0; a < 3; ++a) {
+                if ((am >> a) & 1u) {
+                  pen |= planes[a * C::NCH + c] ^ (((code_i >> a) & 1u) ? ~uint64_t(0) : uint64_t(0));
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < W; ++j) {
+                if ((pen >> j) & 1u) x[j] = kNegInf;
+              }
+            }
+          }
+          if constexpr (kTail) {
+#pragma unroll
+            for (int j = 0; j < W; ++j) {
+              if (j >= valid_cols) x[j] = kNegInf;
             }
           }
           float m = kNegInf;
 #pragma unroll
-          for (int j = 0; j < kCH; ++j) {
-            if (j < W) m = fmaxf(m, x[j]);
-          }
-          const float mref = (m == kNegInf) ? 0.f : m;
-          const float moff = mref * kLog2e;
-          float l = 0.f;
-          uint32_t pk[kCH / 2];
+          for (int j = 0; j < W; j += 2) m = max3(m, x[j], x[j + 1]);
+          const float moff = (m == kNegInf) ? 0.f : m * kLog2e;
+          const float2 nmoff2 = make_float2(-moff, -moff);
+          float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                           make_float2(0.f, 0.f)};
+          uint32_t pk[W / 2];
 #pragma unroll
-          for (int j = 0; j < kCH; j += 2) {
-            if (j < W) {
-              const float e0 = fast_ex2(fmaf(x[j], kLog2e, -moff));
-              const float e1 = fast_ex2(fmaf(x[j + 1], kLog2e, -moff));
-              l += e0 + e1;
-              pk[j / 2] = pack2<BF16>(e0, e1);
-            }
+          for (int k = 0; k < W / 2; ++k) {
+            const float2 t = ffma2(make_float2(x[2 * k], x[2 * k + 1]), log2e2, nmoff2);
+            const float2 e = make_float2(fast_ex2(t.x), fast_ex2(t.y));
+            acc[k & 3] = fadd2(acc[k & 3], e);
+            pk[k] = pack2<BF16>(e.x, e.y);
           }
-          mc[c] = m;
-          lc[c] = l;
+          const float2 a01 = fadd2(acc[0], acc[1]);
+          const float2 a23 = fadd2(acc[2], acc[3]);
+          const float2 a = fadd2(a01, a23);
+          const float l = a.x + a.y;
           // P buffer must be free: PV of the previous chunk has completed.
-          if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) return false;
           ++n_pe;
           tc_fence_after();
           tmem_st16(tP, pk);
-          if (W > 32) tmem_st16(tP + 16, pk + 16);
+          if constexpr (W > 32) tmem_st16(tP + 16, pk + 16);
+          tmem_st2(tStat + 2 * c, __float_as_uint(m), __float_as_uint(l));
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(w, kPF));
-        }
+          return true;
+        };
+
+        for (int c = 0; c < C::NCH - 1 && ok; ++c)
+          ok = chunk(std::integral_constant<int, kCH>{}, std::false_type{}, c);
+        if (ok) ok = chunk(std::integral_constant<int, C::LAST_W>{}, std::true_type{}, C::NCH - 1);
         if (!ok) break;
 
         // ---- epilogue: combine the per-chunk partial outputs
@@ -447,9 +631,16 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         }
         ++n_of;
         tc_fence_after();
+        if (!warp_live) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(w, kOE));
+          continue;
+        }
         uint32_t o[C::NCH][kHD];
+        uint32_t stat[16];
 #pragma unroll
         for (int c = 0; c < C::NCH; ++c) tmem_ld16(tO + uint32_t(c * kHD), o[c]);
+        tmem_ld16(tStat, stat);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -457,15 +648,16 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
 
         float mmax = kNegInf;
 #pragma unroll
-        for (int c = 0; c < C::NCH; ++c) mmax = fmaxf(mmax, mc[c]);
+        for (int c = 0; c < C::NCH; ++c) mmax = fmaxf(mmax, __uint_as_float(stat[2 * c]));
         float acc[kHD];
 #pragma unroll
         for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
         float L = 0.f;
 #pragma unroll
         for (int c = 0; c < C::NCH; ++c) {
-          const float wc = (mc[c] == kNegInf) ? 0.f : fast_ex2((mc[c] - mmax) * kLog2e);
-          L = fmaf(wc, lc[c], L);
+          const float mc = __uint_as_float(stat[2 * c]);
+          const float wc = (mc == kNegInf) ? 0.f : fast_ex2((mc - mmax) * kLog2e);
+          L = fmaf(wc, __uint_as_float(stat[2 * c + 1]), L);
 #pragma unroll
           for (int d = 0; d < kHD; ++d) acc[d] = fmaf(wc, __uint_as_float(o[c][d]), acc[d]);
         }
@@ -540,12 +732,12 @@ int num_sms() {
   return sms > 0 ? sms : 148;
 }
 
-template <int NPAD, bool BF16, bool HAS_MASK>
-int launch_impl(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
-                const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
+template <int NPAD, bool BF16, int MASK>
+int launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                const KParams& kp, cudaStream_t stream) {
   using C = Cfg<NPAD>;
-  auto kern = window_attention_kernel<NPAD, BF16, HAS_MASK>;
-  static bool configured[64] = {false};  // per device; attribute is per function
+  auto kern = window_attention_kernel<NPAD, BF16, MASK>;
+  static bool configured[64] = {false};  // per device; the attribute is per function
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
@@ -563,14 +755,15 @@ int launch_impl(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
 template <int NPAD>
 int dispatch_npad(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
                   const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
-  const bool bf = a.dtype == kBF16;
-  const bool m = a.mask != nullptr;
-  if (bf) {
-    return m ? launch_impl<NPAD, true, true>(a, tq, tk, tv, kp, stream)
-             : launch_impl<NPAD, true, false>(a, tq, tk, tv, kp, stream);
+  const int mode = a.analytic ? kMaskAnalytic : (a.mask ? kMaskDense : kMaskNone);
+  if (a.dtype == kBF16) {
+    if (mode == kMaskDense) return launch_impl<NPAD, true, kMaskDense>(tq, tk, tv, kp, stream);
+    if (mode == kMaskAnalytic) return launch_impl<NPAD, true, kMaskAnalytic>(tq, tk, tv, kp, stream);
+    return launch_impl<NPAD, true, kMaskNone>(tq, tk, tv, kp, stream);
   }
-  return m ? launch_impl<NPAD, false, true>(a, tq, tk, tv, kp, stream)
-           : launch_impl<NPAD, false, false>(a, tq, tk, tv, kp, stream);
+  if (mode == kMaskDense) return launch_impl<NPAD, false, kMaskDense>(tq, tk, tv, kp, stream);
+  if (mode == kMaskAnalytic) return launch_impl<NPAD, false, kMaskAnalytic>(tq, tk, tv, kp, stream);
+  return launch_impl<NPAD, false, kMaskNone>(tq, tk, tv, kp, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -585,14 +778,25 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.B < 0 || a.H < 1) return set_error(kErrInvalid, "B must be >= 0 and H >= 1");
   if (a.B == 0) return kOk;
   if (a.B > 0x7fffffff || a.H > 0xffff) return set_error(kErrInvalid, "B or H too large");
-  if (!a.q || !a.k || !a.v || !a.out || !a.bias)
-    return set_error(kErrInvalid, "null tensor pointer");
+  if (!a.q || !a.k || !a.v || !a.out) return set_error(kErrInvalid, "null tensor pointer");
+  if (a.bias_from_table ? (!a.table || !a.index) : !a.bias)
+    return set_error(kErrInvalid, "null bias pointer");
+  if (a.bias_from_table && a.index_stride < a.N)
+    return set_error(kErrInvalid, "relative position index is smaller than N x N");
   if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(a.out))
     return set_error(kErrInvalid, "q, k, v and out must be 16-byte aligned");
   if ((a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 != 0 ||
       (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 != 0)
     return set_error(kErrInvalid, "q/k/v/out strides must be multiples of 8 elements");
   if (a.mask && a.mask_windows < 1) return set_error(kErrInvalid, "mask_windows must be >= 1");
+  if (a.analytic) {
+    if (a.mask) return set_error(kErrInvalid, "analytic and dense masks are exclusive");
+    if (a.win[0] * a.win[1] * a.win[2] != a.N || a.nwin[0] < 1 || a.nwin[1] < 1 || a.nwin[2] < 1)
+      return set_error(kErrInvalid, "analytic mask geometry does not match N");
+    for (int i = 0; i < 3; ++i)
+      if (a.shift[i] < 0 || a.shift[i] >= a.win[i])
+        return set_error(kErrInvalid, "analytic mask shift must satisfy 0 <= shift < window");
+  }
 
   CUtensorMap tq, tk, tv;
   if (int e = make_qkv_map(&tq, a.q, a)) return e;
@@ -601,8 +805,23 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
 
   KParams kp{};
   kp.bias = static_cast<const uint16_t*>(a.bias);
+  kp.table = a.table;
+  kp.index = reinterpret_cast<const long long*>(a.index);
+  kp.index_stride = int(a.index_stride);
+  kp.bias_from_table = a.bias_from_table ? 1 : 0;
+  kp.table_f32 = a.table_f32 ? 1 : 0;
   kp.mask = static_cast<const uint16_t*>(a.mask);
   kp.boundary = a.boundary;
+  kp.mask_windows = a.mask ? int(a.mask_windows) : 1;
+  kp.nwd = int(a.nwin[0]);
+  kp.nwh = int(a.nwin[1]);
+  kp.nww = int(a.nwin[2]);
+  kp.wsd = int(a.win[0]);
+  kp.wsh = int(a.win[1]);
+  kp.wsw = int(a.win[2]);
+  kp.ssd = int(a.shift[0]);
+  kp.ssh = int(a.shift[1]);
+  kp.ssw = int(a.shift[2]);
   kp.out = static_cast<uint16_t*>(a.out);
   kp.out_sb = a.out_stride_b;
   kp.out_sh = a.out_stride_h;
@@ -612,8 +831,12 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.N = int(a.N);
   kp.MT = int((a.N + kBM - 1) / kBM);
   kp.P = kp.H * kp.MT;
-  kp.mask_windows = a.mask ? int(a.mask_windows) : 1;
   kp.scale = a.scale;
+  if (!a.analytic) {
+    // keep the analytic-mask geometry harmless when unused
+    kp.nwd = kp.nwh = kp.nww = 1;
+    kp.wsd = kp.wsh = kp.wsw = 1;
+  }
 
   const int n32 = int((a.N + 31) / 32) * 32;
   if (n32 <= 64) return dispatch_npad<64>(a, tq, tk, tv, kp, stream);

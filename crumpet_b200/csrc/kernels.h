@@ -42,10 +42,19 @@ struct AttnArgs {
   int64_t qkv_stride_b, qkv_stride_h, qkv_stride_n;
   void* out;
   int64_t out_stride_b, out_stride_h, out_stride_n;
-  const void* bias;        // [H, N, N] contiguous, same dtype as q
+  const void* bias;        // [H, N, N] contiguous, same dtype as q (when !bias_from_table)
+  bool bias_from_table;    // gather bias[h,i,j] = table[index[i*index_stride + j], h]
+  const void* table;       // [T, H] fp32 (table_f32) or the element type
+  bool table_f32;
+  const int64_t* index;    // [>=N, index_stride] relative position index, sliced [:N, :N]
+  int64_t index_stride;
   const void* mask;        // [mask_windows, N, N] contiguous or nullptr
   int64_t mask_windows;    // window b uses mask[b % mask_windows]
   const uint8_t* boundary; // [B] or nullptr (nullptr + mask => every window masked)
+  bool analytic;           // shifted-window mask computed on chip from the geometry below
+  int64_t nwin[3];         // windows per axis of one batch entry (window b is b % prod)
+  int64_t win[3];          // window size (win[0]*win[1]*win[2] == N)
+  int64_t shift[3];        // cyclic shift; all zero means no mask
   int64_t B, H, N, head_dim;
   float scale;
   int dtype;               // kF16 or kBF16

@@ -163,6 +163,35 @@ void fused_swin_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor
                                         cur_stream(q)));
 }
 
+void swin_window_attention_qkv(at::Tensor& out, const at::Tensor& qkv, const at::Tensor& table,
+                               const at::Tensor& index, at::IntArrayRef num_windows,
+                               at::IntArrayRef window_size, at::IntArrayRef shift_size,
+                               double scale) {
+  check_cuda_contig(out, "out");
+  check_cuda_contig(qkv, "qkv");
+  check_cuda_contig(table, "relative_position_bias_table");
+  check_cuda_contig(index, "relative_position_index");
+  TORCH_CHECK(qkv.dim() == 5 && qkv.size(2) == 3, "qkv must have shape [B, N, 3, H, head_dim]");
+  const int64_t B = qkv.size(0), N = qkv.size(1), H = qkv.size(3), Dh = qkv.size(4);
+  TORCH_CHECK(out.dim() == 3 && out.size(0) == B && out.size(1) == N && out.size(2) == H * Dh,
+              "out must have shape [B, N, H * head_dim]");
+  TORCH_CHECK(out.scalar_type() == qkv.scalar_type(), "out and qkv dtypes differ");
+  TORCH_CHECK(table.dim() == 2 && table.size(1) == H, "relative_position_bias_table must be [T, H]");
+  TORCH_CHECK(table.scalar_type() == at::kFloat || table.scalar_type() == qkv.scalar_type(),
+              "relative_position_bias_table must be float32 or the dtype of qkv");
+  TORCH_CHECK(index.scalar_type() == at::kLong && index.dim() == 2 && index.size(0) >= N &&
+                  index.size(1) >= N,
+              "relative_position_index must be int64 [>=N, >=N]");
+  TORCH_CHECK(num_windows.size() == 3 && window_size.size() == 3 && shift_size.size() == 3,
+              "num_windows, window_size and shift_size take three values");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  check_rc(crumpet_swin_window_attention_qkv(
+      out.data_ptr(), qkv.data_ptr(), table.data_ptr(), table.scalar_type() == at::kFloat ? 1 : 0,
+      index.data_ptr<int64_t>(), index.size(1), num_windows[0], num_windows[1], num_windows[2],
+      window_size[0], window_size[1], window_size[2], shift_size[0], shift_size[1],
+      shift_size[2], dtype_code(qkv), B, H, N, Dh, static_cast<float>(scale), cur_stream(qkv)));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(crumpet_ops, ops) {
@@ -190,6 +219,10 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "fused_swin_attention(Tensor! out, Tensor q, Tensor k, Tensor v, Tensor rel_bias, "
       "Tensor? mask, Tensor? boundary, float scale) -> ()",
       kTags);
+  ops.def(
+      "swin_window_attention_qkv(Tensor! out, Tensor qkv, Tensor table, Tensor index, "
+      "int[] num_windows, int[] window_size, int[] shift_size, float scale) -> ()",
+      kTags);
 }
 
 TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
@@ -199,4 +232,5 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("fused_unshift_unpartition_3d", &fused_unshift_unpartition_3d);
   ops.impl("fused_unshift_unpartition_3d_backward", &fused_unshift_unpartition_3d_backward);
   ops.impl("fused_swin_attention", &fused_swin_attention);
+  ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
 }

@@ -84,4 +84,60 @@ def fused_swin_attention(
     return out
 
 
-__all__ = ["fused_swin_attention"]
+def swin_window_attention_qkv(
+    qkv: torch.Tensor,
+    relative_position_bias_table: torch.Tensor,
+    relative_position_index: torch.Tensor,
+    num_windows=(1, 1, 1),
+    window_size=None,
+    shift_size=(0, 0, 0),
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Window attention straight from the packed qkv Linear output.
+
+    ``qkv``: ``[B, N, 3, H, head_dim]`` (the qkv Linear output viewed per head);
+    returns ``[B, N, H * head_dim]`` ready for the proj Linear.  The bias is
+    gathered in the kernel from ``relative_position_bias_table[index[:N, :N]]``
+    and, when ``shift_size`` is non-zero, the shifted-window mask of a grid of
+    ``num_windows`` windows of ``window_size`` is computed on chip (window ``b``
+    is ``b % prod(num_windows)``).  This is the whole body of MONAI's
+    ``WindowAttention.forward`` between its two Linears
+    (torch-ext/crumpet/monai_patch.py:152-196 does the same with eager glue).
+    """
+    if not qkv.is_cuda:
+        raise RuntimeError("swin_window_attention_qkv runs on CUDA tensors only")
+    if qkv.ndim != 5 or qkv.shape[2] != 3:
+        raise ValueError("qkv must have shape [B, N, 3, H, head_dim]")
+    B, N, _, H, D = (int(s) for s in qkv.shape)
+    if D != 16:
+        raise ValueError("swin_window_attention_qkv requires head_dim 16")
+    if qkv.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("swin_window_attention_qkv supports torch.float16 and torch.bfloat16")
+    if window_size is None:
+        window_size = (N, 1, 1)
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    table = relative_position_bias_table
+    if table.dtype not in (torch.float32, qkv.dtype):
+        table = table.float()
+    out = torch.empty((B, N, H * D), dtype=qkv.dtype, device=qkv.device)
+    ops = _native.require()
+    token = None
+    if _prof._active:
+        esize = qkv.element_size()
+        token = _prof.attention_begin({
+            # algorithmic bytes: q, k, v, out (the bias is gathered on chip and
+            # the mask computed on chip)
+            "bytes": 4 * B * H * N * D * esize,
+            "flops": 4 * B * H * N * N * D,
+            "exps": B * H * N * N,
+        })
+    ops.swin_window_attention_qkv(out, qkv.contiguous(), table.contiguous(),
+                                  relative_position_index.contiguous(), list(num_windows),
+                                  list(window_size), list(shift_size), float(scale))
+    _prof.count("swin_window_attention_qkv")
+    _prof.attention_end(token)
+    return out
+
+
+__all__ = ["fused_swin_attention", "swin_window_attention_qkv"]

@@ -22,11 +22,15 @@ when the target module lacks one of the patched names.
 ``monai.networks.nets.swin_unetr`` by default (as in the reference), or
 ``crumpet_b200.swin_unetr``, the bundled MONAI-architecture network.
 
-Differences from the reference glue, all of them removals of work: the mask
-is never tiled with ``repeat`` (the kernel indexes it modulo the number of
-windows), and the per-window boundary flags are derived once per mask from
-the window geometry instead of an ``abs().amax()`` scan of the whole mask on
-every attention call.
+Differences from the reference glue, all of them removals of work: for masks
+built by the patched ``BasicLayer`` (which records their window geometry on
+the tensor), attention runs ``swin_window_attention_qkv`` -- q/k/v read in
+place from the qkv Linear output, bias gathered and shifted-window mask
+computed inside the kernel, output written proj-ready -- so the q/k/v copies,
+bias gather, mask ``repeat``, per-call ``abs().amax()`` mask scan and output
+transpose disappear.  Masks without recorded geometry take the dense-mask
+kernel, indexed modulo the number of windows and with boundary flags derived
+once per mask.
 """
 
 from __future__ import annotations
@@ -39,10 +43,11 @@ import torch
 import torch.nn.functional as F
 
 from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpartition_3d
-from .fused_attention import fused_swin_attention
+from .fused_attention import fused_swin_attention, swin_window_attention_qkv
 
 _STATE: dict[str, Any] = {}
 _BOUNDARY_ATTR = "_crumpet_boundary"
+_GEOMETRY_ATTR = "_crumpet_geometry"
 
 
 def _fused_attn_enabled() -> bool:
@@ -119,6 +124,16 @@ def _patched_window_attention_forward(original):
         qkv = self.qkv(x)
         if head_dim != 16 or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
             return original(self, x, mask)
+        geometry = None if mask is None else getattr(mask, _GEOMETRY_ATTR, None)
+        if mask is None or geometry is not None:
+            # Fast path: packed qkv in, proj-ready [b, n, c] out, bias gathered and
+            # shifted-window mask computed inside the kernel.
+            num_windows, window_size, shift_size = geometry or ((1, 1, 1), (n, 1, 1), (0, 0, 0))
+            out = swin_window_attention_qkv(
+                qkv.view(b, n, 3, heads, head_dim), self.relative_position_bias_table,
+                self.relative_position_index, num_windows, window_size, shift_size, self.scale)
+            return self.proj_drop(self.proj(out))
+        # A mask from elsewhere: dense mask path.
         qkv = qkv.reshape(b, n, 3, heads, head_dim).permute(2, 0, 3, 1, 4)
         q, k, v = qkv[0], qkv[1], qkv[2]
         index = self.relative_position_index[:n, :n].reshape(-1)
@@ -153,6 +168,8 @@ def _patched_basic_layer_forward(original, swin):
         attn_mask = compute_attn_mask_3d(*dims, window_size, shift_size, x.dtype, x.device)
         if getattr(attn_mask, _BOUNDARY_ATTR, None) is None:
             setattr(attn_mask, _BOUNDARY_ATTR, boundary_flags(dims, window_size, shift_size, x.device))
+            num_windows = tuple(d // w for d, w in zip(dims, window_size))
+            setattr(attn_mask, _GEOMETRY_ATTR, (num_windows, window_size, shift_size))
         for blk in self.blocks:
             x = blk(x, attn_mask)
         x = x.view(b, d, h, w, -1)

@@ -127,6 +127,32 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
                                  int64_t N, int64_t head_dim, float scale, void* stream);
 
 /*
+ * Fused window attention straight from the packed qkv Linear output, with the
+ * relative-position bias gathered in-kernel and the shifted-window mask
+ * computed on chip -- the whole body of MONAI's WindowAttention.forward
+ * between its qkv and proj Linears.
+ *   qkv   [B, N, 3, H, head_dim]   (q | k | v along dim 2; B = batch * nW)
+ *   out   [B, N, H * head_dim]     (heads interleaved per token: ready for proj)
+ *   bias_table [T, H]              fp32 when table_f32 != 0, else dtype
+ *   rel_index  [>=N, index_stride] int64; bias[h,i,j] = table[rel_index[i,j], h]
+ *              for i, j < N (MONAI slices the configured window's index [:N, :N])
+ *   nw_*  windows per axis of one batch entry (window b is b % (nw_d*nw_h*nw_w))
+ *   ws_*  window size (ws_d*ws_h*ws_w == N); ss_* cyclic shift (all 0: no mask)
+ * The mask equals crumpet_compute_attn_mask_3d's on the padded grid; masked
+ * scores are dropped exactly (e^-100 and e^-inf are both 0 in fp32).
+ * dtype F16 or BF16, head_dim == 16, N <= 384.
+ * Replaces the eager glue of torch-ext/crumpet/monai_patch.py:152-196 (q/k/v
+ * split and .contiguous() copies, bias gather and permute, mask repeat, the
+ * per-call mask abs().amax() scan, the output transpose) plus
+ * fused_swin_attention.
+ */
+CRUMPET_API int crumpet_swin_window_attention_qkv(
+    void* out, const void* qkv, const void* bias_table, int table_f32, const int64_t* rel_index,
+    int64_t index_stride, int64_t nw_d, int64_t nw_h, int64_t nw_w, int64_t ws_d, int64_t ws_h,
+    int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype, int64_t B, int64_t H,
+    int64_t N, int64_t head_dim, float scale, void* stream);
+
+/*
  * Device error word: non-zero once a kernel of this library gave up on a
  * bounded wait (it then drained its work, freed its tensor memory and
  * returned without completing its output).  Reading it synchronises with the

@@ -152,3 +152,16 @@ def test_reference_functions_round_trip_on_cpu():
     w = crumpet.unfused_shift_partition_3d_reference(x, (4, 4, 4), (2, 2, 2))
     back = crumpet.unfused_unshift_unpartition_3d_reference(w, 2, 8, 8, 8, 3, (4, 4, 4), (2, 2, 2))
     assert torch.equal(back, x)
+
+
+def test_packed_attention_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    # analytic geometry that does not multiply out to N
+    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, null, 343, 2, 2, 2, 7, 7, 6, 3, 3,
+                                               3, 1, 8, 3, 343, 16, 0.25, null)
+    assert rc == 1 and _ops.last_error()
+    # null pointers
+    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, null, 343, 2, 2, 2, 7, 7, 7, 3, 3,
+                                               3, 1, 8, 3, 343, 16, 0.25, null)
+    assert rc == 1

@@ -1,0 +1,97 @@
+"""swin_window_attention_qkv (packed qkv in, proj-ready out, in-kernel bias gather,
+on-chip shifted-window mask) against the float64 oracle, through the torch op and
+the C ABI."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from crumpet_b200 import _ops
+from crumpet_b200.fused_attention import swin_window_attention_qkv
+from helpers import DTYPE_CODE, ptr, stream_ptr
+from oracle import attention as OA
+from oracle import mechanics as OM
+
+pytestmark = pytest.mark.gpu
+
+# (name, grid dims (padded), window, shift, heads, batch repeats, configured window, dtype)
+CASES = [
+    ("shift_n343_h3", (14, 14, 14), (7, 7, 7), (3, 3, 3), 3, 2, (7, 7, 7), "float16"),
+    ("shift_n343_h6_28", (28, 28, 28), (7, 7, 7), (3, 3, 3), 6, 1, (7, 7, 7), "float16"),
+    ("noshift_n343_h3", (14, 14, 14), (7, 7, 7), (0, 0, 0), 3, 1, (7, 7, 7), "float16"),
+    ("quirk_n216_h24", (6, 6, 6), (6, 6, 6), (0, 0, 0), 24, 3, (7, 7, 7), "float16"),
+    ("mixed_shift", (14, 21, 7), (7, 7, 7), (3, 0, 2), 3, 1, (7, 7, 7), "float16"),
+    ("shift_n64_h2", (8, 8, 8), (4, 4, 4), (2, 2, 2), 2, 2, (4, 4, 4), "float16"),
+    ("shift_n343_bf16", (14, 14, 14), (7, 7, 7), (3, 3, 3), 3, 1, (7, 7, 7), "bfloat16"),
+]
+
+
+def make_case(case, dev, table_dtype=torch.float32):
+    name, dims, ws, ss, H, reps, cfg, dtype = case
+    g = torch.Generator().manual_seed(abs(hash(name)) % (2**31))
+    nw = tuple(d // w for d, w in zip(dims, ws))
+    nwin = nw[0] * nw[1] * nw[2]
+    B, N = nwin * reps, ws[0] * ws[1] * ws[2]
+    dt = getattr(torch, dtype)
+    qkv = torch.randn((B, N, 3, H, 16), generator=g).to(dt)
+    ncfg = cfg[0] * cfg[1] * cfg[2]
+    table = (torch.randn(((2 * cfg[0] - 1) * (2 * cfg[1] - 1) * (2 * cfg[2] - 1), H), generator=g)
+             * 0.5).to(table_dtype)
+    index = torch.from_numpy(OA.relative_position_index(cfg)).long()
+    assert index.shape == (ncfg, ncfg)
+    # oracle inputs: bias rounded to the activation dtype, as the reference does
+    bias = torch.from_numpy(OA.gather_bias(table.float().numpy(), index.numpy(), N)).to(dt)
+    mask = None
+    if any(ss):
+        mask = OM.attn_mask(*dims, ws, ss, np.float32)
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
+    want = OA.window_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                               bias.float().numpy(), mask)
+    want = np.transpose(want, (0, 2, 1, 3)).reshape(B, N, H * 16)
+    return (qkv.to(dev), table.to(dev), index.to(dev), nw, ws, ss), want
+
+
+def tol(dtype):
+    return 1.6e-2 if dtype == torch.bfloat16 else 2e-3
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_packed_attention_matches_oracle(case, cuda_device):
+    (qkv, table, index, nw, ws, ss), want = make_case(case, cuda_device)
+    out = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
+    torch.cuda.synchronize()
+    err = np.abs(out.float().cpu().numpy() - want).max()
+    assert err <= tol(qkv.dtype), err
+    assert _ops.capi().crumpet_device_status(1) == 0
+
+
+def test_packed_attention_capi_fp16_table(cuda_device):
+    case = CASES[0]
+    (qkv, table, index, nw, ws, ss), want = make_case(case, cuda_device, torch.float16)
+    B, N, _, H, D = qkv.shape
+    out = torch.empty((B, N, H * D), dtype=qkv.dtype, device=cuda_device)
+    rc = _ops.capi().crumpet_swin_window_attention_qkv(
+        ptr(out), ptr(qkv), ptr(table), 0, ptr(index), index.shape[1], *nw, *ws, *ss,
+        DTYPE_CODE[qkv.dtype], B, H, N, D, 0.25, stream_ptr())
+    assert rc == 0, _ops.last_error()
+    torch.cuda.synchronize()
+    assert np.abs(out.float().cpu().numpy() - want).max() <= 2e-3
+
+
+def test_packed_matches_dense_kernel(cuda_device):
+    # the packed/analytic kernel and the dense-mask kernel agree
+    import crumpet_b200 as crumpet
+
+    case = CASES[0]
+    (qkv, table, index, nw, ws, ss), _ = make_case(case, cuda_device)
+    B, N, _, H, D = qkv.shape
+    packed = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
+    bias = table[index[:N, :N].reshape(-1)].reshape(N, N, H).permute(2, 0, 1).contiguous().half()
+    mask = crumpet.compute_attn_mask_3d(14, 14, 14, ws, ss, torch.float16, cuda_device)
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).contiguous() for i in range(3))
+    dense = crumpet.fused_swin_attention(q, k, v, bias, mask, None, 0.25)
+    dense = dense.transpose(1, 2).reshape(B, N, H * D)
+    assert (packed.float() - dense.float()).abs().max().item() <= 2e-3
