@@ -211,6 +211,19 @@ def time_kernels(device, peaks) -> dict:
                                    "tflops": flops / ms / 1e9,
                                    "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
                                    "gexp_s": B * H * N * N / ms / 1e6}
+    # the patched-network path: packed qkv, in-kernel bias gather, on-chip mask
+    from crumpet_b200.fused_attention import swin_window_attention_qkv
+
+    qkv_packed = qkv.permute(1, 3, 0, 2, 4).contiguous()  # [B, N, 3, H, 16]
+    ms = timed(lambda: swin_window_attention_qkv(qkv_packed, table, index, (14, 14, 14), ws, ss,
+                                                 0.25), iters=10)
+    pbytes = 4 * B * H * N * 16 * 2
+    res["swin_window_attention_qkv"] = {"config": "2744x3x343x16 fp16 packed qkv, table bias, on-chip mask",
+                                        "ms": ms, "bytes": pbytes, "gbs": pbytes / ms / 1e6,
+                                        "frac_hbm": pbytes / ms / 1e6 / hbm,
+                                        "tflops": flops / ms / 1e9,
+                                        "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
+                                        "gexp_s": B * H * N * N / ms / 1e6}
     del flush
     return res
 

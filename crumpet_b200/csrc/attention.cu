@@ -60,13 +60,17 @@ using namespace sm100;
 constexpr int kHD = 16;       // head dimension
 constexpr int kBM = 128;      // query rows per tile (UMMA M)
 constexpr int kCH = 64;       // key chunk
-constexpr int kNumWG = 2;     // independent tile pipelines per CTA
-constexpr int kStages = 2;    // Q/K/V stages per WG
-constexpr int kThreads = (kNumWG * 2 + kNumWG * 4) * 32;  // 384
+constexpr int kNumWG = 3;      // independent tile pipelines (softmax warpgroups) per CTA
+constexpr int kStages = 4;     // Q/K/V stages, one ring shared by all WGs
+constexpr int kCtrlWarps = 4;  // warp 0: TMA producer; warps 1..kNumWG: MMA issuers
+static_assert(kNumWG + 1 <= kCtrlWarps, "one TMA warp and one MMA warp per WG");
+constexpr int kSmThreads = kNumWG * 4 * 32;            // softmax threads (one per TMEM lane)
+constexpr int kThreads = kCtrlWarps * 32 + kSmThreads;  // 512
 constexpr int kRowBytes = kHD * 2;
-constexpr int kBarsPerWG = 2 * kStages + 7;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemPerWG = 256;
+constexpr int kBarsPerWG = 7;
+constexpr uint32_t kTmemPerWG = 128;
+constexpr uint32_t kTmemCols = kTmemPerWG * kNumWG <= 256 ? 256u : 512u;  // power of two
+constexpr float kRescaleLog2 = 8.f;  // P = 2^(x - m_ref) stays <= 2^8
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int NPAD>
@@ -80,15 +84,15 @@ struct Cfg {
   static constexpr int KV_BYTES = NKB * 128 * kRowBytes;
   static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
   static constexpr int BIAS_BYTES = kBM * BSTRIDE * 2;
+  static constexpr int ONES_BYTES = NKB * 128 * kRowBytes;  // [keys][16] of 1.0
   static constexpr int PLANE_BYTES = 3 * NCH * 8;     // analytic-mask code planes
-  // TMEM columns of one WG: S chunk, P chunk, per-chunk O, per-chunk (m, l).
+  // TMEM columns of one WG: S chunk (64), P chunk (32 packed), O (16) + row sum (16).
   static constexpr int TM_S = 0;
   static constexpr int TM_P = kCH;
   static constexpr int TM_O = kCH + kCH / 2;
-  static constexpr int TM_STAT = TM_O + NCH * kHD;
-  static_assert(TM_STAT + 16 <= int(kTmemPerWG), "TMEM budget");
-  static constexpr int SMEM_BYTES = 1024 + kNumWG * kStages * STAGE_BYTES + BIAS_BYTES +
-                                    PLANE_BYTES + kNumWG * kBarsPerWG * 8 + 64;
+  static_assert(TM_O + 2 * kHD <= int(kTmemPerWG), "TMEM budget");
+  static constexpr int SMEM_BYTES = 1024 + kStages * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
+                                    PLANE_BYTES + (2 * kStages + kNumWG * kBarsPerWG) * 8 + 64;
 };
 
 enum MaskMode : int { kMaskNone = 0, kMaskDense = 1, kMaskAnalytic = 2 };
@@ -156,26 +160,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// Packed fp32 pair arithmetic (sm_100 f32x2).
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-
 template <bool BF16>
 __device__ __forceinline__ float2 unpack2(uint32_t w) {
   if constexpr (BF16) {
@@ -187,15 +171,42 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
 }
 
 template <bool BF16>
-__device__ __forceinline__ uint32_t add_pairs(uint32_t a, uint32_t b) {
+__device__ __forceinline__ float to_f32(uint16_t h) {
   if constexpr (BF16) {
-    __nv_bfloat162 r = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+    return __uint_as_float(uint32_t(h) << 16);
+  } else {
+    return __half2float(__ushort_as_half(h));
+  }
+}
+
+// m * log2(e) + b on a pair of 16-bit values (mask folded into the scaled bias).
+template <bool BF16>
+__device__ __forceinline__ uint32_t fma_pairs_log2e(uint32_t m, uint32_t b) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 l2e = __floats2bfloat162_rn(kLog2e, kLog2e);
+    __nv_bfloat162 r = __hfma2(*reinterpret_cast<const __nv_bfloat162*>(&m), l2e,
                                *reinterpret_cast<const __nv_bfloat162*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
   } else {
-    __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    const __half2 l2e = __floats2half2_rn(kLog2e, kLog2e);
+    __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&m), l2e, *reinterpret_cast<const __half2*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
   }
+}
+
+// 2^t for a pair, computed by the SFU in packed 16-bit form (two per op) and
+// returned packed, ready to be the P operand of the PV MMA.
+template <bool BF16>
+__device__ __forceinline__ uint32_t ex2_pair(float2 t) {
+  uint32_t r;
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(t.x, t.y);
+    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
+  } else {
+    __half2 v = __floats2half2_rn(t.x, t.y);
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
+  }
+  return r;
 }
 
 template <bool BF16>
@@ -216,12 +227,6 @@ __device__ __forceinline__ uint16_t f32_to_elem(float v) {
   } else {
     return __half_as_ushort(__float2half_rn(v));
   }
-}
-
-__device__ __forceinline__ void tmem_st2(uint32_t taddr, uint32_t a, uint32_t b) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(a),
-               "r"(b)
-               : "memory");
 }
 
 __device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) {
@@ -258,11 +263,12 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint16_t* bias_s = reinterpret_cast<uint16_t*>(smem + kNumWG * kStages * C::STAGE_BYTES);
-  uint64_t* planes = reinterpret_cast<uint64_t*>(smem + kNumWG * kStages * C::STAGE_BYTES +
+  uint16_t* ones_s = reinterpret_cast<uint16_t*>(smem + kStages * C::STAGE_BYTES);
+  uint16_t* bias_s = ones_s + C::ONES_BYTES / 2;
+  uint64_t* planes = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bias_s) +
                                                  C::BIAS_BYTES);
   uint64_t* bars = planes + 3 * C::NCH;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumWG * kBarsPerWG);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + kNumWG * kBarsPerWG);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -270,18 +276,19 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   const Sched sc = make_sched(p.P);
   if (sc.pair_count == 0) return;  // uniform for the CTA
 
-  // Barrier block of WG w: [load_full x kStages][load_empty x kStages]
-  //                        [s_full][s_empty][p_full][p_empty][o_full][o_empty][drain]
-  auto bar = [&](int w, int i) { return bars + w * kBarsPerWG + i; };
-  constexpr int kLF = 0, kLE = kStages, kSF = 2 * kStages, kSE = kSF + 1, kPF = kSF + 2,
-                kPE = kSF + 3, kOF = kSF + 4, kOE = kSF + 5, kDR = kSF + 6;
+  // Barriers: the stage ring [load_full x kStages][load_empty x kStages], then per WG
+  //           [s_full][s_empty][p_full][p_empty][o_full][o_empty][drain]
+  uint64_t* load_full = bars;
+  uint64_t* load_empty = bars + kStages;
+  auto bar = [&](int w, int i) { return bars + 2 * kStages + w * kBarsPerWG + i; };
+  constexpr int kSF = 0, kSE = 1, kPF = 2, kPE = 3, kOF = 4, kOE = 5, kDR = 6;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(load_full + s, 1);
+      mbar_init(load_empty + s, 1);
+    }
     for (int w = 0; w < kNumWG; ++w) {
-      for (int s = 0; s < kStages; ++s) {
-        mbar_init(bar(w, kLF + s), 1);
-        mbar_init(bar(w, kLE + s), 1);
-      }
       mbar_init(bar(w, kSF), 1);
       mbar_init(bar(w, kSE), 4);
       mbar_init(bar(w, kPF), 4);
@@ -305,6 +312,14 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
       planes[a * C::NCH + c] = bits;
     }
   }
+  {
+    // Ones tile: the second 16 columns of the PV B operand, so the MMA also
+    // accumulates the row sums of P next to O.
+    const uint32_t one2 = BF16 ? 0x3F803F80u : 0x3C003C00u;
+    uint32_t* o32 = reinterpret_cast<uint32_t*>(ones_s);
+    for (int i = threadIdx.x; i < C::ONES_BYTES / 4; i += kThreads) o32[i] = one2;
+    fence_proxy_async_shared();
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -314,29 +329,28 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 2 * kNumWG) {
-    const int w = warp >> 1;
-    if ((warp & 1) == 0) {
+  if (warp < kCtrlWarps) {
+    if (warp == 0) {
       // ------------------------------------------------------------ TMA warp
+      // Tiles of the CTA in order k = 0, 1, ...; tile k uses ring stage k % kStages.
       if (lane == 0) {
         tma_prefetch_map(&tq);
         tma_prefetch_map(&tk);
         tma_prefetch_map(&tv);
-        uint32_t it = 0;
+        uint32_t k = 0;
         bool ok = true;
         for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
           const int pair = sc.pair_begin + pi * sc.pair_step;
           const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
-          for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok;
-               b += kNumWG * sc.win_step) {
-            const int st = int(it % kStages);
-            const uint32_t ph = (it / kStages) & 1u;
-            if (!mbar_wait(bar(w, kLE + st), ph ^ 1u, abort_flag)) {
+          for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k) {
+            const int st = int(k % kStages);
+            const uint32_t ph = (k / kStages) & 1u;
+            if (!mbar_wait(load_empty + st, ph ^ 1u, abort_flag)) {
               ok = false;
               break;
             }
-            uint8_t* sb = smem + (w * kStages + st) * C::STAGE_BYTES;
-            uint64_t* full = bar(w, kLF + st);
+            uint8_t* sb = smem + st * C::STAGE_BYTES;
+            uint64_t* full = load_full + st;
             mbar_arrive_expect_tx(full, C::STAGE_BYTES);
             tma_load_4d(sb, &tq, full, 0, mt * kBM, h, b);
 #pragma unroll
@@ -345,23 +359,24 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + kb * 128 * kRowBytes, &tv, full, 0,
                           kb * 128, h, b);
             }
-            ++it;
           }
         }
         // Drain: every stage's most recent load must have landed before exit.
         for (uint32_t s = 0; s < kStages; ++s) {
-          if (it > s) {
-            const uint32_t last = ((it - 1 - s) / kStages) * kStages + s;  // last use of stage s
-            drain_wait(bar(w, kLF + int(s)), (last / kStages) & 1u);
+          if (k > s) {
+            const uint32_t last = ((k - 1 - s) / kStages) * kStages + s;  // last use of stage s
+            drain_wait(load_full + int(s), (last / kStages) & 1u);
           }
         }
       }
-    } else {
+    } else if (warp <= kNumWG) {
       // ------------------------------------------------------------ MMA warp
+      const int w = warp - 1;
       if (lane == 0) {
         const uint32_t tS = tmem_base + w * kTmemPerWG + C::TM_S;
         const uint32_t tP = tmem_base + w * kTmemPerWG + C::TM_P;
         const uint32_t tO = tmem_base + w * kTmemPerWG + C::TM_O;
+        const uint32_t ones_addr = smem_u32(ones_s);
         uint32_t it = 0, n_se = 0, n_pf = 0, n_oe = 0;
         bool ok = true;
         auto issue_pv = [&](int c, uint32_t v_addr) -> bool {
@@ -374,27 +389,29 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             tc_fence_after();
           }
           const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
-          constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, BF16, true);
+          // B = [V | ones]: MN-major, the ones atom sits LBO bytes after V
+          constexpr uint32_t idesc_pv = idesc_f16(kBM, 2 * kHD, BF16, true);
+          const uint32_t lbo = ones_addr - v_addr;
           for (int k = 0; k < width / 16; ++k) {
             const uint64_t vdesc =
-                smem_desc(v_addr + uint32_t(c * kCH + k * 16) * kRowBytes, 0, 256, kLayoutSW32);
-            umma_ts(tO + uint32_t(c * kHD), tP + uint32_t(k * 8), vdesc, idesc_pv,
-                    k > 0 ? 1u : 0u);
+                smem_desc(v_addr + uint32_t(c * kCH + k * 16) * kRowBytes, lbo, 256, kLayoutSW32);
+            umma_ts(tO, tP + uint32_t(k * 8), vdesc, idesc_pv, (c > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(bar(w, kPE));
           return true;
         };
+        uint32_t k = 0;
         for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
-          for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok;
-               b += kNumWG * sc.win_step) {
-            const int st = int(it % kStages);
-            const uint32_t ph = (it / kStages) & 1u;
-            if (!mbar_wait(bar(w, kLF + st), ph, abort_flag)) {
+          for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k) {
+            if (int(k % kNumWG) != w) continue;
+            const int st = int(k % kStages);
+            const uint32_t ph = (k / kStages) & 1u;
+            if (!mbar_wait(load_full + st, ph, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t sb = smem_u32(smem + (w * kStages + st) * C::STAGE_BYTES);
+            const uint32_t sb = smem_u32(smem + st * C::STAGE_BYTES);
             const uint32_t q_addr = sb;
             const uint32_t k_addr = sb + C::Q_BYTES;
             const uint32_t v_addr = sb + C::Q_BYTES + C::KV_BYTES;
@@ -416,7 +433,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             if (ok && !issue_pv(C::NCH - 1, v_addr)) ok = false;
             if (!ok) break;
             umma_commit(bar(w, kOF));
-            umma_commit(bar(w, kLE + st));
+            umma_commit(load_empty + st);
             ++it;
           }
         }
@@ -427,47 +444,71 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     }
   } else {
     // -------------------------------------------------------- softmax warps
-    const int sw = warp - 2 * kNumWG;  // 0 .. 4*kNumWG-1
+    const int sw = warp - kCtrlWarps;  // 0 .. 4*kNumWG-1
     const int w = sw >> 2;
     const int quarter = warp & 3;      // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int tid_sm = threadIdx.x - 2 * kNumWG * 32;
+    const int tid_sm = threadIdx.x - kCtrlWarps * 32;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + w * kTmemPerWG + C::TM_S;
     const uint32_t tP = tmem_base + lane_off + w * kTmemPerWG + C::TM_P;
     const uint32_t tO = tmem_base + lane_off + w * kTmemPerWG + C::TM_O;
-    const uint32_t tStat = tmem_base + lane_off + w * kTmemPerWG + C::TM_STAT;
     const float kNegInf = __int_as_float(0xff800000);
-    const float2 scale2 = make_float2(p.scale, p.scale);
-    const float2 log2e2 = make_float2(kLog2e, kLog2e);
+    // scores are carried in the log2 domain: x = (q.k * scale + bias + mask) * log2(e)
+    const float2 c1 = make_float2(p.scale * kLog2e, p.scale * kLog2e);
     uint32_t n_sf = 0, n_pe = 0, n_of = 0;
+    uint32_t k_tile = 0;  // tile index within the CTA (shared numbering with the TMA/MMA warps)
     bool ok = true;
 
     for (int pi = 0; pi < sc.pair_count; ++pi) {
       const int pair = sc.pair_begin + pi * sc.pair_step;
       const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
-      // Relative-position bias rows of this (head, query tile): one load per CTA
-      // and pair, shared by every window and both WGs.
-      named_bar_sync(1, kNumWG * 128);
-      for (int e = tid_sm; e < kBM * NPAD; e += kNumWG * 128) {
-        const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
-        const int grow = mt * kBM + r;
-        uint16_t val = 0;
-        if (grow < p.N && col < p.N) {
-          if (p.bias_from_table) {
-            const long long idx = p.index[(long long)grow * p.index_stride + col];
-            if (p.table_f32) {
-              val = f32_to_elem<BF16>(static_cast<const float*>(p.table)[idx * p.H + h]);
+      // Relative-position bias rows of this (head, query tile), times log2(e):
+      // one load per CTA and pair, shared by every window and both WGs.  Eight
+      // independent loads per thread are kept in flight.
+      named_bar_sync(1, kSmThreads);
+      constexpr int kBatch = 8;
+      for (int e0 = tid_sm; e0 < kBM * NPAD; e0 += kBatch * kSmThreads) {
+        float vals[kBatch];
+        long long idx[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int e = e0 + u * kSmThreads;
+          const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
+          const int grow = mt * kBM + r;
+          const bool in = e < kBM * NPAD && grow < p.N && col < p.N;
+          idx[u] = -1;
+          vals[u] = 0.f;
+          if (in) {
+            if (p.bias_from_table) {
+              idx[u] = p.index[(long long)grow * p.index_stride + col];
             } else {
-              val = static_cast<const uint16_t*>(p.table)[idx * p.H + h];
+              vals[u] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
             }
-          } else {
-            val = p.bias[(size_t(h) * p.N + grow) * p.N + col];
           }
         }
-        bias_s[r * C::BSTRIDE + col] = val;
+        if (p.bias_from_table) {
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            if (idx[u] >= 0) {
+              vals[u] = p.table_f32
+                            ? static_cast<const float*>(p.table)[idx[u] * p.H + h]
+                            : to_f32<BF16>(static_cast<const uint16_t*>(p.table)[idx[u] * p.H + h]);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int e = e0 + u * kSmThreads;
+          if (e < kBM * NPAD) {
+            const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
+            // round to the element type first (as the reference's .to(dtype)), then scale
+            bias_s[r * C::BSTRIDE + col] =
+                f32_to_elem<BF16>(to_f32<BF16>(f32_to_elem<BF16>(vals[u])) * kLog2e);
+          }
+        }
       }
-      named_bar_sync(1, kNumWG * 128);
+      named_bar_sync(1, kSmThreads);
       if (!ok) continue;
 
       const int qrow = mt * kBM + row;
@@ -477,7 +518,8 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
       uint32_t code_i = 0;
       if constexpr (MASK == kMaskAnalytic) code_i = valid ? token_code(p, qrow) : 0u;
 
-      for (int b = sc.win_begin + w * sc.win_step; b < p.B && ok; b += kNumWG * sc.win_step) {
+      for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k_tile) {
+        if (int(k_tile % kNumWG) != w) continue;
         // ---- per-tile mask state
         bool use_dense = false;
         const uint16_t* mrow = nullptr;
@@ -495,6 +537,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
                (uint32_t(p.ssh != 0 && ih == p.nwh - 1) << 1) |
                (uint32_t(p.ssw != 0 && iw == p.nww - 1) << 2);
         }
+        // Reference maximum of this row (log2 domain).  P = 2^(x - m_ref) is kept
+        // <= 2^8: m_ref moves up only when a chunk exceeds it by more than 8, and
+        // then the O accumulator (with the row sums) is rescaled in TMEM first.
+        float m_ref = kNegInf;
 
         // One chunk of W keys (W = 64, or the ragged last chunk).
         auto chunk = [&](auto w_tag, auto tail_tag, int c) -> bool {
@@ -521,49 +567,57 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(w, kSE));
 
-          // bias pairs for the W keys (16-byte shared loads)
-          uint32_t bw[W / 2];
-#pragma unroll
-          for (int q = 0; q < W / 8; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(brow + c * kCH + 8 * q);
-            bw[4 * q + 0] = v.x;
-            bw[4 * q + 1] = v.y;
-            bw[4 * q + 2] = v.z;
-            bw[4 * q + 3] = v.w;
-          }
+          // x = s * scale * log2(e) + bias * log2(e) (+ mask * log2(e)), in groups of 16
+          // keys so the bias words (16-byte shared loads) and mask words stay few.
           const int valid_cols = p.N - c * kCH;
+          uint32_t odd = 0;
+          const uint32_t* wp = nullptr;
           if constexpr (MASK == kMaskDense) {
-            if (use_dense && valid) {
-              // mask row slice: aligned 32-bit words, re-paired when the row
-              // starts on an odd element, added to the bias pairs in half2.
-              const uintptr_t addr = reinterpret_cast<uintptr_t>(mrow + c * kCH);
-              const uint32_t odd = uint32_t(addr >> 1) & 1u;
-              const uint32_t* wp = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
-              uint32_t mw[W / 2 + 1];
-#pragma unroll
-              for (int k = 0; k <= W / 2; ++k) {
-                // word k holds elements 2k - odd and 2k - odd + 1 of the slice
-                // (only the last chunk can run past the row end)
-                if constexpr (kTail) {
-                  mw[k] = (2 * k - int(odd) < valid_cols) ? ldg_u32(wp + k) : 0u;
-                } else {
-                  mw[k] = ldg_u32(wp + k);
-                }
-              }
-              const uint32_t sel = odd ? 0x5432u : 0x3210u;
-#pragma unroll
-              for (int k = 0; k < W / 2; ++k) {
-                bw[k] = add_pairs<BF16>(bw[k], __byte_perm(mw[k], mw[k + 1], sel));
-              }
-            }
+            // mask row slice: aligned 32-bit words, re-paired when the row starts on
+            // an odd element (word k holds elements 2k - odd and 2k - odd + 1)
+            const uintptr_t addr = reinterpret_cast<uintptr_t>(mrow + c * kCH);
+            odd = uint32_t(addr >> 1) & 1u;
+            wp = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
           }
+          const bool dense_now = (MASK == kMaskDense) && use_dense && valid;
+          const uint32_t sel = odd ? 0x5432u : 0x3210u;
           float x[W];
 #pragma unroll
-          for (int k = 0; k < W / 2; ++k) {
-            const float2 r = ffma2(make_float2(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])),
-                                   scale2, unpack2<BF16>(bw[k]));
-            x[2 * k] = r.x;
-            x[2 * k + 1] = r.y;
+          for (int g = 0; g < W / 16; ++g) {
+            uint32_t bw[8];
+            {
+              const uint4 v0 = *reinterpret_cast<const uint4*>(brow + c * kCH + 16 * g);
+              const uint4 v1 = *reinterpret_cast<const uint4*>(brow + c * kCH + 16 * g + 8);
+              bw[0] = v0.x; bw[1] = v0.y; bw[2] = v0.z; bw[3] = v0.w;
+              bw[4] = v1.x; bw[5] = v1.y; bw[6] = v1.z; bw[7] = v1.w;
+            }
+            if constexpr (MASK == kMaskDense) {
+              if (dense_now) {
+                uint32_t mw[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) {
+                  const int kk = 8 * g + k;
+                  // only the last chunk can run past the row end
+                  if constexpr (kTail) {
+                    mw[k] = (2 * kk - int(odd) < valid_cols) ? ldg_u32(wp + kk) : 0u;
+                  } else {
+                    mw[k] = ldg_u32(wp + kk);
+                  }
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  bw[k] = fma_pairs_log2e<BF16>(__byte_perm(mw[k], mw[k + 1], sel), bw[k]);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int j = 16 * g + 2 * k;
+              const float2 r = __ffma2_rn(
+                  make_float2(__uint_as_float(s[j]), __uint_as_float(s[j + 1])), c1,
+                  unpack2<BF16>(bw[k]));
+              x[j] = r.x;
+              x[j + 1] = r.y;
+            }
           }
           if constexpr (MASK == kMaskAnalytic) {
             if (am != 0) {
@@ -586,32 +640,38 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               if (j >= valid_cols) x[j] = kNegInf;
             }
           }
-          float m = kNegInf;
+          float mc = kNegInf;
 #pragma unroll
-          for (int j = 0; j < W; j += 2) m = max3(m, x[j], x[j + 1]);
-          const float moff = (m == kNegInf) ? 0.f : m * kLog2e;
-          const float2 nmoff2 = make_float2(-moff, -moff);
-          float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                           make_float2(0.f, 0.f)};
-          uint32_t pk[W / 2];
-#pragma unroll
-          for (int k = 0; k < W / 2; ++k) {
-            const float2 t = ffma2(make_float2(x[2 * k], x[2 * k + 1]), log2e2, nmoff2);
-            const float2 e = make_float2(fast_ex2(t.x), fast_ex2(t.y));
-            acc[k & 3] = fadd2(acc[k & 3], e);
-            pk[k] = pack2<BF16>(e.x, e.y);
-          }
-          const float2 a01 = fadd2(acc[0], acc[1]);
-          const float2 a23 = fadd2(acc[2], acc[3]);
-          const float2 a = fadd2(a01, a23);
-          const float l = a.x + a.y;
-          // P buffer must be free: PV of the previous chunk has completed.
+          for (int j = 0; j < W; j += 2) mc = max3(mc, x[j], x[j + 1]);
+          const bool need = mc > m_ref + kRescaleLog2;  // m_ref = -inf: any finite mc
+          const float new_ref = need ? mc : m_ref;
+
+          // P buffer free <=> PV of the previous chunk has completed (also makes O
+          // safe to rescale).
           if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) return false;
           ++n_pe;
           tc_fence_after();
+          const bool rescale = need && (m_ref != kNegInf);  // O holds sums vs the old m_ref
+          if (c > 0 && __any_sync(0xffffffffu, rescale)) {
+            const float f = rescale ? fast_ex2(m_ref - new_ref) : 1.f;
+            uint32_t o[2 * kHD];
+            tmem_ld32(tO, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 2 * kHD; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st32(tO, o);
+          }
+          m_ref = new_ref;
+          const float mb = (m_ref == kNegInf) ? 0.f : m_ref;
+          const float2 nmb = make_float2(-mb, -mb);
+          uint32_t pk[W / 2];
+#pragma unroll
+          for (int k = 0; k < W / 2; ++k) {
+            const float2 t = __fadd2_rn(make_float2(x[2 * k], x[2 * k + 1]), nmb);
+            pk[k] = ex2_pair<BF16>(t);
+          }
           tmem_st16(tP, pk);
           if constexpr (W > 32) tmem_st16(tP + 16, pk + 16);
-          tmem_st2(tStat + 2 * c, __float_as_uint(m), __float_as_uint(l));
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
@@ -624,7 +684,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         if (ok) ok = chunk(std::integral_constant<int, C::LAST_W>{}, std::true_type{}, C::NCH - 1);
         if (!ok) break;
 
-        // ---- epilogue: combine the per-chunk partial outputs
+        // ---- epilogue: O / row sum
         if (!mbar_wait(bar(w, kOF), n_of & 1u, abort_flag)) {
           ok = false;
           break;
@@ -636,36 +696,18 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           if (lane == 0) mbar_arrive(bar(w, kOE));
           continue;
         }
-        uint32_t o[C::NCH][kHD];
-        uint32_t stat[16];
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c) tmem_ld16(tO + uint32_t(c * kHD), o[c]);
-        tmem_ld16(tStat, stat);
+        uint32_t o[2 * kHD];
+        tmem_ld32(tO, o);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(w, kOE));
-
-        float mmax = kNegInf;
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c) mmax = fmaxf(mmax, __uint_as_float(stat[2 * c]));
-        float acc[kHD];
-#pragma unroll
-        for (int d = 0; d < kHD; ++d) acc[d] = 0.f;
-        float L = 0.f;
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c) {
-          const float mc = __uint_as_float(stat[2 * c]);
-          const float wc = (mc == kNegInf) ? 0.f : fast_ex2((mc - mmax) * kLog2e);
-          L = fmaf(wc, __uint_as_float(stat[2 * c + 1]), L);
-#pragma unroll
-          for (int d = 0; d < kHD; ++d) acc[d] = fmaf(wc, __uint_as_float(o[c][d]), acc[d]);
-        }
         if (valid) {
-          const float inv = 1.f / L;
+          const float inv = 1.f / __uint_as_float(o[kHD]);
           uint32_t packed[kHD / 2];
 #pragma unroll
-          for (int d = 0; d < kHD; d += 2) packed[d / 2] = pack2<BF16>(acc[d] * inv, acc[d + 1] * inv);
+          for (int d = 0; d < kHD; d += 2)
+            packed[d / 2] = pack2<BF16>(__uint_as_float(o[d]) * inv, __uint_as_float(o[d + 1]) * inv);
           uint16_t* dst = p.out + b * p.out_sb + h * p.out_sh + qrow * p.out_sn;
           stg(reinterpret_cast<uint4*>(dst),
               make_uint4(packed[0], packed[1], packed[2], packed[3]));
