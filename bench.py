@@ -405,7 +405,7 @@ def main() -> None:
             exp_rate = attn["exps"] / (attn["avg_ms"] / 1e3)
             hbm_side = f_hbm >= f_tc
             roofline = {
-                "kernel": "window_attention_kernel (fused_swin_attention)",
+                "kernel": "window_attention_kernel (swin_window_attention_qkv: packed qkv, on-chip mask)",
                 "bound": "hbm" if hbm_side else "tensor",
                 "achieved": gbs if hbm_side else tflops,
                 "peak": peaks["hbm_gbs"] if hbm_side else peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
