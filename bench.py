@@ -224,6 +224,26 @@ def time_kernels(device, peaks) -> dict:
                                         "tflops": flops / ms / 1e9,
                                         "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
                                         "gexp_s": B * H * N * N / ms / 1e6}
+    # the fused block glue at the first stage of an 8-ROI sliding-window batch:
+    # [8,48,48,48,48] fp16 -> LayerNorm + pad to 49^3 + roll + partition -> fp16 windows,
+    # and windows -> unpartition + roll back + crop + residual add
+    del q, k, v, qkv, qkv_packed, mask, win, x
+    xs = torch.randn((8, 48, 48, 48, 48), device=device, generator=g).half()
+    gamma = torch.ones(48, device=device)
+    beta = torch.zeros(48, device=device)
+    wins = crumpet.norm_shift_partition_3d(xs, gamma, beta, 1e-5, ws, ss, torch.float16)
+    nb_in = xs.numel() * 2
+    nb = nb_in + wins.numel() * 2
+    ms = timed(lambda: crumpet.norm_shift_partition_3d(xs, gamma, beta, 1e-5, ws, ss, torch.float16))
+    res["norm_shift_partition_3d"] = {"config": "[8,48,48,48,48] fp16 -> [2744,343,48] fp16 (pad 49^3)",
+                                      "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
+                                      "frac_hbm": nb / ms / 1e6 / hbm}
+    nb = 3 * nb_in
+    ms = timed(lambda: crumpet.unshift_unpartition_crop_3d(wins, 8, 48, 48, 48, 48, ws, ss,
+                                                           residual=xs))
+    res["unshift_unpartition_crop_3d"] = {"config": "[2744,343,48] fp16 -> [8,48,48,48,48] + residual",
+                                          "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
+                                          "frac_hbm": nb / ms / 1e6 / hbm}
     del flush
     return res
 

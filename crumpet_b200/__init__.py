@@ -44,6 +44,9 @@ _OP_NAMES = (
     "fused_unshift_unpartition_3d",
     "fused_unshift_unpartition_3d_backward",
     "fused_swin_attention",
+    "swin_window_attention_qkv",
+    "norm_shift_partition_3d",
+    "unshift_unpartition_crop_3d",
 )
 
 
@@ -263,7 +266,8 @@ def fused_unshift_unpartition_3d(
         return out
 
 
-from .fused_attention import fused_swin_attention  # noqa: E402
+from .fused_attention import fused_swin_attention, swin_window_attention_qkv  # noqa: E402
+from .block_fusion import norm_shift_partition_3d, unshift_unpartition_crop_3d  # noqa: E402
 
 
 def patch_monai_swin_unetr(swin_module=None) -> bool:
@@ -290,6 +294,9 @@ __all__ = [
     "fused_shift_partition_3d",
     "fused_unshift_unpartition_3d",
     "fused_swin_attention",
+    "swin_window_attention_qkv",
+    "norm_shift_partition_3d",
+    "unshift_unpartition_crop_3d",
     "patch_monai_swin_unetr",
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",

@@ -68,6 +68,11 @@ def capi() -> ctypes.CDLL:
         lib.crumpet_swin_window_attention_qkv.argtypes = (
             [vp, vp, vp, i32, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
         lib.crumpet_swin_window_attention_qkv.restype = i32
+        lib.crumpet_norm_shift_partition_3d.argtypes = (
+            [vp, i32, vp, i32, vp, vp, ctypes.c_float] + [i64] * 11 + [vp])
+        lib.crumpet_norm_shift_partition_3d.restype = i32
+        lib.crumpet_unshift_unpartition_crop_3d.argtypes = [vp, vp, vp, i32] + [i64] * 11 + [vp]
+        lib.crumpet_unshift_unpartition_crop_3d.restype = i32
         lib.crumpet_last_error.argtypes = []
         lib.crumpet_last_error.restype = ctypes.c_char_p
         lib.crumpet_abi_version.argtypes = []

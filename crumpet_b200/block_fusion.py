@@ -1,0 +1,162 @@
+"""Fused memory passes around a Swin block's window attention.
+
+The reference's patched ``forward_part1`` (torch-ext/crumpet/monai_patch.py:72-114)
+runs norm1, ``F.pad``, the roll + partition op, (autocast's fp16 cast for the
+qkv Linear), the attention, the unpartition op and the crop as separate passes,
+and MONAI's block adds the residual in one more.  Two ops replace the passes
+on either side of the attention:
+
+* :func:`norm_shift_partition_3d` -- LayerNorm + zero pad to a window multiple
+  + roll by ``-shift`` + window partition, written in the dtype the qkv Linear
+  consumes;
+* :func:`unshift_unpartition_crop_3d` -- window reverse on the padded grid +
+  roll by ``+shift`` + crop, optionally adding the block's residual.
+
+Both are inference ops (no backward): they raise when autograd would need a
+gradient through them.  The MONAI patch uses them only outside autograd.
+"""
+
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from . import _ops as _native
+from . import profiling as _prof
+
+
+def _triple(name: str, value: Sequence[int]) -> tuple[int, int, int]:
+    if len(value) != 3:
+        raise ValueError(f"{name} must contain exactly three values")
+    return tuple(int(v) for v in value)  # type: ignore[return-value]
+
+
+def _check_window(window_size, shift_size) -> None:
+    if any(v <= 0 for v in window_size):
+        raise ValueError("window_size values must be positive")
+    for axis, (shift, window) in enumerate(zip(shift_size, window_size)):
+        if shift < 0 or shift >= window:
+            raise ValueError(f"shift_size[{axis}] must satisfy 0 <= shift < window_size[{axis}]")
+
+
+def _check_dtype(dtype: torch.dtype) -> None:
+    if dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise TypeError("CRUMPET supports torch.float32, torch.float16 and torch.bfloat16")
+
+
+def padded_geometry(D: int, H: int, W: int, window_size) -> tuple[tuple[int, int, int], int, int]:
+    """(padded dims, number of windows, window volume) for a window-multiple padding."""
+    dims = tuple(-(-d // w) * w for d, w in zip((D, H, W), window_size))
+    num_windows = (dims[0] // window_size[0]) * (dims[1] // window_size[1]) * (dims[2] // window_size[2])
+    volume = window_size[0] * window_size[1] * window_size[2]
+    return dims, num_windows, volume  # type: ignore[return-value]
+
+
+def _aligned(t: torch.Tensor, nbytes: int) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % nbytes == 0 else t.clone()
+
+
+def norm_shift_partition_3d(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor,
+    eps: float,
+    window_size: Sequence[int],
+    shift_size: Sequence[int],
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """``partition(roll(pad(layer_norm(x)), -shift))`` in one pass.
+
+    ``x`` is ``[B, D, H, W, C]`` with any D/H/W; the volume is zero-padded at
+    the far end of each axis up to a multiple of the window (padding after the
+    norm, so padded tokens are exact zeros) and the result is
+    ``[B * num_windows, volume, C]`` in ``out_dtype`` (default ``x.dtype``).
+    The norm is computed in fp32 with a biased variance, as ``nn.LayerNorm``;
+    C must be a multiple of 8 and at most 384.
+    """
+    if x.ndim != 5:
+        raise ValueError("x must have shape [B, D, H, W, C]")
+    window_size = _triple("window_size", window_size)
+    shift_size = _triple("shift_size", shift_size)
+    _check_window(window_size, shift_size)
+    _check_dtype(x.dtype)
+    out_dtype = x.dtype if out_dtype is None else out_dtype
+    _check_dtype(out_dtype)
+    B, D, H, W, C = (int(v) for v in x.shape)
+    if C % 8 or C > 384 or C == 0:
+        raise ValueError("norm_shift_partition_3d needs C a multiple of 8 and at most 384")
+    if tuple(weight.shape) != (C,) or tuple(bias.shape) != (C,):
+        raise ValueError("weight and bias must have shape [C]")
+    _, num_windows, volume = padded_geometry(D, H, W, window_size)
+    shape = (B * num_windows, volume, C)
+    if x.device.type == "meta":
+        return torch.empty(shape, dtype=out_dtype, device=x.device)
+    if x.device.type != "cuda":
+        raise RuntimeError("crumpet_b200 runs norm_shift_partition_3d on CUDA devices only "
+                           f"(got {x.device})")
+    if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad or bias.requires_grad):
+        raise RuntimeError("norm_shift_partition_3d has no backward; call it under torch.no_grad()")
+    out = torch.empty(shape, dtype=out_dtype, device=x.device)
+    w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
+    b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
+    _native.require().norm_shift_partition_3d(out, _aligned(x, 16), w, b, float(eps),
+                                              *window_size, *shift_size)
+    _prof.count("norm_shift_partition_3d")
+    return out
+
+
+def unshift_unpartition_crop_3d(
+    windows: torch.Tensor,
+    B: int,
+    D: int,
+    H: int,
+    W: int,
+    C: int,
+    window_size: Sequence[int],
+    shift_size: Sequence[int],
+    residual: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``roll(unpartition(windows), +shift)[:, :D, :H, :W]`` (``+ residual``) in one pass.
+
+    ``windows`` is ``[B * num_windows, volume, C]`` on the grid padded to window
+    multiples; the result is ``[B, D, H, W, C]``.  ``residual``, when given,
+    has that shape and the dtype of ``windows`` and is added in fp32 with one
+    rounding (torch's elementwise add).  Rows of C elements must be a multiple
+    of 4 bytes.
+    """
+    if windows.ndim != 3:
+        raise ValueError("windows must have shape [B * num_windows, window_volume, C]")
+    window_size = _triple("window_size", window_size)
+    shift_size = _triple("shift_size", shift_size)
+    _check_window(window_size, shift_size)
+    _check_dtype(windows.dtype)
+    B, D, H, W, C = int(B), int(D), int(H), int(W), int(C)
+    if min(D, H, W) <= 0 or B < 0 or C < 0:
+        raise ValueError("D, H and W must be positive")
+    _, num_windows, volume = padded_geometry(D, H, W, window_size)
+    expected = (B * num_windows, volume, C)
+    if tuple(int(v) for v in windows.shape) != expected:
+        raise ValueError(f"windows must have shape {expected}")
+    if (C * windows.element_size()) % 4:
+        raise ValueError("unshift_unpartition_crop_3d needs rows of C elements to be a multiple of 4 bytes")
+    if residual is not None:
+        if tuple(residual.shape) != (B, D, H, W, C):
+            raise ValueError(f"residual must have shape {(B, D, H, W, C)}")
+        if residual.dtype != windows.dtype:
+            raise TypeError("residual must have the dtype of windows")
+    if windows.device.type == "meta":
+        return torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
+    if windows.device.type != "cuda":
+        raise RuntimeError("crumpet_b200 runs unshift_unpartition_crop_3d on CUDA devices only "
+                           f"(got {windows.device})")
+    if torch.is_grad_enabled() and (windows.requires_grad or
+                                    (residual is not None and residual.requires_grad)):
+        raise RuntimeError("unshift_unpartition_crop_3d has no backward; call it under torch.no_grad()")
+    out = torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
+    res = None if residual is None else _aligned(residual, 16)
+    _native.require().unshift_unpartition_crop_3d(out, _aligned(windows, 16), res, B, D, H, W, C,
+                                                  *window_size, *shift_size)
+    _prof.count("unshift_unpartition_crop_3d")
+    return out

@@ -198,6 +198,28 @@ int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bi
   return launch_window_attention(a, static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_norm_shift_partition_3d(void* output, int out_dtype, const void* x, int in_dtype,
+                                    const float* weight, const float* bias, float eps, int64_t B,
+                                    int64_t D, int64_t H, int64_t W, int64_t C, int64_t ws_d,
+                                    int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h,
+                                    int64_t ss_w, void* stream) {
+  if (int e = check_dtype(out_dtype)) return e;
+  if (int e = check_dtype(in_dtype)) return e;
+  const int64_t ws[3] = {ws_d, ws_h, ws_w}, ss[3] = {ss_d, ss_h, ss_w};
+  return launch_norm_shift_partition(output, out_dtype, x, in_dtype, weight, bias, eps, B, D, H, W,
+                                     C, ws, ss, static_cast<cudaStream_t>(stream));
+}
+
+int crumpet_unshift_unpartition_crop_3d(void* output, const void* windows, const void* residual,
+                                        int dtype, int64_t B, int64_t D, int64_t H, int64_t W,
+                                        int64_t C, int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                                        int64_t ss_d, int64_t ss_h, int64_t ss_w, void* stream) {
+  if (int e = check_dtype(dtype)) return e;
+  const int64_t ws[3] = {ws_d, ws_h, ws_w}, ss[3] = {ss_d, ss_h, ss_w};
+  return launch_unshift_unpartition_crop(output, windows, residual, dtype, B, D, H, W, C, ws, ss,
+                                         static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_device_status(int clear) {
   const int v = read_device_error(clear != 0);
   if (v < 0) return set_error(kErrCuda, "could not read the device error word");

@@ -32,6 +32,19 @@ int launch_attn_mask(void* out, int64_t D, int64_t H, int64_t W, int64_t ws_d, i
                      int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype,
                      cudaStream_t stream);
 
+// LayerNorm + zero pad to a window multiple + roll(-ss) + partition.  D/H/W are the
+// unpadded dims; ws/ss point at 3 values.  gamma/beta are fp32 [C].
+int launch_norm_shift_partition(void* out, int out_dtype, const void* x, int in_dtype,
+                                const float* gamma, const float* beta, float eps, int64_t B,
+                                int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
+                                const int64_t* ss, cudaStream_t stream);
+
+// Unpartition on the padded grid + roll(+ss) + crop to D/H/W (+ residual, same dtype).
+int launch_unshift_unpartition_crop(void* out, const void* windows, const void* residual,
+                                    int dtype, int64_t B, int64_t D, int64_t H, int64_t W,
+                                    int64_t C, const int64_t* ws, const int64_t* ss,
+                                    cudaStream_t stream);
+
 // Window attention: out = softmax(q k^T * scale + bias[h] + mask[b mod nmask]) v.
 struct AttnArgs {
   // q/k/v addressing: element (b, h, n, d) lives at

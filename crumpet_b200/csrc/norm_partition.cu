@@ -1,0 +1,486 @@
+// crumpet_b200: the memory passes around the window attention of a Swin block,
+// fused.
+//
+// The reference's patched block (torch-ext/crumpet/monai_patch.py:79-111) runs
+//   norm1 (LayerNorm; fp32 under fp16 autocast) -> F.pad of D/H/W up to a window
+//   multiple -> roll + partition -> [qkv Linear casts to fp16] -> attention ->
+//   unpartition + roll back -> crop of the padding -> residual add (MONAI block)
+// as separate full-volume passes.  Two kernels replace them:
+//
+// norm_shift_partition: out[b*nW + win, loc, :] =
+//     LN(x[b, s_d, s_h, s_w, :])  when s lies inside the D x H x W volume,
+//     0                            when s lies in the padding (F.pad comes after
+//                                  the norm, so padded tokens are exact zeros),
+//   with s = (win_coord*ws + loc_coord + ss) mod padded_dim per axis -- the
+//   geometry of partition.cu on the padded grid Dp = ceil(D/ws)*ws.
+//   LN(v) = (v - mean) * rsqrt(var + eps) * weight + bias over C channels in fp32,
+//   biased variance (torch.nn.LayerNorm), rounded once to the output type, which
+//   may differ from the input type (fp16 out for the qkv Linear under autocast).
+//
+// unshift_unpartition_crop: out[b, d, h, w, :] (+ residual[b, d, h, w, :]) =
+//     windows[b*nW + win(p), loc(p), :],  p = (d - ss) mod Dp, ... per axis,
+//   for the unpadded volume only: padded tokens are never read, the cropped
+//   volume is written directly.  The residual add happens in fp32 and is
+//   rounded once, as torch's elementwise add for half types.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace crumpet {
+
+namespace {
+
+constexpr int kThreads = 256;
+// LayerNorm kernel work split: a token's C channels are 8-channel groups spread
+// over L lanes (L a power of two, the smallest with L * kGroupsPerLane >= C/8),
+// kGroupsPerLane groups per lane, and each L-lane group normalises
+// kTokensPerGroup tokens with all their loads in flight before any arithmetic.
+constexpr int kGroupsPerLane = 3;
+constexpr int kTokensPerGroup = 2;
+constexpr int kMaxC = 16 * kGroupsPerLane * 8;  // L <= 16: C <= 384
+
+struct BlockGeom {
+  uint32_t D, H, W;        // unpadded volume
+  uint32_t Dp, Hp, Wp;     // padded grid (window multiples)
+  uint32_t wd, wh, ww, sd, sh, sw;
+  uint32_t nwh, nww, nw, N, C, groups;  // groups = C / 8
+  uint32_t tokens;         // output tokens of this launch (B_slice * nW * N)
+  DivMod32 f_N, f_nw, f_nww, f_nwh, f_ww, f_wh, f_wd;
+  float eps;
+};
+
+// 8 consecutive channels: raw 16/32-byte load, conversion to fp32, store.
+template <typename T>
+struct Io;
+template <>
+struct Io<float> {
+  struct Raw {
+    uint4 a, b;
+  };
+  static __device__ __forceinline__ Raw load(const float* p) {
+    return Raw{ldg_stream(reinterpret_cast<const uint4*>(p)),
+               ldg_stream(reinterpret_cast<const uint4*>(p) + 1)};
+  }
+  static __device__ __forceinline__ void to_float(const Raw& r, float (&v)[8]) {
+    const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(w[i]);
+  }
+  static __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+    stg(reinterpret_cast<uint4*>(p), make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
+                                                __float_as_uint(v[2]), __float_as_uint(v[3])));
+    stg(reinterpret_cast<uint4*>(p) + 1,
+        make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
+                   __float_as_uint(v[7])));
+  }
+};
+template <>
+struct Io<__half> {
+  struct Raw {
+    uint4 a;
+  };
+  static __device__ __forceinline__ Raw load(const __half* p) {
+    return Raw{ldg_stream(reinterpret_cast<const uint4*>(p))};
+  }
+  static __device__ __forceinline__ void to_float(const Raw& r, float (&v)[8]) {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    stg(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
+  }
+};
+template <>
+struct Io<__nv_bfloat16> {
+  struct Raw {
+    uint4 a;
+  };
+  static __device__ __forceinline__ Raw load(const __nv_bfloat16* p) {
+    return Raw{ldg_stream(reinterpret_cast<const uint4*>(p))};
+  }
+  static __device__ __forceinline__ void to_float(const Raw& r, float (&v)[8]) {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+  static __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    stg(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
+  }
+};
+
+// Token t's source voxel: ((b*D + s_d)*H + s_h)*W + s_w, or "padding".
+__device__ __forceinline__ bool token_source(const BlockGeom& g, uint32_t token, uint64_t& src) {
+  uint32_t bw, loc, b, win, t, iw, id, ih, t2, lw, ld, lh;
+  g.f_N.divmod(token, bw, loc);
+  g.f_nw.divmod(bw, b, win);
+  g.f_nww.divmod(win, t, iw);
+  g.f_nwh.divmod(t, id, ih);
+  g.f_ww.divmod(loc, t2, lw);
+  g.f_wh.divmod(t2, ld, lh);
+  uint32_t sd = id * g.wd + ld + g.sd;
+  uint32_t sh = ih * g.wh + lh + g.sh;
+  uint32_t sw = iw * g.ww + lw + g.sw;
+  sd -= (sd >= g.Dp) ? g.Dp : 0u;
+  sh -= (sh >= g.Hp) ? g.Hp : 0u;
+  sw -= (sw >= g.Wp) ? g.Wp : 0u;
+  src = ((uint64_t(b) * g.D + sd) * g.H + sh) * g.W + sw;
+  return sd < g.D && sh < g.H && sw < g.W;
+}
+
+template <int L>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int off = L / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Lane `sub` of an L-lane group owns channel groups sub, sub + L, sub + 2L of
+// its tokens; the group's tokens in one block step are consecutive output
+// tokens, so a warp reads and writes contiguous rows.
+template <typename TIn, typename TOut, int L>
+__global__ void __launch_bounds__(kThreads)
+norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
+                            const float* __restrict__ gamma, const float* __restrict__ beta,
+                            const BlockGeom g) {
+  constexpr uint32_t kGroups = kThreads / L;  // lane groups per block
+  const uint32_t sub = threadIdx.x % L;
+  const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
+  uint32_t token[kTokensPerGroup];
+  bool inside[kTokensPerGroup];
+  typename Io<TIn>::Raw raw[kTokensPerGroup][kGroupsPerLane];
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    token[j] = first + j * kGroups;
+    uint64_t src = 0;
+    inside[j] = token[j] < g.tokens && token_source(g, token[j], src);
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (inside[j] && grp < g.groups) raw[j][k] = Io<TIn>::load(x + src * g.C + grp * 8);
+    }
+  }
+  const float inv_c = 1.f / float(g.C);
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    float v[kGroupsPerLane][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (inside[j] && grp < g.groups) {
+        Io<TIn>::to_float(raw[j][k], v[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += v[k][e];
+      }
+    }
+    // every lane takes part in the shuffles (padding and dead tokens add zeros)
+    const float mean = group_sum<L>(sum) * inv_c;
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (inside[j] && grp < g.groups) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[k][e] - mean;
+          sq = fmaf(d, d, sq);
+        }
+      }
+    }
+    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
+    if (token[j] >= g.tokens) continue;
+    TOut* dst = out + uint64_t(token[j]) * g.C;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (grp >= g.groups) continue;
+      float y[8];
+      if (inside[j]) {
+        const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
+        const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
+        const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
+        const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = 0.f;  // F.pad after the norm: zeros
+      }
+      Io<TOut>::store8(dst + grp * 8, y);
+    }
+  }
+}
+
+// a + b per 32-bit word, in fp32, rounded once (torch's add for half types).
+template <typename T>
+__device__ __forceinline__ uint32_t add_word(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t add_word<float>(uint32_t a, uint32_t b) {
+  return __float_as_uint(__uint_as_float(a) + __uint_as_float(b));
+}
+template <>
+__device__ __forceinline__ uint32_t add_word<__half>(uint32_t a, uint32_t b) {
+  const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  const __half2 r = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t add_word<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  const float lo = __uint_as_float(a << 16) + __uint_as_float(b << 16);
+  const float hi = __uint_as_float(a & 0xFFFF0000u) + __uint_as_float(b & 0xFFFF0000u);
+  const __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+template <typename T, int VB>
+__device__ __forceinline__ typename VecT<VB>::type add_vec(typename VecT<VB>::type a,
+                                                          typename VecT<VB>::type b) {
+  if constexpr (VB == 16) {
+    return make_uint4(add_word<T>(a.x, b.x), add_word<T>(a.y, b.y), add_word<T>(a.z, b.z),
+                      add_word<T>(a.w, b.w));
+  } else if constexpr (VB == 8) {
+    return make_uint2(add_word<T>(a.x, b.x), add_word<T>(a.y, b.y));
+  } else {
+    return add_word<T>(a, b);
+  }
+}
+
+// One thread per output vector of the cropped volume.
+template <typename T, int VB, bool RES>
+__global__ void __launch_bounds__(kThreads)
+unshift_unpartition_crop_kernel(typename VecT<VB>::type* __restrict__ out,
+                                const typename VecT<VB>::type* __restrict__ windows,
+                                const typename VecT<VB>::type* __restrict__ residual,
+                                const BlockGeom g, uint32_t cv, DivMod32 f_cv, DivMod32 f_W,
+                                DivMod32 f_H, DivMod32 f_D, uint32_t total) {
+  const uint32_t o = blockIdx.x * kThreads + threadIdx.x;
+  if (o >= total) return;
+  uint32_t p, v, t, w, t2, h, b, d, id, ld, ih, lh, iw, lw;
+  f_cv.divmod(o, p, v);
+  f_W.divmod(p, t, w);
+  f_H.divmod(t, t2, h);
+  f_D.divmod(t2, b, d);
+  d = (d >= g.sd) ? d - g.sd : d + g.Dp - g.sd;
+  h = (h >= g.sh) ? h - g.sh : h + g.Hp - g.sh;
+  w = (w >= g.sw) ? w - g.sw : w + g.Wp - g.sw;
+  g.f_wd.divmod(d, id, ld);
+  g.f_wh.divmod(h, ih, lh);
+  g.f_ww.divmod(w, iw, lw);
+  const uint32_t win = (id * g.nwh + ih) * g.nww + iw;
+  const uint32_t loc = (ld * g.wh + lh) * g.ww + lw;
+  const uint64_t src = (uint64_t(b) * g.nw + win) * g.N * cv + uint64_t(loc) * cv + v;
+  auto val = ldg_stream(windows + src);
+  if constexpr (RES) val = add_vec<T, VB>(ldg_stream(residual + o), val);
+  stg(out + o, val);
+}
+
+int check_geometry(int64_t B, int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
+                   const int64_t* ss) {
+  const int64_t dims[3] = {D, H, W};
+  if (B < 0 || C < 0) return set_error(kErrInvalid, "B and C must be non-negative");
+  for (int a = 0; a < 3; ++a) {
+    if (dims[a] <= 0) return set_error(kErrInvalid, "D, H and W must be positive");
+    if (ws[a] <= 0) return set_error(kErrInvalid, "window_size values must be positive");
+    if (ss[a] < 0 || ss[a] >= ws[a])
+      return set_error(kErrInvalid, "shift_size must satisfy 0 <= shift < window_size");
+  }
+  int64_t padded = 1;
+  for (int a = 0; a < 3; ++a) padded *= (dims[a] + ws[a] - 1) / ws[a] * ws[a];
+  if (padded >= (int64_t(1) << 31))
+    return set_error(kErrInvalid, "padded D*H*W must be below 2^31");
+  return kOk;
+}
+
+BlockGeom make_geom(int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
+                    const int64_t* ss) {
+  BlockGeom g{};
+  g.D = uint32_t(D);
+  g.H = uint32_t(H);
+  g.W = uint32_t(W);
+  g.wd = uint32_t(ws[0]);
+  g.wh = uint32_t(ws[1]);
+  g.ww = uint32_t(ws[2]);
+  g.Dp = (g.D + g.wd - 1) / g.wd * g.wd;
+  g.Hp = (g.H + g.wh - 1) / g.wh * g.wh;
+  g.Wp = (g.W + g.ww - 1) / g.ww * g.ww;
+  g.sd = uint32_t(ss[0]);
+  g.sh = uint32_t(ss[1]);
+  g.sw = uint32_t(ss[2]);
+  g.nwh = g.Hp / g.wh;
+  g.nww = g.Wp / g.ww;
+  g.nw = (g.Dp / g.wd) * g.nwh * g.nww;
+  g.N = g.wd * g.wh * g.ww;
+  g.C = uint32_t(C);
+  g.groups = g.C / 8;
+  g.f_N = DivMod32::make(g.N);
+  g.f_nw = DivMod32::make(g.nw);
+  g.f_nww = DivMod32::make(g.nww);
+  g.f_nwh = DivMod32::make(g.nwh);
+  g.f_ww = DivMod32::make(g.ww);
+  g.f_wh = DivMod32::make(g.wh);
+  g.f_wd = DivMod32::make(g.wd);
+  return g;
+}
+
+template <typename TIn, typename TOut>
+cudaError_t launch_norm(void* out, const void* x, const float* gamma, const float* beta,
+                        const BlockGeom& g, cudaStream_t stream) {
+  int lanes = 1;
+  while (uint32_t(lanes * kGroupsPerLane) < g.groups) lanes *= 2;
+  const uint32_t per_block = uint32_t(kThreads / lanes) * kTokensPerGroup;
+  const uint32_t blocks = (g.tokens + per_block - 1) / per_block;
+  auto o = static_cast<TOut*>(out);
+  auto xi = static_cast<const TIn*>(x);
+  switch (lanes) {
+    case 1: norm_shift_partition_kernel<TIn, TOut, 1><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 2: norm_shift_partition_kernel<TIn, TOut, 2><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 4: norm_shift_partition_kernel<TIn, TOut, 4><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 8: norm_shift_partition_kernel<TIn, TOut, 8><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    default: norm_shift_partition_kernel<TIn, TOut, 16><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+  }
+  return cudaGetLastError();
+}
+
+template <typename TIn>
+cudaError_t launch_norm_out(int out_dtype, void* out, const void* x, const float* gamma,
+                            const float* beta, const BlockGeom& g, cudaStream_t stream) {
+  if (out_dtype == kF32) return launch_norm<TIn, float>(out, x, gamma, beta, g, stream);
+  if (out_dtype == kF16) return launch_norm<TIn, __half>(out, x, gamma, beta, g, stream);
+  return launch_norm<TIn, __nv_bfloat16>(out, x, gamma, beta, g, stream);
+}
+
+template <typename T, int VB, bool RES>
+cudaError_t launch_crop_t(void* out, const void* windows, const void* residual, const BlockGeom& g,
+                          uint32_t cv, uint32_t batches, cudaStream_t stream) {
+  using V = typename VecT<VB>::type;
+  const uint32_t total = batches * g.D * g.H * g.W * cv;
+  const uint32_t blocks = (total + kThreads - 1) / kThreads;
+  unshift_unpartition_crop_kernel<T, VB, RES><<<blocks, kThreads, 0, stream>>>(
+      static_cast<V*>(out), static_cast<const V*>(windows), static_cast<const V*>(residual), g, cv,
+      DivMod32::make(cv), DivMod32::make(g.W), DivMod32::make(g.H), DivMod32::make(g.D), total);
+  return cudaGetLastError();
+}
+
+template <typename T, bool RES>
+cudaError_t launch_crop_vb(int vb, void* out, const void* windows, const void* residual,
+                           const BlockGeom& g, uint32_t cv, uint32_t batches,
+                           cudaStream_t stream) {
+  switch (vb) {
+    case 16: return launch_crop_t<T, 16, RES>(out, windows, residual, g, cv, batches, stream);
+    case 8: return launch_crop_t<T, 8, RES>(out, windows, residual, g, cv, batches, stream);
+    default: return launch_crop_t<T, 4, RES>(out, windows, residual, g, cv, batches, stream);
+  }
+}
+
+}  // namespace
+
+int launch_norm_shift_partition(void* out, int out_dtype, const void* x, int in_dtype,
+                                const float* gamma, const float* beta, float eps, int64_t B,
+                                int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
+                                const int64_t* ss, cudaStream_t stream) {
+  if (int e = check_geometry(B, D, H, W, C, ws, ss)) return e;
+  if (C == 0 || C % 8 != 0 || C > kMaxC)
+    return set_error(kErrUnsupported,
+                     "norm_shift_partition_3d needs C a multiple of 8 and at most 384");
+  if (ws[0] * ws[1] * ws[2] > 4096) return set_error(kErrInvalid, "window volume above 4096");
+  if (B == 0) return kOk;
+  if (!out || !x || !gamma || !beta) return set_error(kErrInvalid, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
+       reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15u)
+    return set_error(kErrInvalid, "tensors must be 16-byte aligned");
+  BlockGeom g = make_geom(D, H, W, C, ws, ss);
+  g.eps = eps;
+  // batch slices keep every in-launch token index below 2^31
+  const uint64_t per_batch = uint64_t(g.nw) * g.N;
+  const uint64_t bmax = ((uint64_t(1) << 31) - 1) / per_batch;
+  const int64_t in_row = C * dtype_size(in_dtype), out_row = C * dtype_size(out_dtype);
+  for (int64_t b0 = 0; b0 < B; b0 += int64_t(bmax)) {
+    const uint64_t nb = uint64_t(B - b0) < bmax ? uint64_t(B - b0) : bmax;
+    g.tokens = uint32_t(nb * per_batch);
+    const void* xs = static_cast<const uint8_t*>(x) + uint64_t(b0) * D * H * W * in_row;
+    void* os = static_cast<uint8_t*>(out) + uint64_t(b0) * per_batch * out_row;
+    cudaError_t err;
+    if (in_dtype == kF32)
+      err = launch_norm_out<float>(out_dtype, os, xs, gamma, beta, g, stream);
+    else if (in_dtype == kF16)
+      err = launch_norm_out<__half>(out_dtype, os, xs, gamma, beta, g, stream);
+    else
+      err = launch_norm_out<__nv_bfloat16>(out_dtype, os, xs, gamma, beta, g, stream);
+    if (err != cudaSuccess) return set_cuda_error(err, "norm_shift_partition launch");
+  }
+  return kOk;
+}
+
+int launch_unshift_unpartition_crop(void* out, const void* windows, const void* residual,
+                                    int dtype, int64_t B, int64_t D, int64_t H, int64_t W,
+                                    int64_t C, const int64_t* ws, const int64_t* ss,
+                                    cudaStream_t stream) {
+  if (int e = check_geometry(B, D, H, W, C, ws, ss)) return e;
+  if (B == 0 || C == 0) return kOk;
+  if (!out || !windows) return set_error(kErrInvalid, "null tensor pointer");
+  const int64_t row = C * dtype_size(dtype);
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(windows) |
+                        reinterpret_cast<uintptr_t>(residual);
+  int vb = 0;
+  for (int c = 16; c >= 4; c /= 2) {
+    if (row % c == 0 && mis % c == 0) {
+      vb = c;
+      break;
+    }
+  }
+  if (vb == 0)
+    return set_error(kErrUnsupported,
+                     "unshift_unpartition_crop_3d needs 4-byte aligned rows and pointers");
+  const BlockGeom g = make_geom(D, H, W, C, ws, ss);
+  const uint32_t cv = uint32_t(row / vb);
+  const uint64_t per_batch_vec = uint64_t(D) * H * W * cv;
+  if (uint64_t(g.nw) * g.N * cv >= (uint64_t(1) << 32))
+    return set_error(kErrInvalid, "one batch entry of windows is too large");
+  const uint64_t bmax = ((uint64_t(1) << 31) - 1) / per_batch_vec;
+  if (bmax == 0) return set_error(kErrInvalid, "one batch entry is too large for one launch");
+  for (int64_t b0 = 0; b0 < B; b0 += int64_t(bmax)) {
+    const uint64_t nb = uint64_t(B - b0) < bmax ? uint64_t(B - b0) : bmax;
+    void* os = static_cast<uint8_t*>(out) + uint64_t(b0) * per_batch_vec * vb;
+    const void* wsrc =
+        static_cast<const uint8_t*>(windows) + uint64_t(b0) * g.nw * g.N * uint64_t(row);
+    const void* rs =
+        residual ? static_cast<const uint8_t*>(residual) + uint64_t(b0) * per_batch_vec * vb
+                 : nullptr;
+    cudaError_t err;
+    if (residual == nullptr) {
+      err = launch_crop_vb<float, false>(vb, os, wsrc, nullptr, g, cv, uint32_t(nb), stream);
+    } else if (dtype == kF32) {
+      err = launch_crop_vb<float, true>(vb, os, wsrc, rs, g, cv, uint32_t(nb), stream);
+    } else if (dtype == kF16) {
+      err = launch_crop_vb<__half, true>(vb, os, wsrc, rs, g, cv, uint32_t(nb), stream);
+    } else {
+      err = launch_crop_vb<__nv_bfloat16, true>(vb, os, wsrc, rs, g, cv, uint32_t(nb), stream);
+    }
+    if (err != cudaSuccess) return set_cuda_error(err, "unshift_unpartition_crop launch");
+  }
+  return kOk;
+}
+
+}  // namespace crumpet

@@ -192,6 +192,61 @@ void swin_window_attention_qkv(at::Tensor& out, const at::Tensor& qkv, const at:
       shift_size[2], dtype_code(qkv), B, H, N, Dh, static_cast<float>(scale), cur_stream(qkv)));
 }
 
+int64_t ceil_to(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+void norm_shift_partition_3d(at::Tensor& output, const at::Tensor& x, const at::Tensor& weight,
+                             const at::Tensor& bias, double eps, int64_t ws_d, int64_t ws_h,
+                             int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(output, "output");
+  check_cuda_contig(weight, "weight");
+  check_cuda_contig(bias, "bias");
+  TORCH_CHECK(x.dim() == 5, "x must have shape [B, D, H, W, C]");
+  const int64_t B = x.size(0), D = x.size(1), H = x.size(2), W = x.size(3), C = x.size(4);
+  TORCH_CHECK(weight.scalar_type() == at::kFloat && bias.scalar_type() == at::kFloat &&
+                  weight.numel() == C && bias.numel() == C,
+              "weight and bias must be float32 tensors of C elements");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
+                                 ws_w);
+  TORCH_CHECK(output.dim() == 3 && output.size(0) == B * nw &&
+                  output.size(1) == ws_d * ws_h * ws_w && output.size(2) == C,
+              "output must have shape [B * num_windows(padded), volume, C]");
+  if (output.numel() == 0) return;
+  check_rc(crumpet_norm_shift_partition_3d(
+      output.data_ptr(), dtype_code(output), x.data_ptr(), dtype_code(x), weight.data_ptr<float>(),
+      bias.data_ptr<float>(), static_cast<float>(eps), B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h,
+      ss_w, cur_stream(x)));
+}
+
+void unshift_unpartition_crop_3d(at::Tensor& output, const at::Tensor& windows,
+                                 const c10::optional<at::Tensor>& residual, int64_t B, int64_t D,
+                                 int64_t H, int64_t W, int64_t C, int64_t ws_d, int64_t ws_h,
+                                 int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w) {
+  check_cuda_contig(windows, "windows");
+  check_cuda_contig(output, "output");
+  TORCH_CHECK(output.scalar_type() == windows.scalar_type(), "output and windows dtypes differ");
+  const c10::cuda::CUDAGuard guard(windows.device());
+  const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
+                                 ws_w);
+  TORCH_CHECK(windows.dim() == 3 && windows.size(0) == B * nw &&
+                  windows.size(1) == ws_d * ws_h * ws_w && windows.size(2) == C,
+              "windows must have shape [B * num_windows(padded), volume, C]");
+  TORCH_CHECK(output.numel() == B * D * H * W * C, "output must have B*D*H*W*C elements");
+  const void* res = nullptr;
+  if (residual.has_value() && residual->defined()) {
+    check_cuda_contig(*residual, "residual");
+    TORCH_CHECK(residual->scalar_type() == windows.scalar_type(),
+                "residual must have the dtype of windows");
+    TORCH_CHECK(residual->numel() == B * D * H * W * C, "residual must have B*D*H*W*C elements");
+    res = residual->data_ptr();
+  }
+  if (output.numel() == 0) return;
+  check_rc(crumpet_unshift_unpartition_crop_3d(output.data_ptr(), windows.data_ptr(), res,
+                                               dtype_code(windows), B, D, H, W, C, ws_d, ws_h,
+                                               ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
+}
+
 }  // namespace
 
 TORCH_LIBRARY(crumpet_ops, ops) {
@@ -223,6 +278,14 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "swin_window_attention_qkv(Tensor! out, Tensor qkv, Tensor table, Tensor index, "
       "int[] num_windows, int[] window_size, int[] shift_size, float scale) -> ()",
       kTags);
+  ops.def(
+      "norm_shift_partition_3d(Tensor! output, Tensor x, Tensor weight, Tensor bias, float eps, "
+      "int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
+  ops.def(
+      "unshift_unpartition_crop_3d(Tensor! output, Tensor windows, Tensor? residual, int B, int D, "
+      "int H, int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
 }
 
 TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
@@ -233,4 +296,6 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("fused_unshift_unpartition_3d_backward", &fused_unshift_unpartition_3d_backward);
   ops.impl("fused_swin_attention", &fused_swin_attention);
   ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
+  ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
+  ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
 }

@@ -5,7 +5,13 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
 
 * ``SwinTransformerBlock.forward_part1``: LayerNorm -> pad -> fused roll +
   partition -> attention -> fused unpartition + reverse roll -> crop
-  (reference :72-114);
+  (reference :72-114), with norm1, the pad, the roll + partition and the
+  autocast cast for the qkv Linear in one kernel (``norm_shift_partition_3d``)
+  and the unpartition, roll back and crop in another
+  (``unshift_unpartition_crop_3d``);
+* ``SwinTransformerBlock.forward`` (not patched by the reference): in eval
+  mode without checkpointing, the residual add of the attention half is folded
+  into the unpartition + crop kernel;
 * ``BasicLayer.forward``: channels-last permute, the cached shifted-window mask
   from ``compute_attn_mask_3d`` on the padded grid, blocks, downsample
   (reference :201-232);
@@ -43,6 +49,7 @@ import torch
 import torch.nn.functional as F
 
 from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpartition_3d
+from .block_fusion import norm_shift_partition_3d, unshift_unpartition_crop_3d
 from .fused_attention import fused_swin_attention, swin_window_attention_qkv
 
 _STATE: dict[str, Any] = {}
@@ -87,30 +94,111 @@ def boundary_flags(dims, window_size, shift_size, device) -> torch.Tensor:
     return flags.reshape(-1).to(torch.uint8).to(device, non_blocking=True)
 
 
+def _block_fusion_enabled() -> bool:
+    """Opt out of the fused norm/partition and unpartition/crop with CRUMPET_DISABLE_BLOCK_FUSION=1."""
+    return os.environ.get("CRUMPET_DISABLE_BLOCK_FUSION", "0") != "1"
+
+
+_FUSED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def _no_grad_needed(*tensors) -> bool:
+    return not torch.is_grad_enabled() or not any(t is not None and t.requires_grad for t in tensors)
+
+
+def _norm_fusable(norm, x: torch.Tensor) -> bool:
+    c = x.shape[-1]
+    return (
+        _block_fusion_enabled()
+        and isinstance(norm, torch.nn.LayerNorm)
+        and norm.weight is not None
+        and norm.bias is not None
+        and tuple(norm.normalized_shape) == (c,)
+        and c % 8 == 0
+        and c <= 384
+        and x.is_cuda
+        and x.dtype in _FUSED_DTYPES
+        and _no_grad_needed(x, norm.weight, norm.bias)
+    )
+
+
+def _norm_out_dtype(x: torch.Tensor) -> torch.dtype:
+    # Under autocast the norm runs in fp32 and the qkv Linear casts its input to
+    # the autocast dtype: the fused op writes that dtype directly.
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
+
+
+def _crop_fusable(windows: torch.Tensor) -> bool:
+    return (
+        _block_fusion_enabled()
+        and windows.is_cuda
+        and windows.dtype in _FUSED_DTYPES
+        and (windows.shape[-1] * windows.element_size()) % 4 == 0
+        and _no_grad_needed(windows)
+    )
+
+
+def _attention_branch(self, x, mask_matrix, swin, residual=None):
+    """norm1 -> pad -> roll + partition -> attn -> unpartition + roll back -> crop
+    (reference monai_patch.py:72-114), plus ``residual +`` when given."""
+    b, d, h, w, c = x.shape
+    window_size, shift_size = swin.get_window_size((d, h, w), self.window_size, self.shift_size)
+    window_size = _as_triple(window_size)
+    shift_size = _as_triple(shift_size)
+    attn_mask = mask_matrix if any(s > 0 for s in shift_size) else None
+    pad_d = (window_size[0] - d % window_size[0]) % window_size[0]
+    pad_h = (window_size[1] - h % window_size[1]) % window_size[1]
+    pad_w = (window_size[2] - w % window_size[2]) % window_size[2]
+    if _norm_fusable(self.norm1, x):
+        x_windows = norm_shift_partition_3d(x, self.norm1.weight, self.norm1.bias, self.norm1.eps,
+                                            window_size, shift_size, _norm_out_dtype(x))
+    else:
+        xn = F.pad(self.norm1(x), (0, 0, 0, pad_w, 0, pad_h, 0, pad_d))
+        x_windows = fused_shift_partition_3d(xn, window_size, shift_size)
+    attn_windows = self.attn(x_windows, mask=attn_mask)
+    if _crop_fusable(attn_windows):
+        fuse_res = (residual is not None and residual.dtype == attn_windows.dtype
+                    and residual.device == attn_windows.device and _no_grad_needed(residual))
+        out = unshift_unpartition_crop_3d(attn_windows, b, d, h, w, c, window_size, shift_size,
+                                          residual=residual if fuse_res else None)
+        if residual is not None and not fuse_res:
+            out = residual + out
+        return out
+    out = fused_unshift_unpartition_3d(attn_windows, b, d + pad_d, h + pad_h, w + pad_w, c,
+                                       window_size, shift_size)
+    if pad_d or pad_h or pad_w:
+        out = out[:, :d, :h, :w, :].contiguous()
+    return out if residual is None else residual + out
+
+
 def _patched_forward_part1(original, swin):
     @functools.wraps(original)
     def forward_part1(self, x, mask_matrix):
         if x.dim() != 5:
             return original(self, x, mask_matrix)
-        x = self.norm1(x)
-        b, d, h, w, c = x.shape
-        window_size, shift_size = swin.get_window_size((d, h, w), self.window_size, self.shift_size)
-        window_size = _as_triple(window_size)
-        shift_size = _as_triple(shift_size)
-        pad_d = (window_size[0] - d % window_size[0]) % window_size[0]
-        pad_h = (window_size[1] - h % window_size[1]) % window_size[1]
-        pad_w = (window_size[2] - w % window_size[2]) % window_size[2]
-        x = F.pad(x, (0, 0, 0, pad_w, 0, pad_h, 0, pad_d))
-        _, dp, hp, wp, _ = x.shape
-        attn_mask = mask_matrix if any(s > 0 for s in shift_size) else None
-        x_windows = fused_shift_partition_3d(x, window_size, shift_size)
-        attn_windows = self.attn(x_windows, mask=attn_mask)
-        x = fused_unshift_unpartition_3d(attn_windows, b, dp, hp, wp, c, window_size, shift_size)
-        if pad_d or pad_h or pad_w:
-            x = x[:, :d, :h, :w, :].contiguous()
-        return x
+        return _attention_branch(self, x, mask_matrix, swin)
 
     return forward_part1
+
+
+def _patched_block_forward(original, swin):
+    """``x + attention_branch(x)`` with the residual folded into the crop, then the MLP half.
+
+    Inference only (eval mode, no activation checkpointing): there drop_path is
+    the identity and the block is ``x = x + part1(x); x = x + part2(x)``.
+    """
+
+    @functools.wraps(original)
+    def forward(self, x, mask_matrix):
+        if (x.dim() != 5 or self.training or getattr(self, "use_checkpoint", False)
+                or not _block_fusion_enabled()):
+            return original(self, x, mask_matrix)
+        x = _attention_branch(self, x, mask_matrix, swin, residual=x)
+        return x + self.forward_part2(x)
+
+    return forward
 
 
 def _patched_window_attention_forward(original):
@@ -189,9 +277,11 @@ def patch_monai_swin_unetr(swin_module=None) -> bool:
         patched=True,
         swin=swin,
         forward_part1=swin.SwinTransformerBlock.forward_part1,
+        block_forward=swin.SwinTransformerBlock.forward,
         basic_layer_forward=swin.BasicLayer.forward,
     )
     swin.SwinTransformerBlock.forward_part1 = _patched_forward_part1(_STATE["forward_part1"], swin)
+    swin.SwinTransformerBlock.forward = _patched_block_forward(_STATE["block_forward"], swin)
     swin.BasicLayer.forward = _patched_basic_layer_forward(_STATE["basic_layer_forward"], swin)
     if _fused_attn_enabled():
         _STATE["window_attention_forward"] = swin.WindowAttention.forward
@@ -205,6 +295,7 @@ def unpatch_monai_swin_unetr() -> bool:
         return False
     swin = _STATE["swin"]
     swin.SwinTransformerBlock.forward_part1 = _STATE["forward_part1"]
+    swin.SwinTransformerBlock.forward = _STATE["block_forward"]
     swin.BasicLayer.forward = _STATE["basic_layer_forward"]
     if "window_attention_forward" in _STATE:
         swin.WindowAttention.forward = _STATE["window_attention_forward"]

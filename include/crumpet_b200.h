@@ -153,6 +153,48 @@ CRUMPET_API int crumpet_swin_window_attention_qkv(
     int64_t N, int64_t head_dim, float scale, void* stream);
 
 /*
+ * LayerNorm, zero padding, cyclic roll by -ss and window partition in one pass:
+ * the first half of a Swin block's attention branch.
+ *   x      [B, D, H, W, C]  (in_dtype), any D/H/W (not window multiples)
+ *   output [B * nW, ws_d*ws_h*ws_w, C]  (out_dtype)
+ *          nW = ceil(D/ws_d) * ceil(H/ws_h) * ceil(W/ws_w)
+ * Token (b, win, loc) is LN(x[b, s]) with s = (win_coord*ws + loc_coord + ss)
+ * mod padded dim when s lies inside the volume, and exactly 0 in the padding.
+ * LN = (v - mean) / sqrt(var + eps) * weight + bias over C, fp32 arithmetic,
+ * biased variance, one rounding to out_dtype.  weight, bias: fp32 [C].
+ * C a multiple of 8, at most 384; all pointers 16-byte aligned.
+ * Replaces norm1 -> F.pad -> crumpet_ops::fused_shift_partition_3d, and the fp16
+ * cast autocast inserts before the qkv Linear, in
+ *   torch-ext/crumpet/monai_patch.py:79-97 (the reference runs them as separate
+ *   torch passes around its partition op).
+ */
+CRUMPET_API int crumpet_norm_shift_partition_3d(void* output, int out_dtype, const void* x,
+                                                int in_dtype, const float* weight,
+                                                const float* bias, float eps, int64_t B, int64_t D,
+                                                int64_t H, int64_t W, int64_t C, int64_t ws_d,
+                                                int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                                int64_t ss_h, int64_t ss_w, void* stream);
+
+/*
+ * Window reverse on the padded grid, cyclic roll by +ss and crop to D/H/W in one
+ * pass, optionally adding a residual:
+ *   windows  [B * nW, ws_d*ws_h*ws_w, C]  (nW on the padded grid, as above)
+ *   residual [B, D, H, W, C] or NULL
+ *   output   [B, D, H, W, C] = unpartition(windows)[:, :D, :H, :W] (+ residual)
+ * All three share dtype; the add is done in fp32 and rounded once (torch's
+ * elementwise add).  Rows of C elements and the pointers must be 4-byte aligned.
+ * Replaces crumpet_ops::fused_unshift_unpartition_3d -> crop .contiguous() in
+ *   torch-ext/crumpet/monai_patch.py:108-111, and the residual add of the Swin
+ *   block that calls it.
+ */
+CRUMPET_API int crumpet_unshift_unpartition_crop_3d(void* output, const void* windows,
+                                                    const void* residual, int dtype, int64_t B,
+                                                    int64_t D, int64_t H, int64_t W, int64_t C,
+                                                    int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                                                    int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                                    void* stream);
+
+/*
  * Device error word: non-zero once a kernel of this library gave up on a
  * bounded wait (it then drained its work, freed its tensor memory and
  * returned without completing its output).  Reading it synchronises with the

@@ -110,3 +110,31 @@ def attention_inputs(case, mask_fn=None):
         reps = B // mask.shape[0]
         boundary = boundary.repeat(reps)
     return q, k, v, bias, mask, boundary
+
+
+# Block glue around the attention (norm1 -> pad -> roll + partition ... unpartition
+# -> crop).  (name, (B, D, H, W, C), configured window, configured shift, seed);
+# the runtime window/shift follow MONAI's clamp (an axis no longer than its
+# window uses the axis length and no shift).
+BLOCK_CASES = [
+    ("b_9x8x10_ws4_ss2_C16", (2, 9, 8, 10, 16), (4, 4, 4), (2, 2, 2), 51),
+    ("b_13x10x9_ws7_ss3_C48", (1, 13, 10, 9, 48), (7, 7, 7), (3, 3, 3), 52),
+    ("b_6x6x6_clamped_C24", (1, 6, 6, 6, 24), (7, 7, 7), (3, 3, 3), 53),
+    ("b_5x9x11_mixed_C32", (2, 5, 9, 11, 32), (7, 7, 7), (3, 3, 3), 54),
+    ("b_8x8x8_noshift_C40", (1, 8, 8, 8, 40), (4, 4, 4), (0, 0, 0), 55),
+]
+
+
+def block_inputs(case):
+    """x [B,D,H,W,C] fp32, LayerNorm weight/bias fp32 [C], eps."""
+    _, shape, _, _, seed = case
+    C = shape[-1]
+    x = randn(seed, shape, "float32") * 2.0 + 0.5
+    weight = 1.0 + 0.25 * randn(seed + 1, (C,), "float32")
+    bias = 0.1 * randn(seed + 2, (C,), "float32")
+    return x, weight, bias, 1e-5
+
+
+def block_attn_output(case, windows_shape):
+    """The stand-in attention output fed back through the unpartition + crop."""
+    return randn(case[-1] + 3, windows_shape, "float32")

@@ -9,6 +9,11 @@ the tests themselves):
   functions (torch-ext/crumpet/reference.py: unfused_shift_partition_3d_reference,
   unfused_unshift_unpartition_3d_reference, compute_attn_mask_3d_reference) on
   the seeded inputs of tests/golden/inputs.py.
+* Block glue: the reference's patched ``forward_part1``
+  (torch-ext/crumpet/monai_patch.py:72-114) run on the CPU on a stand-in block
+  (LayerNorm norm1, configured window/shift, an ``attn`` that records the
+  windows it is given and returns a seeded tensor): the windows after
+  norm1 -> pad -> roll + partition, and the cropped output.
 * Attention: outputs of the reference Triton kernel
   (torch-ext/crumpet/fused_attention.py:48-146), launched exactly as its
   launcher does (:149-226), executed by the Triton CPU interpreter.
@@ -94,6 +99,46 @@ def main(ref_root: str) -> None:
         manifest["attention"][name] = {"shape": list(out.shape), "dtype": str(q.dtype)}
         print("attention", name, flush=True)
     np.savez_compressed(HERE / "attention_ref_out.npz", **arrays)
+
+    from crumpet import monai_patch as MP
+    import crumpet_b200.swin_unetr as swin  # provides get_window_size (MONAI rule)
+
+    class _Attn(torch.nn.Module):
+        def __init__(self, case):
+            super().__init__()
+            self.case = case
+
+        def forward(self, windows, mask=None):
+            self.windows = windows.clone()
+            return I.block_attn_output(self.case, windows.shape)
+
+    class _Block(torch.nn.Module):
+        def __init__(self, case):
+            super().__init__()
+            _, shape, window, shift, _ = case
+            x, w, b, eps = I.block_inputs(case)
+            self.norm1 = torch.nn.LayerNorm(shape[-1], eps=eps)
+            with torch.no_grad():
+                self.norm1.weight.copy_(w)
+                self.norm1.bias.copy_(b)
+            self.window_size, self.shift_size = window, shift
+            self.attn = _Attn(case)
+
+    part1 = MP._patched_forward_part1(lambda *a: None, swin)
+    block_arrays = {}
+    manifest["block"] = {}
+    for case in I.BLOCK_CASES:
+        name = case[0]
+        blk = _Block(case)
+        x = I.block_inputs(case)[0]
+        with torch.no_grad():
+            out = part1(blk, x, None)
+        block_arrays[name + ".windows"] = blk.attn.windows.numpy()
+        block_arrays[name + ".out"] = out.numpy()
+        manifest["block"][name] = {"windows_shape": list(blk.attn.windows.shape),
+                                   "out_sha256": sha(out)}
+        print("block", name, flush=True)
+    np.savez_compressed(HERE / "block_ref.npz", **block_arrays)
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
 
 

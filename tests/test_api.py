@@ -65,6 +65,13 @@ def test_dispatcher_ops_keep_reference_schemas():
     tags = ops.fused_shift_partition_3d.default.tags
     assert torch.Tag.pt2_compliant_tag in tags and torch.Tag.needs_fixed_stride_order in tags
     assert "Tensor? mask" in str(ops.fused_swin_attention.default._schema)
+    assert str(ops.norm_shift_partition_3d.default._schema) == (
+        "crumpet_ops::norm_shift_partition_3d(Tensor($0! -> ) output, Tensor x, Tensor weight, "
+        "Tensor bias, float eps, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()")
+    assert str(ops.unshift_unpartition_crop_3d.default._schema) == (
+        "crumpet_ops::unshift_unpartition_crop_3d(Tensor($0! -> ) output, Tensor windows, "
+        "Tensor? residual, int B, int D, int H, int W, int C, int ws_d, int ws_h, int ws_w, "
+        "int ss_d, int ss_h, int ss_w) -> ()")
 
 
 def test_invalid_divisibility_fails_clearly():
@@ -165,3 +172,63 @@ def test_packed_attention_capi_validation():
     rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, null, 343, 2, 2, 2, 7, 7, 7, 3, 3,
                                                3, 1, 8, 3, 343, 16, 0.25, null)
     assert rc == 1
+
+
+def test_block_fusion_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    norm = lib.crumpet_norm_shift_partition_3d
+    # C not a multiple of 8 / above 384
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 44, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 3 and "multiple of 8" in _ops.last_error()
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 392, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 3
+    # shift >= window, bad dtype, null pointers, empty batch
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 7, 3, 3, null)
+    assert rc == 1 and "shift" in _ops.last_error()
+    rc = norm(null, 5, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "float32" in _ops.last_error()
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 0, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 0
+    # misaligned pointers (checked before any launch)
+    rc = norm(ctypes.c_void_p(8), 1, ctypes.c_void_p(16), 1, ctypes.c_void_p(16), ctypes.c_void_p(16),
+              1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "aligned" in _ops.last_error()
+    crop = lib.crumpet_unshift_unpartition_crop_3d
+    rc = crop(null, null, null, 1, 1, 0, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "positive" in _ops.last_error()
+    rc = crop(null, null, null, 1, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    # fp16 rows of an odd C are not 4-byte multiples
+    rc = crop(ctypes.c_void_p(16), ctypes.c_void_p(16), null, 1, 1, 13, 10, 9, 13, 7, 7, 7, 3, 3, 3,
+              null)
+    assert rc == 3
+    rc = crop(null, null, null, 1, 0, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 0
+
+
+def test_block_fusion_wrappers_validate_and_have_no_cpu_path():
+    x = torch.randn(1, 13, 10, 9, 48)
+    w, b = torch.ones(48), torch.zeros(48)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        crumpet.norm_shift_partition_3d(torch.randn(1, 8, 8, 8, 12), torch.ones(12), torch.zeros(12),
+                                        1e-5, (4, 4, 4), (2, 2, 2))
+    with pytest.raises(ValueError, match="shift_size"):
+        crumpet.norm_shift_partition_3d(x, w, b, 1e-5, (7, 7, 7), (7, 3, 3))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.norm_shift_partition_3d(x, w, b, 1e-5, (7, 7, 7), (3, 3, 3))
+    meta = crumpet.norm_shift_partition_3d(x.to("meta"), w, b, 1e-5, (7, 7, 7), (3, 3, 3),
+                                           torch.float16)
+    assert meta.shape == (8, 343, 48) and meta.dtype == torch.float16
+    win = torch.randn(8, 343, 48)
+    with pytest.raises(ValueError, match="windows must have shape"):
+        crumpet.unshift_unpartition_crop_3d(win, 1, 15, 10, 9, 48, (7, 7, 7), (3, 3, 3))
+    with pytest.raises(TypeError, match="residual"):
+        crumpet.unshift_unpartition_crop_3d(win, 1, 13, 10, 9, 48, (7, 7, 7), (3, 3, 3),
+                                            residual=torch.randn(1, 13, 10, 9, 48).half())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.unshift_unpartition_crop_3d(win, 1, 13, 10, 9, 48, (7, 7, 7), (3, 3, 3))
+    out = crumpet.unshift_unpartition_crop_3d(win.to("meta"), 1, 13, 10, 9, 48, (7, 7, 7), (3, 3, 3))
+    assert out.shape == (1, 13, 10, 9, 48)

@@ -32,8 +32,11 @@ def test_shifted_block_matches_eager(cuda_device):
     x = torch.randn((1, 28, 28, 28, 48), device=cuda_device)
     mask = swin_unetr.compute_mask((28, 28, 28), (7, 7, 7), (3, 3, 3), cuda_device)
     before = profiling.total_launches()
-    patched = _run(lambda t: blk(t, crumpet.compute_attn_mask_3d(28, 28, 28, (7, 7, 7), (3, 3, 3),
-                                                               torch.float16, cuda_device)), x, True)
+    # a mask without recorded window geometry (a copy, not the cached tensor the
+    # patched BasicLayer annotates): the block takes the dense-mask kernel
+    dense = crumpet.compute_attn_mask_3d(28, 28, 28, (7, 7, 7), (3, 3, 3), torch.float16,
+                                         cuda_device).clone()
+    patched = _run(lambda t: blk(t, dense), x, True)
     assert profiling.counters["fused_swin_attention"] > 0
     assert profiling.total_launches() - before >= 3
     eager = _run(lambda t: blk(t, mask), x, False)

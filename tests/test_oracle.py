@@ -12,6 +12,7 @@ import torch
 
 import inputs as I
 from oracle import attention as OA
+from oracle import block as OB
 from oracle import mechanics as OM
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -79,3 +80,23 @@ def test_relative_position_index_quirk():
     full = OA.relative_position_index((7, 7, 7))
     assert full.shape == (343, 343) and full.min() == 0 and full.max() == 13**3 - 1
     assert np.array_equal(full[:216, :216], I.relative_index((7, 7, 7))[:216, :216])
+
+
+BLOCK_REF = np.load(GOLDEN / "block_ref.npz")
+
+
+@pytest.mark.parametrize("case", I.BLOCK_CASES, ids=[c[0] for c in I.BLOCK_CASES])
+def test_oracle_block_glue_matches_reference_forward_part1(case):
+    """norm1 -> pad -> roll + partition and unpartition -> crop, against the
+    outputs of the reference's own patched forward_part1 (monai_patch.py:72-114)."""
+    name, shape, window, shift, _ = case
+    x, w, b, eps = I.block_inputs(case)
+    ws, ss = OB.window_geometry(shape[1:4], window, shift)
+    win = OB.norm_shift_partition(x.numpy(), w.numpy(), b.numpy(), eps, ws, ss)
+    ref_win = BLOCK_REF[name + ".windows"]
+    assert list(win.shape) == MANIFEST["block"][name]["windows_shape"] == list(ref_win.shape)
+    np.testing.assert_allclose(win, ref_win, rtol=0, atol=2e-5)
+    attn = I.block_attn_output(case, win.shape).numpy()
+    out = OB.unshift_unpartition_crop(attn, *shape, ws, ss)
+    assert sha(torch.from_numpy(out)) == MANIFEST["block"][name]["out_sha256"]
+    assert np.array_equal(out, BLOCK_REF[name + ".out"])

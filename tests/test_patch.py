@@ -15,15 +15,17 @@ from oracle import mechanics as OM
 
 
 def test_patch_unpatch_repeated_safe():
-    originals = (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.BasicLayer.forward,
-                 swin_unetr.WindowAttention.forward)
+    def current():
+        return (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.SwinTransformerBlock.forward,
+                swin_unetr.BasicLayer.forward, swin_unetr.WindowAttention.forward)
+
+    originals = current()
     assert crumpet.patch_monai_swin_unetr(swin_unetr) is True
     assert crumpet.patch_monai_swin_unetr(swin_unetr) is False
-    assert swin_unetr.WindowAttention.forward is not originals[2]
+    assert all(p is not o for p, o in zip(current(), originals))
     assert crumpet.unpatch_monai_swin_unetr() is True
     assert crumpet.unpatch_monai_swin_unetr() is False
-    assert (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.BasicLayer.forward,
-            swin_unetr.WindowAttention.forward) == originals
+    assert current() == originals
 
 
 def test_patch_without_monai_raises():
