@@ -67,8 +67,8 @@ static_assert(kNumWG + 1 <= kCtrlWarps, "one TMA warp and one MMA warp per WG");
 constexpr int kSmThreads = kNumWG * 4 * 32;            // softmax threads (one per TMEM lane)
 constexpr int kThreads = kCtrlWarps * 32 + kSmThreads;  // 512
 constexpr int kRowBytes = kHD * 2;
-constexpr int kBarsPerWG = 7;
-constexpr uint32_t kTmemPerWG = 128;
+constexpr int kBarsPerWG = 9;
+constexpr uint32_t kTmemPerWG = 160;
 constexpr uint32_t kTmemCols = kTmemPerWG * kNumWG <= 256 ? 256u : 512u;  // power of two
 constexpr float kRescaleLog2 = 8.f;  // P = 2^(x - m_ref) stays <= 2^8
 constexpr float kLog2e = 1.4426950408889634f;
@@ -79,20 +79,25 @@ struct Cfg {
   static constexpr int NKB = (NPAD + 127) / 128;      // 128-row TMA boxes for K and V
   static constexpr int NCH = (NPAD + kCH - 1) / kCH;  // key chunks
   static constexpr int LAST_W = NPAD - (NCH - 1) * kCH;
-  static constexpr int BSTRIDE = NPAD + 8;            // bias tile row stride (elements)
   static constexpr int Q_BYTES = kBM * kRowBytes;
   static constexpr int KV_BYTES = NKB * 128 * kRowBytes;
   static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
-  static constexpr int BIAS_BYTES = kBM * BSTRIDE * 2;
+  // Bias tile: UMMA A operand, K-major without swizzle: 8x8 core matrices of
+  // 128 bytes; core matrix (row group rg, column group cg) at cg * 2048 + rg * 128.
+  static constexpr int BIAS_CG_BYTES = (kBM / 8) * 128;  // 2048
+  static constexpr int BIAS_BYTES = (NPAD / 8) * BIAS_CG_BYTES;
   static constexpr int ONES_BYTES = NKB * 128 * kRowBytes;  // [keys][16] of 1.0
   static constexpr int PLANE_BYTES = 3 * NCH * 8;     // analytic-mask code planes
-  // TMEM columns of one WG: S chunk (64), P chunk (32 packed), O (16) + row sum (16).
+  // TMEM columns of one WG: S chunk (64), two P chunk buffers (32 packed each),
+  // O (16) + row sum (16).
   static constexpr int TM_S = 0;
   static constexpr int TM_P = kCH;
-  static constexpr int TM_O = kCH + kCH / 2;
+  static constexpr int TM_O = kCH + kCH;
   static_assert(TM_O + 2 * kHD <= int(kTmemPerWG), "TMEM budget");
+  static constexpr int IDENT_BYTES = 512;             // 16x16 identity, UMMA B operand
   static constexpr int SMEM_BYTES = 1024 + kStages * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
-                                    PLANE_BYTES + (2 * kStages + kNumWG * kBarsPerWG) * 8 + 64;
+                                    IDENT_BYTES + PLANE_BYTES +
+                                    (2 * kStages + kNumWG * kBarsPerWG + 1) * 8 + 64;
 };
 
 enum MaskMode : int { kMaskNone = 0, kMaskDense = 1, kMaskAnalytic = 2 };
@@ -264,11 +269,13 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint16_t* ones_s = reinterpret_cast<uint16_t*>(smem + kStages * C::STAGE_BYTES);
-  uint16_t* bias_s = ones_s + C::ONES_BYTES / 2;
-  uint64_t* planes = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bias_s) +
-                                                 C::BIAS_BYTES);
+  uint8_t* bias_s = reinterpret_cast<uint8_t*>(ones_s) + C::ONES_BYTES;
+  uint16_t* ident_s = reinterpret_cast<uint16_t*>(bias_s + C::BIAS_BYTES);
+  uint64_t* planes = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(ident_s) +
+                                                 C::IDENT_BYTES);
   uint64_t* bars = planes + 3 * C::NCH;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + kNumWG * kBarsPerWG);
+  uint64_t* bias_ready = bars + 2 * kStages + kNumWG * kBarsPerWG;  // one phase per pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -281,7 +288,9 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   uint64_t* load_full = bars;
   uint64_t* load_empty = bars + kStages;
   auto bar = [&](int w, int i) { return bars + 2 * kStages + w * kBarsPerWG + i; };
-  constexpr int kSF = 0, kSE = 1, kPF = 2, kPE = 3, kOF = 4, kOE = 5, kDR = 6;
+  // kPF/kPE: one barrier per P buffer (kPF + b, kPE + b).  Per-buffer P barriers keep a
+  // warp that runs a chunk ahead from arriving on the barrier of the previous chunk.
+  constexpr int kSF = 0, kSE = 1, kPF = 2, kPE = 4, kOF = 6, kOE = 7, kDR = 8;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -292,11 +301,14 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
       mbar_init(bar(w, kSF), 1);
       mbar_init(bar(w, kSE), 4);
       mbar_init(bar(w, kPF), 4);
+      mbar_init(bar(w, kPF + 1), 4);
       mbar_init(bar(w, kPE), 1);
+      mbar_init(bar(w, kPE + 1), 1);
       mbar_init(bar(w, kOF), 1);
       mbar_init(bar(w, kOE), 4);
       mbar_init(bar(w, kDR), 1);
     }
+    mbar_init(bias_ready, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -318,6 +330,14 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     const uint32_t one2 = BF16 ? 0x3F803F80u : 0x3C003C00u;
     uint32_t* o32 = reinterpret_cast<uint32_t*>(ones_s);
     for (int i = threadIdx.x; i < C::ONES_BYTES / 4; i += kThreads) o32[i] = one2;
+    // 16x16 identity (B operand of the bias MMA, K-major, no swizzle: core matrix
+    // (n group, k group) at k_group * 256 + n_group * 128, row n at +16 n).
+    if (threadIdx.x < 256) {
+      const int n = threadIdx.x >> 4, kk = threadIdx.x & 15;
+      const uint16_t one = BF16 ? 0x3F80u : 0x3C00u;
+      ident_s[((kk >> 3) * 256 + (n >> 3) * 128 + (n & 7) * 16 + (kk & 7) * 2) / 2] =
+          n == kk ? one : uint16_t(0);
+    }
     fence_proxy_async_shared();
   }
   if (warp == 1) {
@@ -377,11 +397,12 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         const uint32_t tP = tmem_base + w * kTmemPerWG + C::TM_P;
         const uint32_t tO = tmem_base + w * kTmemPerWG + C::TM_O;
         const uint32_t ones_addr = smem_u32(ones_s);
-        uint32_t it = 0, n_se = 0, n_pf = 0, n_oe = 0;
+        uint32_t it = 0, n_se = 0, n_oe = 0, n_pv = 0;
         bool ok = true;
         auto issue_pv = [&](int c, uint32_t v_addr) -> bool {
-          if (!mbar_wait(bar(w, kPF), n_pf & 1u, abort_flag)) return false;
-          ++n_pf;
+          // P chunk n_pv is in buffer n_pv & 1; its use (n_pv >> 1) completes phase
+          // n_pv >> 1 of that buffer's P-full barrier
+          if (!mbar_wait(bar(w, kPF + int(n_pv & 1u)), (n_pv >> 1) & 1u, abort_flag)) return false;
           tc_fence_after();
           if (c == 0) {
             if (!mbar_wait(bar(w, kOE), (n_oe & 1u) ^ 1u, abort_flag)) return false;
@@ -392,16 +413,28 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           // B = [V | ones]: MN-major, the ones atom sits LBO bytes after V
           constexpr uint32_t idesc_pv = idesc_f16(kBM, 2 * kHD, BF16, true);
           const uint32_t lbo = ones_addr - v_addr;
+          const uint32_t buf = n_pv & 1u;  // P chunks alternate between two buffers
           for (int k = 0; k < width / 16; ++k) {
             const uint64_t vdesc =
                 smem_desc(v_addr + uint32_t(c * kCH + k * 16) * kRowBytes, lbo, 256, kLayoutSW32);
-            umma_ts(tO, tP + uint32_t(k * 8), vdesc, idesc_pv, (c > 0 || k > 0) ? 1u : 0u);
+            umma_ts(tO, tP + buf * uint32_t(kCH / 2) + uint32_t(k * 8), vdesc, idesc_pv,
+                    (c > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(bar(w, kPE));
+          umma_commit(bar(w, kPE + int(buf)));
+          ++n_pv;
           return true;
         };
+        // Bias MMA: S[:, 16i..16i+16) += bias_tile[:, 16i..16i+16) * I16, which adds
+        // the (bias / scale) tile to the scores exactly (one non-zero product per sum).
+        const uint32_t bias_addr = smem_u32(bias_s);
+        const uint64_t ident_desc = smem_desc(smem_u32(ident_s), 256, 128, kLayoutNone);
+        constexpr uint32_t idesc_bias = idesc_f16(kBM, 16, BF16, false);
         uint32_t k = 0;
         for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
+          if (!mbar_wait(bias_ready, uint32_t(pi) & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
           for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k) {
             if (int(k % kNumWG) != w) continue;
             const int st = int(k % kStages);
@@ -427,6 +460,12 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               const uint64_t kdesc =
                   smem_desc(k_addr + uint32_t(c * kCH) * kRowBytes, 16, 256, kLayoutSW32);
               umma_ss(tS, qdesc, kdesc, idesc_f16(kBM, width, BF16, false), 0u);
+              for (int i = 0; i < width / 16; ++i) {
+                const uint64_t bdesc = smem_desc(
+                    bias_addr + uint32_t(c * (kCH / 8) + 2 * i) * C::BIAS_CG_BYTES,
+                    C::BIAS_CG_BYTES, 128, kLayoutNone);
+                umma_ss(tS + uint32_t(16 * i), bdesc, ident_desc, idesc_bias, 1u);
+              }
               umma_commit(bar(w, kSF));
               if (c > 0 && !issue_pv(c - 1, v_addr)) ok = false;
             }
@@ -456,65 +495,98 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     const float kNegInf = __int_as_float(0xff800000);
     // scores are carried in the log2 domain: x = (q.k * scale + bias + mask) * log2(e)
     const float2 c1 = make_float2(p.scale * kLog2e, p.scale * kLog2e);
-    uint32_t n_sf = 0, n_pe = 0, n_of = 0;
+    uint32_t n_sf = 0, n_of = 0;
+    uint32_t n_chunk = 0;  // chunks of this WG so far: P buffer n_chunk & 1, its use n_chunk >> 1
     uint32_t k_tile = 0;  // tile index within the CTA (shared numbering with the TMA/MMA warps)
     bool ok = true;
 
     for (int pi = 0; pi < sc.pair_count; ++pi) {
       const int pair = sc.pair_begin + pi * sc.pair_step;
       const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
-      // Relative-position bias rows of this (head, query tile), times log2(e):
-      // one load per CTA and pair, shared by every window and both WGs.  Eight
-      // independent loads per thread are kept in flight.
+      // Relative-position bias tile of this (head, query tile) for the bias MMA:
+      // elem(elem(bias) / scale) -- rounded to the element type first, as the
+      // reference's .to(dtype) -- at rows < N and columns < N; -30000 in padded
+      // key columns (their scores drop out of the softmax: 2^(-30000 scale log2 e)
+      // is 0); 0 in padded query rows.  Each item is 8 consecutive columns of one
+      // row (one 16-byte core-matrix row); two items per thread are in flight.
       named_bar_sync(1, kSmThreads);
-      constexpr int kBatch = 8;
-      for (int e0 = tid_sm; e0 < kBM * NPAD; e0 += kBatch * kSmThreads) {
-        float vals[kBatch];
-        long long idx[kBatch];
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int e = e0 + u * kSmThreads;
-          const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
-          const int grow = mt * kBM + r;
-          const bool in = e < kBM * NPAD && grow < p.N && col < p.N;
-          idx[u] = -1;
-          vals[u] = 0.f;
-          if (in) {
-            if (p.bias_from_table) {
-              idx[u] = p.index[(long long)grow * p.index_stride + col];
-            } else {
-              vals[u] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
-            }
-          }
-        }
-        if (p.bias_from_table) {
+      {
+        constexpr int kItems = kBM * (NPAD / 8);
+        constexpr int kBatch = 2;
+        const float inv_scale = 1.f / p.scale;
+        const uint16_t pad_val = f32_to_elem<BF16>(-30000.f);
+        for (int i0 = tid_sm; i0 < kItems; i0 += kBatch * kSmThreads) {
+          float vals[kBatch][8];
+          long long idx[kBatch][8];
 #pragma unroll
           for (int u = 0; u < kBatch; ++u) {
-            if (idx[u] >= 0) {
-              vals[u] = p.table_f32
-                            ? static_cast<const float*>(p.table)[idx[u] * p.H + h]
-                            : to_f32<BF16>(static_cast<const uint16_t*>(p.table)[idx[u] * p.H + h]);
+            const int item = i0 + u * kSmThreads;
+            const int r = item % kBM, cg = item / kBM;
+            const int grow = mt * kBM + r;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int col = cg * 8 + e;
+              const bool in = item < kItems && grow < p.N && col < p.N;
+              idx[u][e] = -1;
+              vals[u][e] = 0.f;
+              if (in) {
+                if (p.bias_from_table) {
+                  idx[u][e] = p.index[(long long)grow * p.index_stride + col];
+                } else {
+                  vals[u][e] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
+                }
+              }
             }
           }
-        }
+          if (p.bias_from_table) {
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const int e = e0 + u * kSmThreads;
-          if (e < kBM * NPAD) {
-            const int r = e / NPAD, col = e - (e / NPAD) * NPAD;
-            // round to the element type first (as the reference's .to(dtype)), then scale
-            bias_s[r * C::BSTRIDE + col] =
-                f32_to_elem<BF16>(to_f32<BF16>(f32_to_elem<BF16>(vals[u])) * kLog2e);
+            for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (idx[u][e] >= 0) {
+                  vals[u][e] =
+                      p.table_f32
+                          ? static_cast<const float*>(p.table)[idx[u][e] * p.H + h]
+                          : to_f32<BF16>(
+                                static_cast<const uint16_t*>(p.table)[idx[u][e] * p.H + h]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int item = i0 + u * kSmThreads;
+            if (item >= kItems) continue;
+            const int r = item % kBM, cg = item / kBM;
+            const int grow = mt * kBM + r;
+            uint32_t wv[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              uint32_t pair = 0;
+#pragma unroll
+              for (int z = 0; z < 2; ++z) {
+                const int col = cg * 8 + e + z;
+                uint16_t v16;
+                if (grow >= p.N) v16 = 0;
+                else if (col >= p.N) v16 = pad_val;
+                else v16 = f32_to_elem<BF16>(to_f32<BF16>(f32_to_elem<BF16>(vals[u][e + z])) * inv_scale);
+                pair |= uint32_t(v16) << (16 * z);
+              }
+              wv[e / 2] = pair;
+            }
+            *reinterpret_cast<uint4*>(bias_s + cg * C::BIAS_CG_BYTES + 16 * r) =
+                make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         }
       }
+      fence_proxy_async_shared();  // bias tile -> tensor-core (async proxy) reads
       named_bar_sync(1, kSmThreads);
+      if (tid_sm == 0) mbar_arrive(bias_ready);
       if (!ok) continue;
 
       const int qrow = mt * kBM + row;
       const bool valid = qrow < p.N;
       const bool warp_live = (mt * kBM + quarter * 32) < p.N;  // uniform per warp
-      const uint16_t* brow = bias_s + row * C::BSTRIDE;
       uint32_t code_i = 0;
       if constexpr (MASK == kMaskAnalytic) code_i = valid ? token_code(p, qrow) : 0u;
 
@@ -546,17 +618,22 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         auto chunk = [&](auto w_tag, auto tail_tag, int c) -> bool {
           constexpr int W = decltype(w_tag)::value;
           constexpr bool kTail = decltype(tail_tag)::value;
+          (void)kTail;
           if (!mbar_wait(bar(w, kSF), n_sf & 1u, abort_flag)) return false;
           ++n_sf;
           tc_fence_after();
+          // P buffer of this chunk is free once the PV MMA of its previous use
+          // (two chunks ago) has completed.
+          const uint32_t pbuf = n_chunk & 1u;
+          const uint32_t puse_parity = ((n_chunk >> 1) & 1u) ^ 1u;
           if (!warp_live) {
             // No valid row in this warp: keep the barrier protocol, skip the math.
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(w, kSE));
-            if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) return false;
-            ++n_pe;
+            if (!mbar_wait(bar(w, kPE + int(pbuf)), puse_parity, abort_flag)) return false;
+            ++n_chunk;
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(w, kPF));
+            if (lane == 0) mbar_arrive(bar(w, kPF + int(pbuf)));
             return true;
           }
           uint32_t s[W];
@@ -567,37 +644,27 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(w, kSE));
 
-          // x = s * scale * log2(e) + bias * log2(e) (+ mask * log2(e)), in groups of 16
-          // keys so the bias words (16-byte shared loads) and mask words stay few.
-          const int valid_cols = p.N - c * kCH;
-          uint32_t odd = 0;
-          const uint32_t* wp = nullptr;
-          if constexpr (MASK == kMaskDense) {
-            // mask row slice: aligned 32-bit words, re-paired when the row starts on
-            // an odd element (word k holds elements 2k - odd and 2k - odd + 1)
-            const uintptr_t addr = reinterpret_cast<uintptr_t>(mrow + c * kCH);
-            odd = uint32_t(addr >> 1) & 1u;
-            wp = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
-          }
-          const bool dense_now = (MASK == kMaskDense) && use_dense && valid;
-          const uint32_t sel = odd ? 0x5432u : 0x3210u;
-          float x[W];
+          // v = q.k + bias/scale (the MMA added the bias tile), plus mask/scale for a
+          // dense mask; the log2-domain score is x = v * scale * log2(e).
+          float v[W];
 #pragma unroll
-          for (int g = 0; g < W / 16; ++g) {
-            uint32_t bw[8];
-            {
-              const uint4 v0 = *reinterpret_cast<const uint4*>(brow + c * kCH + 16 * g);
-              const uint4 v1 = *reinterpret_cast<const uint4*>(brow + c * kCH + 16 * g + 8);
-              bw[0] = v0.x; bw[1] = v0.y; bw[2] = v0.z; bw[3] = v0.w;
-              bw[4] = v1.x; bw[5] = v1.y; bw[6] = v1.z; bw[7] = v1.w;
-            }
-            if constexpr (MASK == kMaskDense) {
-              if (dense_now) {
+          for (int j = 0; j < W; ++j) v[j] = __uint_as_float(s[j]);
+          if constexpr (MASK == kMaskDense) {
+            if (use_dense && valid) {
+              // mask row slice: aligned 32-bit words, re-paired when the row starts on
+              // an odd element (word k holds elements 2k - odd and 2k - odd + 1)
+              const int valid_cols = p.N - c * kCH;
+              const uintptr_t addr = reinterpret_cast<uintptr_t>(mrow + c * kCH);
+              const uint32_t odd = uint32_t(addr >> 1) & 1u;
+              const uint32_t* wp = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+              const uint32_t sel = odd ? 0x5432u : 0x3210u;
+              const float2 inv2 = make_float2(1.f / p.scale, 1.f / p.scale);
+#pragma unroll
+              for (int g = 0; g < W / 16; ++g) {
                 uint32_t mw[9];
 #pragma unroll
                 for (int k = 0; k < 9; ++k) {
                   const int kk = 8 * g + k;
-                  // only the last chunk can run past the row end
                   if constexpr (kTail) {
                     mw[k] = (2 * kk - int(odd) < valid_cols) ? ldg_u32(wp + kk) : 0u;
                   } else {
@@ -605,18 +672,14 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
                   }
                 }
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                  bw[k] = fma_pairs_log2e<BF16>(__byte_perm(mw[k], mw[k + 1], sel), bw[k]);
+                for (int k = 0; k < 8; ++k) {
+                  const int j = 16 * g + 2 * k;
+                  const float2 r = __ffma2_rn(unpack2<BF16>(__byte_perm(mw[k], mw[k + 1], sel)),
+                                              inv2, make_float2(v[j], v[j + 1]));
+                  v[j] = r.x;
+                  v[j + 1] = r.y;
+                }
               }
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int j = 16 * g + 2 * k;
-              const float2 r = __ffma2_rn(
-                  make_float2(__uint_as_float(s[j]), __uint_as_float(s[j + 1])), c1,
-                  unpack2<BF16>(bw[k]));
-              x[j] = r.x;
-              x[j + 1] = r.y;
             }
           }
           if constexpr (MASK == kMaskAnalytic) {
@@ -630,29 +693,25 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               }
 #pragma unroll
               for (int j = 0; j < W; ++j) {
-                if ((pen >> j) & 1u) x[j] = kNegInf;
+                if ((pen >> j) & 1u) v[j] = kNegInf;
               }
             }
           }
-          if constexpr (kTail) {
+          // chunk maximum: four independent max3 chains, then a 3-op tree
+          float mq[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
-            for (int j = 0; j < W; ++j) {
-              if (j >= valid_cols) x[j] = kNegInf;
-            }
-          }
-          float mc = kNegInf;
-#pragma unroll
-          for (int j = 0; j < W; j += 2) mc = max3(mc, x[j], x[j + 1]);
+          for (int j = 0; j < W; j += 2) mq[(j >> 1) & 3] = max3(mq[(j >> 1) & 3], v[j], v[j + 1]);
+          const float mv = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+          const float mc = mv * c1.x;  // chunk maximum in the log2 domain
           const bool need = mc > m_ref + kRescaleLog2;  // m_ref = -inf: any finite mc
           const float new_ref = need ? mc : m_ref;
 
-          // P buffer free <=> PV of the previous chunk has completed (also makes O
-          // safe to rescale).
-          if (!mbar_wait(bar(w, kPE), (n_pe & 1u) ^ 1u, abort_flag)) return false;
-          ++n_pe;
-          tc_fence_after();
           const bool rescale = need && (m_ref != kNegInf);  // O holds sums vs the old m_ref
           if (c > 0 && __any_sync(0xffffffffu, rescale)) {
+            // O may be rescaled once the PV MMA of the previous chunk has completed.
+            const uint32_t prev = n_chunk - 1;
+            if (!mbar_wait(bar(w, kPE + int(prev & 1u)), (prev >> 1) & 1u, abort_flag)) return false;
+            tc_fence_after();
             const float f = rescale ? fast_ex2(m_ref - new_ref) : 1.f;
             uint32_t o[2 * kHD];
             tmem_ld32(tO, o);
@@ -661,21 +720,25 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             for (int i = 0; i < 2 * kHD; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
             tmem_st32(tO, o);
           }
+          if (!mbar_wait(bar(w, kPE + int(pbuf)), puse_parity, abort_flag)) return false;
+          tc_fence_after();
           m_ref = new_ref;
           const float mb = (m_ref == kNegInf) ? 0.f : m_ref;
           const float2 nmb = make_float2(-mb, -mb);
           uint32_t pk[W / 2];
 #pragma unroll
           for (int k = 0; k < W / 2; ++k) {
-            const float2 t = __fadd2_rn(make_float2(x[2 * k], x[2 * k + 1]), nmb);
-            pk[k] = ex2_pair<BF16>(t);
+            const float2 t = __ffma2_rn(make_float2(v[2 * k], v[2 * k + 1]), c1, nmb);
+            pk[k] = pack2<BF16>(fast_ex2(t.x), fast_ex2(t.y));
           }
-          tmem_st16(tP, pk);
-          if constexpr (W > 32) tmem_st16(tP + 16, pk + 16);
+          const uint32_t tPb = tP + pbuf * uint32_t(kCH / 2);
+          tmem_st16(tPb, pk);
+          if constexpr (W > 32) tmem_st16(tPb + 16, pk + 16);
+          ++n_chunk;
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(w, kPF));
+          if (lane == 0) mbar_arrive(bar(w, kPF + int(pbuf)));
           return true;
         };
 
@@ -818,6 +881,8 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.head_dim != kHD) return set_error(kErrUnsupported, "fused_swin_attention requires head_dim 16");
   if (a.N < 1 || a.N > 384) return set_error(kErrUnsupported, "fused_swin_attention supports 1 <= N <= 384");
   if (a.B < 0 || a.H < 1) return set_error(kErrInvalid, "B must be >= 0 and H >= 1");
+  if (!(a.scale > 0.f) || !(a.scale < 1e30f))
+    return set_error(kErrUnsupported, "fused_swin_attention requires a finite scale > 0");
   if (a.B == 0) return kOk;
   if (a.B > 0x7fffffff || a.H > 0xffff) return set_error(kErrInvalid, "B or H too large");
   if (!a.q || !a.k || !a.v || !a.out) return set_error(kErrInvalid, "null tensor pointer");

@@ -199,7 +199,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 // ------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading and
 // stride byte offsets (all >> 4), version 1 at bits 46-47, layout at 61-63.
-enum : uint32_t { kLayoutSW32 = 6 };
+enum : uint32_t { kLayoutNone = 0, kLayoutSW32 = 6 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
                                               uint32_t sbo_bytes, uint32_t layout) {
