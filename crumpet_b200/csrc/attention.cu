@@ -6,33 +6,32 @@
 // torch-ext/crumpet/fused_attention.py:48-146 (eager form: MONAI WindowAttention,
 // as described in torch-ext/crumpet/monai_patch.py:117-198).
 //
-// Design (one persistent CTA per SM, 12 warps):
-//   * A tile is 128 query rows of one (window, head).  Two independent tile
-//     pipelines ("work groups", WG) run per CTA; each has a TMA warp, an MMA
-//     warp and 4 softmax warps (one thread per query row = one TMEM lane).
-//   * TMA loads Q (128 rows) and all K, V rows of the (window, head) into
-//     shared memory with 32-byte swizzle; rows past N are zero-filled by TMA.
-//     Two address layouts share the kernel: separate q/k/v [B, H, N, 16]
-//     tensors, or the packed qkv Linear output [B, N, 3, H, 16].
-//   * The key axis is processed in chunks of 64.  The MMA warp issues
-//     S_c = Q K_c^T (tcgen05.mma, M=128, K=16, fp32 accumulators in TMEM); the
-//     softmax warps pull S_c into registers, add the relative-position bias
-//     (a shared-memory tile per (head, query tile), reused for every window of
-//     the CTA) and the mask, take the chunk maximum m_c, write
-//     P_c = exp(x - m_c) back to TMEM as fp16/bf16, and the MMA warp
-//     accumulates O_c = P_c V_c with P read from TMEM.  Every chunk keeps its
-//     own O_c, m_c and l_c = sum(P_c) (m_c, l_c parked in TMEM), so nothing is
-//     rescaled inside the loop; the epilogue combines them exactly:
-//       out = sum_c e^(m_c - m) O_c / sum_c e^(m_c - m) l_c,  m = max_c m_c.
-//   * Bias: a dense [H, N, N] tensor, or gathered in-kernel from MONAI's
+// Design (one persistent CTA per SM, 16 warps):
+//   * A tile is 128 query rows of one (window, head).  Three independent tile
+//     pipelines ("work groups", WG) run per CTA, each with an MMA-issuing warp and
+//     4 softmax warps (one thread per query row = one TMEM lane); one TMA warp
+//     feeds all three through a 4-stage shared-memory ring.
+//   * TMA loads Q (128 rows) and all K, V rows of the (window, head) with 32-byte
+//     swizzle; rows past N are zero-filled.  Two address layouts share the
+//     kernel: separate q/k/v [B, H, N, 16] tensors, or the packed qkv Linear
+//     output [B, N, 3, H, 16].
+//   * Keys are processed in chunks of 64.  The MMA warp computes the chunk's
+//     scores in TMEM with tcgen05.mma (M=128, K=16, fp32 accumulation) and then
+//     adds the relative-position bias on the tensor cores as well: the bias tile
+//     of the (head, query tile), stored as elem(bias)/scale in shared memory,
+//     multiplied by a 16x16 identity (one exact product per sum).  So S holds
+//     q.k + bias/scale; padded key columns carry -30000 and drop out.
+//   * Softmax warps pull S into registers, add a dense mask (global loads, read
+//     only for windows flagged in `boundary`) or the analytic shifted-window mask
+//     (entries whose roll-side codes differ on a "last window" axis become -inf,
+//     the exact limit of the reference's -100), take the chunk maximum, and
+//     write P = 2^(x - m_ref) (x = S * scale * log2 e) as fp16/bf16 into one of
+//     two TMEM P buffers.  m_ref is a lazy row maximum: it moves only when a
+//     chunk exceeds it by more than 8 (P <= 2^8), and then O is rescaled in TMEM.
+//     The MMA warp accumulates [O | row sum] += P [V | 1] from TMEM, and the
+//     epilogue writes O / row sum.
+//   * Bias source: a dense [H, N, N] tensor, or gathered in-kernel from MONAI's
 //     relative-position table [T, H] and index [Nc, Nc] (sliced [:N, :N]).
-//   * Mask: none; dense [nW, N, N] (window b uses mask[b % nW], rows read only
-//     for windows flagged in `boundary`), read with aligned 32-bit loads and
-//     added to the bias in half2; or analytic: the shifted-window mask
-//     recomputed on chip from the window geometry (a 3-bit roll-side code per
-//     token and a 3-bit "last window on this axis" flag per window; entries
-//     whose codes differ on a flagged axis get -inf, the exact limit of the
-//     reference's -100: e^-100 underflows to 0 in fp32 either way).
 //   * Work: CTAs are split into groups, one per (head, query-tile) pair, and
 //     walk the windows in lock step, so the CTAs that need the same K/V rows
 //     (the other query tiles and heads of a window) read them close together
