@@ -220,6 +220,30 @@ int crumpet_unshift_unpartition_crop_3d(void* output, const void* windows, const
                                          static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_roi_gather(void* out, int out_dtype, const void* volume, int in_dtype, int64_t C,
+                       int64_t D, int64_t H, int64_t W, const int64_t* roi_starts, int64_t n,
+                       int64_t rd, int64_t rh, int64_t rw, void* stream) {
+  if (int e = check_dtype(out_dtype)) return e;
+  if (int e = check_dtype(in_dtype)) return e;
+  return launch_roi_gather(out, out_dtype, volume, in_dtype, C, D, H, W, roi_starts, n, rd, rh,
+                           rw, static_cast<cudaStream_t>(stream));
+}
+
+int crumpet_roi_accumulate(float* acc, const void* pred, int pred_dtype, int64_t classes,
+                           int64_t D, int64_t H, int64_t W, const int64_t* roi_starts, int64_t n,
+                           int64_t rd, int64_t rh, int64_t rw, void* stream) {
+  if (int e = check_dtype(pred_dtype)) return e;
+  return launch_roi_accumulate(acc, pred, pred_dtype, classes, D, H, W, roi_starts, n, rd, rh, rw,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int crumpet_roi_argmax(uint8_t* labels, float* logits, const float* acc, const float* count_d,
+                       const float* count_h, const float* count_w, int64_t classes, int64_t D,
+                       int64_t H, int64_t W, void* stream) {
+  return launch_roi_argmax(labels, logits, acc, count_d, count_h, count_w, classes, D, H, W,
+                           static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_device_status(int clear) {
   const int v = read_device_error(clear != 0);
   if (v < 0) return set_error(kErrCuda, "could not read the device error word");

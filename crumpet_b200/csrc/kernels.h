@@ -45,6 +45,19 @@ int launch_unshift_unpartition_crop(void* out, const void* windows, const void* 
                                     int64_t C, const int64_t* ws, const int64_t* ss,
                                     cudaStream_t stream);
 
+// Sliding-window ROI inference: crop a batch of ROIs, accumulate their predictions,
+// normalise by the ROI count and take the arg-max.  `starts` is a HOST array of
+// n (z, y, x) triples (n <= 64), passed to the kernels by value.
+int launch_roi_gather(void* out, int out_dtype, const void* vol, int in_dtype, int64_t C,
+                      int64_t D, int64_t H, int64_t W, const int64_t* starts, int64_t n,
+                      int64_t rd, int64_t rh, int64_t rw, cudaStream_t stream);
+int launch_roi_accumulate(float* acc, const void* pred, int pred_dtype, int64_t classes,
+                          int64_t D, int64_t H, int64_t W, const int64_t* starts, int64_t n,
+                          int64_t rd, int64_t rh, int64_t rw, cudaStream_t stream);
+int launch_roi_argmax(uint8_t* labels, float* logits, const float* acc, const float* count_d,
+                      const float* count_h, const float* count_w, int64_t classes, int64_t D,
+                      int64_t H, int64_t W, cudaStream_t stream);
+
 // Window attention: out = softmax(q k^T * scale + bias[h] + mask[b mod nmask]) v.
 struct AttnArgs {
   // q/k/v addressing: element (b, h, n, d) lives at

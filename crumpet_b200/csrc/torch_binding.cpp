@@ -247,6 +247,80 @@ void unshift_unpartition_crop_3d(at::Tensor& output, const at::Tensor& windows,
                                                ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
 }
 
+std::vector<int64_t> roi_list(at::IntArrayRef starts, at::IntArrayRef roi) {
+  TORCH_CHECK(roi.size() == 3, "roi takes three values");
+  TORCH_CHECK(starts.size() % 3 == 0, "starts must hold (z, y, x) triples");
+  return std::vector<int64_t>(starts.begin(), starts.end());
+}
+
+void roi_gather(at::Tensor& out, const at::Tensor& volume, at::IntArrayRef starts,
+                at::IntArrayRef roi) {
+  check_cuda_contig(out, "out");
+  check_cuda_contig(volume, "volume");
+  TORCH_CHECK(volume.dim() == 4, "volume must have shape [C, D, H, W]");
+  const auto s = roi_list(starts, roi);
+  const int64_t n = int64_t(s.size() / 3);
+  TORCH_CHECK(out.dim() == 5 && out.size(0) == n && out.size(1) == volume.size(0) &&
+                  out.size(2) == roi[0] && out.size(3) == roi[1] && out.size(4) == roi[2],
+              "out must have shape [n, C, rd, rh, rw]");
+  const c10::cuda::CUDAGuard guard(volume.device());
+  check_rc(crumpet_roi_gather(out.data_ptr(), dtype_code(out), volume.data_ptr(),
+                              dtype_code(volume), volume.size(0), volume.size(1), volume.size(2),
+                              volume.size(3), s.data(), n, roi[0], roi[1], roi[2],
+                              cur_stream(volume)));
+}
+
+void roi_accumulate(at::Tensor& acc, const at::Tensor& pred, at::IntArrayRef starts,
+                    at::IntArrayRef roi) {
+  check_cuda_contig(acc, "acc");
+  check_cuda_contig(pred, "pred");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.dim() == 4,
+              "acc must be a float32 [classes, D, H, W] tensor");
+  const auto s = roi_list(starts, roi);
+  const int64_t n = int64_t(s.size() / 3);
+  TORCH_CHECK(pred.dim() == 5 && pred.size(0) == n && pred.size(1) == acc.size(0) &&
+                  pred.size(2) == roi[0] && pred.size(3) == roi[1] && pred.size(4) == roi[2],
+              "pred must have shape [n, classes, rd, rh, rw]");
+  const c10::cuda::CUDAGuard guard(acc.device());
+  check_rc(crumpet_roi_accumulate(acc.data_ptr<float>(), pred.data_ptr(), dtype_code(pred),
+                                  acc.size(0), acc.size(1), acc.size(2), acc.size(3), s.data(), n,
+                                  roi[0], roi[1], roi[2], cur_stream(acc)));
+}
+
+void roi_argmax_impl(uint8_t* labels, float* logits, const at::Tensor& acc,
+                     const at::Tensor& count_d, const at::Tensor& count_h,
+                     const at::Tensor& count_w) {
+  check_cuda_contig(acc, "acc");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.dim() == 4,
+              "acc must be a float32 [classes, D, H, W] tensor");
+  const at::Tensor* counts[3] = {&count_d, &count_h, &count_w};
+  for (int a = 0; a < 3; ++a) {
+    check_cuda_contig(*counts[a], "count");
+    TORCH_CHECK(counts[a]->scalar_type() == at::kFloat && counts[a]->numel() == acc.size(1 + a),
+                "counts must be float32 vectors of D, H and W elements");
+  }
+  const c10::cuda::CUDAGuard guard(acc.device());
+  check_rc(crumpet_roi_argmax(labels, logits, acc.data_ptr<float>(), count_d.data_ptr<float>(),
+                              count_h.data_ptr<float>(), count_w.data_ptr<float>(), acc.size(0),
+                              acc.size(1), acc.size(2), acc.size(3), cur_stream(acc)));
+}
+
+void roi_argmax(at::Tensor& labels, const at::Tensor& acc, const at::Tensor& count_d,
+                const at::Tensor& count_h, const at::Tensor& count_w) {
+  check_cuda_contig(labels, "labels");
+  TORCH_CHECK(labels.scalar_type() == at::kByte && labels.numel() == acc.numel() / acc.size(0),
+              "labels must be a uint8 [D, H, W] tensor");
+  roi_argmax_impl(labels.data_ptr<uint8_t>(), nullptr, acc, count_d, count_h, count_w);
+}
+
+void roi_normalize(at::Tensor& logits, const at::Tensor& acc, const at::Tensor& count_d,
+                   const at::Tensor& count_h, const at::Tensor& count_w) {
+  check_cuda_contig(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.sizes() == acc.sizes(),
+              "logits must be a float32 tensor shaped like acc");
+  roi_argmax_impl(nullptr, logits.data_ptr<float>(), acc, count_d, count_h, count_w);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(crumpet_ops, ops) {
@@ -286,6 +360,15 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "unshift_unpartition_crop_3d(Tensor! output, Tensor windows, Tensor? residual, int B, int D, "
       "int H, int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
       kTags);
+  ops.def("roi_gather(Tensor! out, Tensor volume, int[] starts, int[] roi) -> ()", kTags);
+  ops.def("roi_accumulate(Tensor! acc, Tensor pred, int[] starts, int[] roi) -> ()", kTags);
+  ops.def(
+      "roi_argmax(Tensor! labels, Tensor acc, Tensor count_d, Tensor count_h, Tensor count_w) -> ()",
+      kTags);
+  ops.def(
+      "roi_normalize(Tensor! logits, Tensor acc, Tensor count_d, Tensor count_h, "
+      "Tensor count_w) -> ()",
+      kTags);
 }
 
 TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
@@ -298,4 +381,8 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
   ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
+  ops.impl("roi_gather", &roi_gather);
+  ops.impl("roi_accumulate", &roi_accumulate);
+  ops.impl("roi_argmax", &roi_argmax);
+  ops.impl("roi_normalize", &roi_normalize);
 }

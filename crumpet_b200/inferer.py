@@ -7,6 +7,12 @@ last ROI of every axis clamped to end at the volume edge, ``sw_batch_size``
 ROIs per forward, predictions summed into a float32 accumulator and divided
 by the per-voxel ROI count.
 
+On CUDA the crop, accumulate and normalise/arg-max passes run as crumpet_b200
+kernels (``roi_gather``, ``roi_accumulate``, ``roi_argmax`` / ``roi_normalize``):
+one launch per ROI batch instead of a copy, a cast and an add per ROI, with the
+same fp32 additions in the same order, so the results are bit-identical to the
+eager loop; CPU tensors take the eager torch path.
+
 Multi-GPU: one process per GPU.  ROI batches are dealt round-robin to ranks
 (rank r runs batches r, r + world, ...); each rank accumulates its own
 predictions, and the only collective is one NCCL sum-reduce of the
@@ -22,6 +28,9 @@ from typing import Sequence
 import torch
 import torch.distributed as dist
 
+from . import _ops
+from . import profiling as _prof
+
 
 def axis_starts(size: int, roi: int, overlap: float) -> list[int]:
     """Start offsets of the ROIs along one axis."""
@@ -35,6 +44,15 @@ def axis_starts(size: int, roi: int, overlap: float) -> list[int]:
 def roi_grid(spatial: Sequence[int], roi: Sequence[int], overlap: float) -> list[tuple[int, int, int]]:
     starts = [axis_starts(s, r, overlap) for s, r in zip(spatial, roi)]
     return list(itertools.product(*starts))
+
+
+def axis_counts(size: int, roi: int, overlap: float) -> list[float]:
+    """Number of ROIs covering each coordinate of one axis (the count map factorises)."""
+    counts = [0.0] * size
+    for s in axis_starts(size, roi, overlap):
+        for i in range(s, min(s + roi, size)):
+            counts[i] += 1.0
+    return counts
 
 
 class SlidingWindowInferer:
@@ -79,6 +97,28 @@ class SlidingWindowInferer:
             self._count_cache[key] = cnt
         return self._count_cache[key]
 
+    def _axis_counts(self, spatial, device) -> list[torch.Tensor]:
+        key = ("axes", tuple(spatial), device)
+        if key not in self._count_cache:
+            self._count_cache[key] = [
+                torch.tensor(axis_counts(s, r, self.overlap), dtype=torch.float32, device=device)
+                for s, r in zip(spatial, self.roi)]
+        return self._count_cache[key]
+
+    def _gather(self, volume: torch.Tensor, batch) -> torch.Tensor:
+        rd, rh, rw = self.roi
+        if not volume.is_cuda:
+            return torch.cat([volume[..., z:z + rd, y:y + rh, x:x + rw] for z, y, x in batch])
+        # under autocast the first convolutions cast their input to the autocast
+        # dtype; the crop writes that dtype directly (same rounding)
+        dtype = self.autocast_dtype if self.autocast_dtype is not None else volume.dtype
+        out = torch.empty((len(batch), volume.shape[1], rd, rh, rw), dtype=dtype,
+                          device=volume.device)
+        _ops.require().roi_gather(out, volume[0].contiguous(), [v for st in batch for v in st],
+                                  list(self.roi))
+        _prof.count("roi_gather")
+        return out
+
     @torch.no_grad()
     def accumulate(self, volume: torch.Tensor) -> tuple[torch.Tensor, int]:
         """This rank's summed predictions [1, classes, D, H, W] (fp32) and its ROI count."""
@@ -87,35 +127,57 @@ class SlidingWindowInferer:
         acc = torch.zeros((1, self.num_classes, *spatial), dtype=torch.float32, device=volume.device)
         done = 0
         for batch in self.my_batches(spatial):
-            window = torch.cat([volume[..., z:z + rd, y:y + rh, x:x + rw] for z, y, x in batch])
+            window = self._gather(volume, batch)
             if self.autocast_dtype is not None:
                 with torch.autocast("cuda", dtype=self.autocast_dtype):
                     pred = self.model(window)
             else:
                 pred = self.model(window)
-            for i, (z, y, x) in enumerate(batch):
-                acc[0, :, z:z + rd, y:y + rh, x:x + rw] += pred[i].float()
+            if volume.is_cuda:
+                _ops.require().roi_accumulate(acc[0], pred.contiguous(),
+                                              [v for st in batch for v in st], list(self.roi))
+                _prof.count("roi_accumulate")
+            else:
+                for i, (z, y, x) in enumerate(batch):
+                    acc[0, :, z:z + rd, y:y + rh, x:x + rw] += pred[i].float()
             done += len(batch)
         return acc, done
 
-    @torch.no_grad()
-    def logits(self, volume: torch.Tensor) -> torch.Tensor | None:
-        """Averaged logits on rank 0 (None on other ranks)."""
+    def _reduced(self, volume: torch.Tensor) -> torch.Tensor | None:
         acc, _ = self.accumulate(volume)
         if self.world > 1:
             dist.reduce(acc, dst=0, op=dist.ReduceOp.SUM, group=self.group)
             if self.rank != 0:
                 return None
-        return acc / self._count_map(tuple(acc.shape[2:]), acc.device)
+        return acc
+
+    @torch.no_grad()
+    def logits(self, volume: torch.Tensor) -> torch.Tensor | None:
+        """Averaged logits on rank 0 (None on other ranks)."""
+        acc = self._reduced(volume)
+        if acc is None:
+            return None
+        if not acc.is_cuda:
+            return acc / self._count_map(tuple(acc.shape[2:]), acc.device)
+        out = torch.empty_like(acc)
+        _ops.require().roi_normalize(out[0], acc[0], *self._axis_counts(acc.shape[2:], acc.device))
+        _prof.count("roi_normalize")
+        return out
 
     @torch.no_grad()
     def segment(self, volume: torch.Tensor) -> torch.Tensor | None:
-        """uint8 label map [D, H, W] on rank 0 (None on other ranks)."""
-        logits = self.logits(volume)
-        if logits is None:
+        """uint8 label map [D, H, W] on rank 0 (None on other ranks): the arg-max of
+        the averaged logits."""
+        acc = self._reduced(volume)
+        if acc is None:
             return None
-        # The positive count normaliser does not change the arg-max.
-        return logits[0].argmax(dim=0).to(torch.uint8)
+        if not acc.is_cuda:
+            logits = acc / self._count_map(tuple(acc.shape[2:]), acc.device)
+            return logits[0].argmax(dim=0).to(torch.uint8)
+        labels = torch.empty(acc.shape[2:], dtype=torch.uint8, device=acc.device)
+        _ops.require().roi_argmax(labels, acc[0], *self._axis_counts(acc.shape[2:], acc.device))
+        _prof.count("roi_argmax")
+        return labels
 
 
 def synthetic_volume(shape=(1, 1, 512, 512, 224), seed: int = 0) -> torch.Tensor:

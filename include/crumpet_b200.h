@@ -195,6 +195,46 @@ CRUMPET_API int crumpet_unshift_unpartition_crop_3d(void* output, const void* wi
                                                     void* stream);
 
 /*
+ * Sliding-window ROI inference around the network forward.  The reference drives
+ * its patched network with MONAI's sliding_window_inference (a third-party
+ * Python function, called at torch-ext/crumpet/demo_btcv.py:98-129 with
+ * mode="constant"); these three entry points replace its crop, accumulate and
+ * normalise/arg-max passes.  `roi_starts` is a HOST array of n (z, y, x)
+ * triples, n <= 64 (one ROI batch), copied into the kernel parameters; every
+ * ROI must lie inside the D x H x W volume.
+ *
+ * crumpet_roi_gather: out[i] = volume[:, z_i:z_i+rd, y_i:y_i+rh, x_i:x_i+rw]
+ *   volume [C, D, H, W] (in_dtype)  ->  out [n, C, rd, rh, rw] (out_dtype, one
+ *   rounding).  Replaces the per-ROI slicing + torch.cat of the inferer.
+ */
+CRUMPET_API int crumpet_roi_gather(void* out, int out_dtype, const void* volume, int in_dtype,
+                                   int64_t C, int64_t D, int64_t H, int64_t W,
+                                   const int64_t* roi_starts, int64_t n, int64_t rd, int64_t rh,
+                                   int64_t rw, void* stream);
+
+/*
+ * crumpet_roi_accumulate: acc[:, ROI i] += float(pred[i]) for i = 0 .. n-1 in
+ * order (the same fp32 additions, in the same order, as a per-ROI loop).
+ *   acc [classes, D, H, W] fp32, pred [n, classes, rd, rh, rw] (pred_dtype).
+ */
+CRUMPET_API int crumpet_roi_accumulate(float* acc, const void* pred, int pred_dtype,
+                                       int64_t classes, int64_t D, int64_t H, int64_t W,
+                                       const int64_t* roi_starts, int64_t n, int64_t rd,
+                                       int64_t rh, int64_t rw, void* stream);
+
+/*
+ * crumpet_roi_argmax: per voxel v, logits[c, v] = acc[c, v] / count(v) with
+ * count(d, h, w) = count_d[d] * count_h[h] * count_w[w] (ROIs covering the voxel
+ * along each axis), labels[v] = first c maximising logits[c, v] (NaN is the
+ * maximum, as torch.argmax).  labels (uint8 [D, H, W]) and logits (fp32
+ * [classes, D, H, W]) may each be NULL.  classes <= 256.
+ */
+CRUMPET_API int crumpet_roi_argmax(uint8_t* labels, float* logits, const float* acc,
+                                   const float* count_d, const float* count_h,
+                                   const float* count_w, int64_t classes, int64_t D, int64_t H,
+                                   int64_t W, void* stream);
+
+/*
  * Device error word: non-zero once a kernel of this library gave up on a
  * bounded wait (it then drained its work, freed its tensor memory and
  * returned without completing its output).  Reading it synchronises with the

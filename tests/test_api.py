@@ -232,3 +232,34 @@ def test_block_fusion_wrappers_validate_and_have_no_cpu_path():
         crumpet.unshift_unpartition_crop_3d(win, 1, 13, 10, 9, 48, (7, 7, 7), (3, 3, 3))
     out = crumpet.unshift_unpartition_crop_3d(win.to("meta"), 1, 13, 10, 9, 48, (7, 7, 7), (3, 3, 3))
     assert out.shape == (1, 13, 10, 9, 48)
+
+
+def test_roi_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    starts = (ctypes.c_int64 * 6)(0, 0, 0, 10, 0, 0)
+    # ROI past the volume end, too many ROIs, null pointers, empty batch
+    rc = lib.crumpet_roi_gather(null, 1, null, 0, 1, 100, 96, 96, starts, 2, 96, 96, 96, null)
+    assert rc == 1 and "outside" in _ops.last_error()
+    rc = lib.crumpet_roi_gather(null, 1, null, 0, 1, 200, 96, 96, starts, 65, 96, 96, 96, null)
+    assert rc == 1 and "64" in _ops.last_error()
+    rc = lib.crumpet_roi_gather(null, 1, null, 0, 1, 200, 96, 96, starts, 2, 96, 96, 96, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = lib.crumpet_roi_gather(null, 1, null, 0, 1, 200, 96, 96, starts, 0, 96, 96, 96, null)
+    assert rc == 0
+    rc = lib.crumpet_roi_accumulate(null, null, 1, 14, 200, 96, 96, starts, 2, 96, 96, 96, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = lib.crumpet_roi_accumulate(null, null, 7, 14, 200, 96, 96, starts, 2, 96, 96, 96, null)
+    assert rc == 1 and "float32" in _ops.last_error()
+    rc = lib.crumpet_roi_argmax(null, null, null, null, null, null, 300, 8, 8, 8, null)
+    assert rc == 1 and "classes" in _ops.last_error()
+
+
+def test_axis_counts_factorise_the_count_map():
+    from crumpet_b200.inferer import SlidingWindowInferer, axis_counts
+
+    inf = SlidingWindowInferer(None, (8, 6, 5), 2, 0.5, 3)
+    spatial = (20, 13, 11)
+    full = inf._count_map(spatial, torch.device("cpu"))[0, 0]
+    cd, ch, cw = (torch.tensor(axis_counts(s, r, 0.5)) for s, r in zip(spatial, (8, 6, 5)))
+    assert torch.equal(full, cd[:, None, None] * ch[None, :, None] * cw[None, None, :])
