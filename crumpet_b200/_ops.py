@@ -84,6 +84,8 @@ def capi() -> ctypes.CDLL:
         lib.crumpet_last_error.restype = ctypes.c_char_p
         lib.crumpet_abi_version.argtypes = []
         lib.crumpet_abi_version.restype = i32
+        lib.crumpet_test_stall_attention.argtypes = [i32]
+        lib.crumpet_test_stall_attention.restype = i32
         lib.crumpet_device_status.argtypes = [i32]
         lib.crumpet_device_status.restype = i32
         _capi = lib

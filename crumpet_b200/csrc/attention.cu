@@ -40,6 +40,7 @@
 // Every wait is bounded (2 s of %globaltimer); on expiry the kernel records an
 // error in g_device_error, drains its in-flight copies and MMAs, frees TMEM and
 // returns.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <type_traits>
@@ -120,6 +121,9 @@ struct KParams {
   long long out_sb, out_sh, out_sn;
   int B, H, N, MT, P;
   float scale;
+  // Test hook (crumpet_test_stall_attention): the TMA warp issues no loads, so every
+  // consumer wait runs into its time limit and the bounded-wait error path runs.
+  int stall_loads;
 };
 
 // Work list of one CTA: `pair_count` (head, query-tile) pairs starting at
@@ -352,7 +356,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     if (warp == 0) {
       // ------------------------------------------------------------ TMA warp
       // Tiles of the CTA in order k = 0, 1, ...; tile k uses ring stage k % kStages.
-      if (lane == 0) {
+      if (lane == 0 && !p.stall_loads) {
         tma_prefetch_map(&tq);
         tma_prefetch_map(&tk);
         tma_prefetch_map(&tv);
@@ -872,7 +876,11 @@ int dispatch_npad(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& t
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+std::atomic<int> g_test_stall{0};
+
 }  // namespace
+
+int set_attention_test_stall(int enable) { return g_test_stall.exchange(enable ? 1 : 0); }
 
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.dtype != kF16 && a.dtype != kBF16)
@@ -938,6 +946,7 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.MT = int((a.N + kBM - 1) / kBM);
   kp.P = kp.H * kp.MT;
   kp.scale = a.scale;
+  kp.stall_loads = g_test_stall.load(std::memory_order_relaxed);
   if (!a.analytic) {
     // keep the analytic-mask geometry harmless when unused
     kp.nwd = kp.nwh = kp.nww = 1;

@@ -244,6 +244,8 @@ int crumpet_roi_argmax(uint8_t* labels, float* logits, const float* acc, const f
                            static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_test_stall_attention(int enable) { return set_attention_test_stall(enable); }
+
 int crumpet_device_status(int clear) {
   const int v = read_device_error(clear != 0);
   if (v < 0) return set_error(kErrCuda, "could not read the device error word");

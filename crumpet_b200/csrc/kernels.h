@@ -88,6 +88,10 @@ struct AttnArgs {
 
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream);
 
+// Test hook: while enabled, attention launches issue no TMA loads (every wait in
+// the kernel expires after its time limit).  Returns the previous setting.
+int set_attention_test_stall(int enable);
+
 // Device-side error word written by kernels whose bounded waits expired.
 // Reads it (synchronously); clears it when `clear`.  Returns -1 on failure.
 int read_device_error(bool clear);

@@ -244,6 +244,16 @@ CRUMPET_API int crumpet_roi_argmax(uint8_t* labels, float* logits, const float* 
  */
 CRUMPET_API int crumpet_device_status(int clear);
 
+/*
+ * Test hook for the bounded-wait error path (no reference counterpart: the
+ * reference kernels contain no waits).  While enabled (enable != 0), attention
+ * launches issue no TMA loads, so every wait of the kernel runs into its 2 s
+ * limit; the kernel then drains, frees its tensor memory, returns and sets the
+ * device error word read by crumpet_device_status.  Returns the previous
+ * setting.  Process-wide; for tests only.
+ */
+CRUMPET_API int crumpet_test_stall_attention(int enable);
+
 #ifdef __cplusplus
 }
 #endif
