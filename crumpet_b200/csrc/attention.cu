@@ -128,7 +128,7 @@ struct KParams {
 
 // Work list of one CTA: `pair_count` (head, query-tile) pairs starting at
 // pair_begin with stride pair_step; inside each pair the windows
-// win_begin, win_begin + win_step, ...  Window k of that list goes to WG k % 2.
+// win_begin, win_begin + win_step, ...  Tile k of the CTA (in that order) goes to WG k % kNumWG.
 struct Sched {
   int pair_begin, pair_step, pair_count, win_begin, win_step;
 };
@@ -185,36 +185,6 @@ __device__ __forceinline__ float to_f32(uint16_t h) {
   } else {
     return __half2float(__ushort_as_half(h));
   }
-}
-
-// m * log2(e) + b on a pair of 16-bit values (mask folded into the scaled bias).
-template <bool BF16>
-__device__ __forceinline__ uint32_t fma_pairs_log2e(uint32_t m, uint32_t b) {
-  if constexpr (BF16) {
-    const __nv_bfloat162 l2e = __floats2bfloat162_rn(kLog2e, kLog2e);
-    __nv_bfloat162 r = __hfma2(*reinterpret_cast<const __nv_bfloat162*>(&m), l2e,
-                               *reinterpret_cast<const __nv_bfloat162*>(&b));
-    return *reinterpret_cast<uint32_t*>(&r);
-  } else {
-    const __half2 l2e = __floats2half2_rn(kLog2e, kLog2e);
-    __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&m), l2e, *reinterpret_cast<const __half2*>(&b));
-    return *reinterpret_cast<uint32_t*>(&r);
-  }
-}
-
-// 2^t for a pair, computed by the SFU in packed 16-bit form (two per op) and
-// returned packed, ready to be the P operand of the PV MMA.
-template <bool BF16>
-__device__ __forceinline__ uint32_t ex2_pair(float2 t) {
-  uint32_t r;
-  if constexpr (BF16) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(t.x, t.y);
-    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
-  } else {
-    __half2 v = __floats2half2_rn(t.x, t.y);
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
-  }
-  return r;
 }
 
 template <bool BF16>
@@ -496,7 +466,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     const uint32_t tP = tmem_base + lane_off + w * kTmemPerWG + C::TM_P;
     const uint32_t tO = tmem_base + lane_off + w * kTmemPerWG + C::TM_O;
     const float kNegInf = __int_as_float(0xff800000);
-    // scores are carried in the log2 domain: x = (q.k * scale + bias + mask) * log2(e)
+    // S holds q.k + bias/scale; the log2-domain score is x = (S + mask/scale) * scale * log2(e)
     const float2 c1 = make_float2(p.scale * kLog2e, p.scale * kLog2e);
     uint32_t n_sf = 0, n_of = 0;
     uint32_t n_chunk = 0;  // chunks of this WG so far: P buffer n_chunk & 1, its use n_chunk >> 1
