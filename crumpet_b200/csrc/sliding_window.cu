@@ -79,8 +79,31 @@ roi_gather_kernel(TOut* __restrict__ out, const TIn* __restrict__ vol, const Roi
   }
 }
 
-// One thread per (class, voxel) of the batch's bounding box [bz0, bz0 + bd) x ...
+// Four consecutive predictions as fp32 (the pointer is aligned to 4 elements).
 template <typename TP>
+__device__ __forceinline__ float4 load4_f32(const TP* p);
+template <>
+__device__ __forceinline__ float4 load4_f32<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+template <>
+__device__ __forceinline__ float4 load4_f32<__half>(const __half* p) {
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <>
+__device__ __forceinline__ float4 load4_f32<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(p));
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u),
+                     __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xFFFF0000u));
+}
+
+// One thread per (class, VX consecutive x voxels) of the batch's bounding box.  With
+// VX = 4 every ROI x start, the ROI width and the box are multiples of 4, so the
+// four voxels share their ROI membership and move as one 16-byte accumulator vector.
+template <typename TP, int VX>
 __global__ void __launch_bounds__(kThreads)
 roi_accumulate_kernel(float* __restrict__ acc, const TP* __restrict__ pred, const RoiList rois,
                       uint32_t classes, uint32_t H, uint32_t W, uint64_t plane, int bz0,
@@ -92,25 +115,41 @@ roi_accumulate_kernel(float* __restrict__ acc, const TP* __restrict__ pred, cons
   f_bw.divmod(o, t, bx);
   f_bh.divmod(t, t2, by);
   f_bd.divmod(t2, c, bz);
-  const int z = bz0 + int(bz), y = by0 + int(by), x = bx0 + int(bx);
+  const int z = bz0 + int(bz), y = by0 + int(by), x = bx0 + int(bx) * VX;
   const uint32_t roi_vol = uint32_t(rois.rd) * rois.rh * rois.rw;
   float* a = acc + uint64_t(c) * plane + (uint64_t(z) * H + y) * W + x;
-  float sum = 0.f;
+  float sum[VX];
   bool touched = false;
   for (int i = 0; i < rois.n; ++i) {
     const int lz = z - rois.z[i], ly = y - rois.y[i], lx = x - rois.x[i];
     if (unsigned(lz) < unsigned(rois.rd) && unsigned(ly) < unsigned(rois.rh) &&
         unsigned(lx) < unsigned(rois.rw)) {
       if (!touched) {
-        sum = *a;
+        if constexpr (VX == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(a);
+          sum[0] = v.x; sum[1] = v.y; sum[2] = v.z; sum[3] = v.w;
+        } else {
+          sum[0] = *a;
+        }
         touched = true;
       }
       const uint64_t p = (uint64_t(i) * classes + c) * roi_vol +
                          (uint32_t(lz) * rois.rh + uint32_t(ly)) * uint32_t(rois.rw) + uint32_t(lx);
-      sum += load_f32<TP>(pred + p);
+      if constexpr (VX == 4) {
+        const float4 q = load4_f32<TP>(pred + p);
+        sum[0] += q.x; sum[1] += q.y; sum[2] += q.z; sum[3] += q.w;
+      } else {
+        sum[0] += load_f32<TP>(pred + p);
+      }
     }
   }
-  if (touched) *a = sum;
+  if (touched) {
+    if constexpr (VX == 4) {
+      *reinterpret_cast<float4*>(a) = make_float4(sum[0], sum[1], sum[2], sum[3]);
+    } else {
+      *a = sum[0];
+    }
+  }
 }
 
 // One thread per voxel: arg-max over classes of acc / count.
@@ -225,21 +264,32 @@ int launch_roi_accumulate(float* acc, const void* pred, int pred_dtype, int64_t 
     x1 = r.x[i] > x1 ? r.x[i] : x1;
   }
   const int64_t bd = z1 + rd - z0, bh = y1 + rh - y0, bw = x1 + rw - x0;
-  const uint64_t total = uint64_t(classes) * bd * bh * bw;
+  // four voxels per thread when every x offset and width is a multiple of 4
+  bool vec4 = (W % 4 == 0) && (rw % 4 == 0) && (reinterpret_cast<uintptr_t>(acc) % 16 == 0) &&
+              (reinterpret_cast<uintptr_t>(pred) % (pred_dtype == kF32 ? 16 : 8) == 0);
+  for (int i = 0; i < r.n && vec4; ++i) vec4 = (r.x[i] % 4 == 0);
+  const int vx = vec4 ? 4 : 1;
+  const uint64_t total = uint64_t(classes) * bd * bh * (bw / vx);
   if (total >= (uint64_t(1) << 31) || uint64_t(n) * classes * rd * rh * rw >= (uint64_t(1) << 40))
     return set_error(kErrInvalid, "ROI batch too large for one launch");
   const uint64_t plane = uint64_t(D) * H * W;
   const uint32_t blocks = uint32_t((total + kThreads - 1) / kThreads);
-  const DivMod32 f_bw = DivMod32::make(uint32_t(bw)), f_bh = DivMod32::make(uint32_t(bh)),
+  const DivMod32 f_bw = DivMod32::make(uint32_t(bw / vx)), f_bh = DivMod32::make(uint32_t(bh)),
                  f_bd = DivMod32::make(uint32_t(bd));
-#define CRUMPET_ACC(TP)                                                                         \
-  roi_accumulate_kernel<TP><<<blocks, kThreads, 0, stream>>>(                                   \
-      acc, static_cast<const TP*>(pred), r, uint32_t(classes), uint32_t(H), uint32_t(W), plane, \
-      z0, y0, x0, uint32_t(total), f_bw, f_bh, f_bd)
-  if (pred_dtype == kF32) CRUMPET_ACC(float);
-  else if (pred_dtype == kF16) CRUMPET_ACC(__half);
-  else CRUMPET_ACC(__nv_bfloat16);
-#undef CRUMPET_ACC
+  auto launch = [&](auto tp) {
+    using TP = decltype(tp);
+    if (vec4)
+      roi_accumulate_kernel<TP, 4><<<blocks, kThreads, 0, stream>>>(
+          acc, static_cast<const TP*>(pred), r, uint32_t(classes), uint32_t(H), uint32_t(W),
+          plane, z0, y0, x0, uint32_t(total), f_bw, f_bh, f_bd);
+    else
+      roi_accumulate_kernel<TP, 1><<<blocks, kThreads, 0, stream>>>(
+          acc, static_cast<const TP*>(pred), r, uint32_t(classes), uint32_t(H), uint32_t(W),
+          plane, z0, y0, x0, uint32_t(total), f_bw, f_bh, f_bd);
+  };
+  if (pred_dtype == kF32) launch(float{});
+  else if (pred_dtype == kF16) launch(__half{});
+  else launch(__nv_bfloat16{});
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "roi_accumulate launch");
   return kOk;

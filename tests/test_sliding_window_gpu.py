@@ -45,10 +45,13 @@ def test_roi_gather_matches_slicing(out_dtype, cuda_device):
     assert torch.equal(out, want)
 
 
+@pytest.mark.parametrize("width", [61, 64], ids=["scalar_x", "vec4_x"])
 @pytest.mark.parametrize("pred_dtype", [torch.float16, torch.bfloat16, torch.float32])
-def test_roi_accumulate_bit_exact_with_overlaps(pred_dtype, cuda_device):
+def test_roi_accumulate_bit_exact_with_overlaps(pred_dtype, width, cuda_device):
+    # W = 64 puts every ROI x start on a multiple of 4 (4-voxel vector path); W = 61
+    # clamps the last ROI to x = 37 (one voxel per thread)
     g = torch.Generator(device=cuda_device).manual_seed(1)
-    classes, spatial, roi = 5, (50, 47, 61), (24, 24, 24)
+    classes, spatial, roi = 5, (50, 47, width), (24, 24, 24)
     starts = roi_grid(spatial, roi, 0.5)
     acc = torch.randn((classes, *spatial), device=cuda_device, generator=g)
     want = acc.clone()
