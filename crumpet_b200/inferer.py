@@ -13,8 +13,8 @@ one launch per ROI batch instead of a copy, a cast and an add per ROI, with the
 same fp32 additions in the same order, so the results are bit-identical to the
 eager loop; CPU tensors take the eager torch path.
 
-Multi-GPU: one process per GPU.  ROI batches are dealt round-robin to ranks
-(rank r runs batches r, r + world, ...); each rank accumulates its own
+Multi-GPU: one process per GPU.  Rank r runs the r-th contiguous 1/world of the ROI
+grid (balanced to one ROI), cut into batches; each rank accumulates its own
 predictions, and the only collective is one NCCL sum-reduce of the
 accumulator onto rank 0 at the end, which then normalises and takes the
 arg-max.  There is no inter-GPU traffic inside the model.
@@ -83,9 +83,13 @@ class SlidingWindowInferer:
         return roi_grid(spatial, self.roi, self.overlap)
 
     def my_batches(self, spatial) -> list[list[tuple[int, int, int]]]:
+        """This rank's ROI batches: a contiguous range of the ROI grid (ranks differ by at
+        most one ROI, and a batch's ROIs stay spatially adjacent), cut into sw_batch."""
         starts = self.rois(spatial)
-        batches = [starts[i:i + self.sw_batch] for i in range(0, len(starts), self.sw_batch)]
-        return batches[self.rank::self.world]
+        lo = self.rank * len(starts) // self.world
+        hi = (self.rank + 1) * len(starts) // self.world
+        mine = starts[lo:hi]
+        return [mine[i:i + self.sw_batch] for i in range(0, len(mine), self.sw_batch)]
 
     def _count_map(self, spatial, device) -> torch.Tensor:
         key = (tuple(spatial), device)

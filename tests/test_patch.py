@@ -80,10 +80,15 @@ def test_roi_grid_matches_config():
     assert axis_starts(64, 96, 0.5) == [0]
 
 
-def test_roi_sharding_partitions_the_batches():
-    inf = [SlidingWindowInferer(None, (96,) * 3, 4, 0.5, rank=r, world=3) for r in range(3)]
-    seen = [roi for i in inf for b in i.my_batches((512, 512, 224)) for roi in b]
-    assert len(seen) == 400 and len(set(seen)) == 400
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_roi_sharding_partitions_the_batches(world):
+    inf = [SlidingWindowInferer(None, (96,) * 3, 8, 0.5, rank=r, world=world) for r in range(world)]
+    per_rank = [[roi for b in i.my_batches((512, 512, 224)) for roi in b] for i in inf]
+    seen = [roi for rois in per_rank for roi in rois]
+    # every ROI exactly once, in grid order, ranks balanced to one ROI
+    assert seen == roi_grid((512, 512, 224), (96,) * 3, 0.5)
+    assert max(map(len, per_rank)) - min(map(len, per_rank)) <= 1
+    assert all(len(b) <= 8 for i in inf for b in i.my_batches((512, 512, 224)))
 
 
 def test_sliding_window_eager_cpu_matches_single_forward():
