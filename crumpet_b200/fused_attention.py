@@ -51,6 +51,8 @@ def fused_swin_attention(
         raise ValueError("fused_swin_attention requires head_dim 16")
     if scale is None:
         scale = 1.0 / (D ** 0.5)
+    if not 0.0 < float(scale) < float("inf"):
+        raise ValueError("fused attention requires a finite scale > 0")
     bias = relative_position_bias.to(q.dtype).contiguous()
     mask_t = None
     bnd = None
@@ -117,6 +119,8 @@ def swin_window_attention_qkv(
         window_size = (N, 1, 1)
     if scale is None:
         scale = 1.0 / (D ** 0.5)
+    if not 0.0 < float(scale) < float("inf"):
+        raise ValueError("fused attention requires a finite scale > 0")
     table = relative_position_bias_table
     if table.dtype not in (torch.float32, qkv.dtype):
         table = table.float()
