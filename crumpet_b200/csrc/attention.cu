@@ -1,6 +1,6 @@
 // crumpet_b200: fused 3D Swin window attention for sm_100a (B200).
 //
-// Computes, per window b and head h (head_dim 16, N <= 384 tokens),
+// Computes, per window b and head h (head_dim 16 or 32, N <= 384 tokens),
 //   out[b,h] = softmax(q k^T * scale + bias[h] + mask) v
 // with fp32 scores and softmax -- the function of the reference Triton kernel
 // torch-ext/crumpet/fused_attention.py:48-146 (eager form: MONAI WindowAttention,
@@ -57,30 +57,37 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kHD = 16;       // head dimension
+constexpr int kAtom = 16;     // channels per 32-byte swizzle atom (head_dim 16 = one atom)
 constexpr int kBM = 128;      // query rows per tile (UMMA M)
 constexpr int kCH = 64;       // key chunk
 constexpr int kNumWG = 3;      // independent tile pipelines (softmax warpgroups) per CTA
-constexpr int kStages = 4;     // Q/K/V stages, one ring shared by all WGs
 constexpr int kCtrlWarps = 4;  // warp 0: TMA producer; warps 1..kNumWG: MMA issuers
 static_assert(kNumWG + 1 <= kCtrlWarps, "one TMA warp and one MMA warp per WG");
 constexpr int kSmThreads = kNumWG * 4 * 32;            // softmax threads (one per TMEM lane)
 constexpr int kThreads = kCtrlWarps * 32 + kSmThreads;  // 512
-constexpr int kRowBytes = kHD * 2;
+constexpr int kRowBytes = kAtom * 2;  // one atom row: 16 channels of fp16/bf16
 constexpr int kBarsPerWG = 9;
-constexpr uint32_t kTmemPerWG = 160;
-constexpr uint32_t kTmemCols = kTmemPerWG * kNumWG <= 256 ? 256u : 512u;  // power of two
+constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;  // P = 2^(x - m_ref) stays <= 2^8
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int NPAD>
+// Per (padded key count, head dim) layout.  A head dim of 32 is two 16-channel
+// atoms: Q, K and V are loaded as one TMA box per atom into separate regions, QK^T
+// takes one MMA per atom, and PV one MMA per atom ([V_0 | 1] then V_1).
+template <int NPAD, int HD>
 struct Cfg {
   static_assert(NPAD % 32 == 0 && NPAD <= 384, "NPAD must be a multiple of 32, at most 384");
+  static_assert(HD == 16 || HD == 32, "head_dim 16 or 32");
+  static constexpr int NKH = HD / kAtom;              // channel atoms
   static constexpr int NKB = (NPAD + 127) / 128;      // 128-row TMA boxes for K and V
   static constexpr int NCH = (NPAD + kCH - 1) / kCH;  // key chunks
   static constexpr int LAST_W = NPAD - (NCH - 1) * kCH;
-  static constexpr int Q_BYTES = kBM * kRowBytes;
-  static constexpr int KV_BYTES = NKB * 128 * kRowBytes;
+  static constexpr int STAGES = HD == 16 ? 4 : 2;     // Q/K/V ring stages (shared memory budget)
+  static constexpr int NPB = HD == 16 ? 2 : 1;        // P chunk buffers (TMEM budget)
+  static constexpr int Q_ATOM = kBM * kRowBytes;
+  static constexpr int KV_ATOM = NKB * 128 * kRowBytes;
+  static constexpr int Q_BYTES = NKH * Q_ATOM;
+  static constexpr int KV_BYTES = NKH * KV_ATOM;
   static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
   // Bias tile: UMMA A operand, K-major without swizzle: 8x8 core matrices of
   // 128 bytes; core matrix (row group rg, column group cg) at cg * 2048 + rg * 128.
@@ -88,16 +95,20 @@ struct Cfg {
   static constexpr int BIAS_BYTES = (NPAD / 8) * BIAS_CG_BYTES;
   static constexpr int ONES_BYTES = NKB * 128 * kRowBytes;  // [keys][16] of 1.0
   static constexpr int PLANE_BYTES = 3 * NCH * 8;     // analytic-mask code planes
-  // TMEM columns of one WG: S chunk (64), two P chunk buffers (32 packed each),
-  // O (16) + row sum (16).
+  // TMEM columns of one WG: S chunk (64), NPB P chunk buffers (32 packed each),
+  // O_0 (16) + row sum (16) [+ O_1 (16) for head dim 32].
   static constexpr int TM_S = 0;
   static constexpr int TM_P = kCH;
-  static constexpr int TM_O = kCH + kCH;
-  static_assert(TM_O + 2 * kHD <= int(kTmemPerWG), "TMEM budget");
+  static constexpr int TM_O = kCH + NPB * (kCH / 2);
+  static constexpr int O_COLS = 2 * kAtom + (NKH - 1) * kAtom;
+  // each WG's block starts on a 32-column boundary
+  static constexpr uint32_t TMEM_PER_WG = (TM_O + O_COLS + 31) / 32 * 32;
+  static_assert(TMEM_PER_WG * kNumWG <= kTmemCols, "TMEM budget");
   static constexpr int IDENT_BYTES = 512;             // 16x16 identity, UMMA B operand
-  static constexpr int SMEM_BYTES = 1024 + kStages * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
                                     IDENT_BYTES + PLANE_BYTES +
-                                    (2 * kStages + kNumWG * kBarsPerWG + 1) * 8 + 64;
+                                    (2 * STAGES + kNumWG * kBarsPerWG + 1) * 8 + 64 + 4 * STAGES;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 enum MaskMode : int { kMaskNone = 0, kMaskDense = 1, kMaskAnalytic = 2 };
@@ -213,6 +224,21 @@ __device__ __forceinline__ uint32_t ldg_u32(const uint32_t* p) {
   return v;
 }
 
+// Waits until *flag == value (bounded like mbar_wait; false on timeout or abort).
+__device__ __forceinline__ bool wait_flag_equals(volatile int* flag, int value,
+                                                 volatile int* abort) {
+  if (*flag == value) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (*flag == value) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 // Waits on a barrier ignoring the abort flag (used only while draining).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
@@ -232,12 +258,14 @@ __device__ __forceinline__ uint32_t token_code(const KParams& p, int t) {
          (uint32_t(lw >= p.wsw - p.ssw) << 2);
 }
 
-template <int NPAD, bool BF16, int MASK>
+template <int NPAD, int HD, bool BF16, int MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 window_attention_kernel(const __grid_constant__ CUtensorMap tq,
                         const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const KParams p) {
-  using C = Cfg<NPAD>;
+  using C = Cfg<NPAD, HD>;
+  constexpr int kStages = C::STAGES;
+  constexpr uint32_t kTmemPerWG = C::TMEM_PER_WG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -250,6 +278,12 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   uint64_t* bias_ready = bars + 2 * kStages + kNumWG * kBarsPerWG;  // one phase per pair
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Tile index each ring stage was last issued for.  The stages are shared by the
+  // warpgroups, so a consumer can reach tile k while the stage's barrier is still
+  // two phases behind (its parity then matches an old phase): it first waits for
+  // the TMA warp to announce tile k in this word, which implies the previous
+  // phase has completed, and only then waits on the barrier's parity.
+  volatile int* stage_tile = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -283,6 +317,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     }
     mbar_init(bias_ready, 1);
     *abort_flag = 0;
+    for (int st = 0; st < kStages; ++st) stage_tile[st] = -1;
     fence_mbar_init();
   }
   if constexpr (MASK == kMaskAnalytic) {
@@ -344,13 +379,18 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             }
             uint8_t* sb = smem + st * C::STAGE_BYTES;
             uint64_t* full = load_full + st;
+            stage_tile[st] = int(k);
             mbar_arrive_expect_tx(full, C::STAGE_BYTES);
-            tma_load_4d(sb, &tq, full, 0, mt * kBM, h, b);
 #pragma unroll
-            for (int kb = 0; kb < C::NKB; ++kb) {
-              tma_load_4d(sb + C::Q_BYTES + kb * 128 * kRowBytes, &tk, full, 0, kb * 128, h, b);
-              tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + kb * 128 * kRowBytes, &tv, full, 0,
-                          kb * 128, h, b);
+            for (int hk = 0; hk < C::NKH; ++hk) {  // one box per 16-channel atom
+              tma_load_4d(sb + hk * C::Q_ATOM, &tq, full, kAtom * hk, mt * kBM, h, b);
+#pragma unroll
+              for (int kb = 0; kb < C::NKB; ++kb) {
+                tma_load_4d(sb + C::Q_BYTES + hk * C::KV_ATOM + kb * 128 * kRowBytes, &tk, full,
+                            kAtom * hk, kb * 128, h, b);
+                tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + hk * C::KV_ATOM + kb * 128 * kRowBytes,
+                            &tv, full, kAtom * hk, kb * 128, h, b);
+              }
             }
           }
         }
@@ -373,9 +413,11 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         uint32_t it = 0, n_se = 0, n_oe = 0, n_pv = 0;
         bool ok = true;
         auto issue_pv = [&](int c, uint32_t v_addr) -> bool {
-          // P chunk n_pv is in buffer n_pv & 1; its use (n_pv >> 1) completes phase
-          // n_pv >> 1 of that buffer's P-full barrier
-          if (!mbar_wait(bar(w, kPF + int(n_pv & 1u)), (n_pv >> 1) & 1u, abort_flag)) return false;
+          // P chunk n_pv is in buffer n_pv % NPB; its use n_pv / NPB completes that
+          // phase of the buffer's P-full barrier
+          const uint32_t buf = n_pv % uint32_t(C::NPB);
+          if (!mbar_wait(bar(w, kPF + int(buf)), (n_pv / uint32_t(C::NPB)) & 1u, abort_flag))
+            return false;
           tc_fence_after();
           if (c == 0) {
             if (!mbar_wait(bar(w, kOE), (n_oe & 1u) ^ 1u, abort_flag)) return false;
@@ -383,15 +425,22 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             tc_fence_after();
           }
           const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
-          // B = [V | ones]: MN-major, the ones atom sits LBO bytes after V
-          constexpr uint32_t idesc_pv = idesc_f16(kBM, 2 * kHD, BF16, true);
+          // B = [V_0 | ones]: MN-major, the ones atom sits LBO bytes after V_0; further
+          // channel atoms V_1.. accumulate into their own 16 columns after the row sums
+          constexpr uint32_t idesc_pv = idesc_f16(kBM, 2 * kAtom, BF16, true);
+          constexpr uint32_t idesc_pv1 = idesc_f16(kBM, kAtom, BF16, true);
           const uint32_t lbo = ones_addr - v_addr;
-          const uint32_t buf = n_pv & 1u;  // P chunks alternate between two buffers
           for (int k = 0; k < width / 16; ++k) {
-            const uint64_t vdesc =
-                smem_desc(v_addr + uint32_t(c * kCH + k * 16) * kRowBytes, lbo, 256, kLayoutSW32);
-            umma_ts(tO, tP + buf * uint32_t(kCH / 2) + uint32_t(k * 8), vdesc, idesc_pv,
-                    (c > 0 || k > 0) ? 1u : 0u);
+            const uint32_t pa = tP + buf * uint32_t(kCH / 2) + uint32_t(k * 8);
+            const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
+            const uint32_t row_off = uint32_t(c * kCH + k * 16) * kRowBytes;
+            umma_ts(tO, pa, smem_desc(v_addr + row_off, lbo, 256, kLayoutSW32), idesc_pv, acc);
+#pragma unroll
+            for (int hk = 1; hk < C::NKH; ++hk) {
+              umma_ts(tO + uint32_t(2 * kAtom + (hk - 1) * kAtom), pa,
+                      smem_desc(v_addr + hk * C::KV_ATOM + row_off, 16, 256, kLayoutSW32),
+                      idesc_pv1, acc);
+            }
           }
           umma_commit(bar(w, kPE + int(buf)));
           ++n_pv;
@@ -412,7 +461,8 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             if (int(k % kNumWG) != w) continue;
             const int st = int(k % kStages);
             const uint32_t ph = (k / kStages) & 1u;
-            if (!mbar_wait(load_full + st, ph, abort_flag)) {
+            if (!wait_flag_equals(stage_tile + st, int(k), abort_flag) ||
+                !mbar_wait(load_full + st, ph, abort_flag)) {
               ok = false;
               break;
             }
@@ -421,7 +471,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             const uint32_t q_addr = sb;
             const uint32_t k_addr = sb + C::Q_BYTES;
             const uint32_t v_addr = sb + C::Q_BYTES + C::KV_BYTES;
-            const uint64_t qdesc = smem_desc(q_addr, 16, 256, kLayoutSW32);
+
             for (int c = 0; c < C::NCH && ok; ++c) {
               if (!mbar_wait(bar(w, kSE), (n_se & 1u) ^ 1u, abort_flag)) {
                 ok = false;
@@ -430,9 +480,13 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               ++n_se;
               tc_fence_after();
               const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
-              const uint64_t kdesc =
-                  smem_desc(k_addr + uint32_t(c * kCH) * kRowBytes, 16, 256, kLayoutSW32);
-              umma_ss(tS, qdesc, kdesc, idesc_f16(kBM, width, BF16, false), 0u);
+#pragma unroll
+              for (int hk = 0; hk < C::NKH; ++hk) {  // QK^T summed over the channel atoms
+                const uint64_t qdesc = smem_desc(q_addr + hk * C::Q_ATOM, 16, 256, kLayoutSW32);
+                const uint64_t kdesc = smem_desc(
+                    k_addr + hk * C::KV_ATOM + uint32_t(c * kCH) * kRowBytes, 16, 256, kLayoutSW32);
+                umma_ss(tS, qdesc, kdesc, idesc_f16(kBM, width, BF16, false), hk > 0 ? 1u : 0u);
+              }
               for (int i = 0; i < width / 16; ++i) {
                 const uint64_t bdesc = smem_desc(
                     bias_addr + uint32_t(c * (kCH / 8) + 2 * i) * C::BIAS_CG_BYTES,
@@ -597,8 +651,8 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           tc_fence_after();
           // P buffer of this chunk is free once the PV MMA of its previous use
           // (two chunks ago) has completed.
-          const uint32_t pbuf = n_chunk & 1u;
-          const uint32_t puse_parity = ((n_chunk >> 1) & 1u) ^ 1u;
+          const uint32_t pbuf = n_chunk % uint32_t(C::NPB);
+          const uint32_t puse_parity = ((n_chunk / uint32_t(C::NPB)) & 1u) ^ 1u;
           if (!warp_live) {
             // No valid row in this warp: keep the barrier protocol, skip the math.
             __syncwarp();
@@ -683,15 +737,25 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           if (c > 0 && __any_sync(0xffffffffu, rescale)) {
             // O may be rescaled once the PV MMA of the previous chunk has completed.
             const uint32_t prev = n_chunk - 1;
-            if (!mbar_wait(bar(w, kPE + int(prev & 1u)), (prev >> 1) & 1u, abort_flag)) return false;
+            if (!mbar_wait(bar(w, kPE + int(prev % uint32_t(C::NPB))),
+                           (prev / uint32_t(C::NPB)) & 1u, abort_flag))
+              return false;
             tc_fence_after();
             const float f = rescale ? fast_ex2(m_ref - new_ref) : 1.f;
-            uint32_t o[2 * kHD];
+            uint32_t o[2 * kAtom];
             tmem_ld32(tO, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 2 * kHD; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            for (int i = 0; i < 2 * kAtom; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
             tmem_st32(tO, o);
+            if constexpr (C::NKH > 1) {
+              uint32_t o1[kAtom];
+              tmem_ld16(tO + 2 * kAtom, o1);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < kAtom; ++i) o1[i] = __float_as_uint(__uint_as_float(o1[i]) * f);
+              tmem_st16(tO + 2 * kAtom, o1);
+            }
           }
           if (!mbar_wait(bar(w, kPE + int(pbuf)), puse_parity, abort_flag)) return false;
           tc_fence_after();
@@ -732,23 +796,34 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           if (lane == 0) mbar_arrive(bar(w, kOE));
           continue;
         }
-        uint32_t o[2 * kHD];
+        uint32_t o[2 * kAtom];
+        uint32_t o1[kAtom];  // channels 16..31 (head dim 32)
         tmem_ld32(tO, o);
+        if constexpr (C::NKH > 1) tmem_ld16(tO + 2 * kAtom, o1);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(w, kOE));
         if (valid) {
-          const float inv = 1.f / __uint_as_float(o[kHD]);
-          uint32_t packed[kHD / 2];
-#pragma unroll
-          for (int d = 0; d < kHD; d += 2)
-            packed[d / 2] = pack2<BF16>(__uint_as_float(o[d]) * inv, __uint_as_float(o[d + 1]) * inv);
+          const float inv = 1.f / __uint_as_float(o[kAtom]);  // row sum
           uint16_t* dst = p.out + b * p.out_sb + h * p.out_sh + qrow * p.out_sn;
-          stg(reinterpret_cast<uint4*>(dst),
-              make_uint4(packed[0], packed[1], packed[2], packed[3]));
+          uint32_t packed[kAtom / 2];
+#pragma unroll
+          for (int d = 0; d < kAtom; d += 2)
+            packed[d / 2] = pack2<BF16>(__uint_as_float(o[d]) * inv, __uint_as_float(o[d + 1]) * inv);
+          stg(reinterpret_cast<uint4*>(dst), make_uint4(packed[0], packed[1], packed[2], packed[3]));
           stg(reinterpret_cast<uint4*>(dst + 8),
               make_uint4(packed[4], packed[5], packed[6], packed[7]));
+          if constexpr (C::NKH > 1) {
+#pragma unroll
+            for (int d = 0; d < kAtom; d += 2)
+              packed[d / 2] =
+                  pack2<BF16>(__uint_as_float(o1[d]) * inv, __uint_as_float(o1[d + 1]) * inv);
+            stg(reinterpret_cast<uint4*>(dst + 16),
+                make_uint4(packed[0], packed[1], packed[2], packed[3]));
+            stg(reinterpret_cast<uint4*>(dst + 24),
+                make_uint4(packed[4], packed[5], packed[6], packed[7]));
+          }
         }
       }
     }
@@ -792,7 +867,7 @@ int make_qkv_map(CUtensorMap* map, const void* base, const AttnArgs& a) {
                               cuuint64_t(a.B)};
   const cuuint64_t strides[3] = {cuuint64_t(a.qkv_stride_n) * 2, cuuint64_t(a.qkv_stride_h) * 2,
                                  cuuint64_t(a.qkv_stride_b) * 2};
-  const cuuint32_t box[4] = {cuuint32_t(kHD), 128u, 1u, 1u};
+  const cuuint32_t box[4] = {cuuint32_t(kAtom), 128u, 1u, 1u};  // one 16-channel atom
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapDataType dt =
       a.dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -810,11 +885,11 @@ int num_sms() {
   return sms > 0 ? sms : 148;
 }
 
-template <int NPAD, bool BF16, int MASK>
+template <int NPAD, int HD, bool BF16, int MASK>
 int launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                 const KParams& kp, cudaStream_t stream) {
-  using C = Cfg<NPAD>;
-  auto kern = window_attention_kernel<NPAD, BF16, MASK>;
+  using C = Cfg<NPAD, HD>;
+  auto kern = window_attention_kernel<NPAD, HD, BF16, MASK>;
   static bool configured[64] = {false};  // per device; the attribute is per function
   int dev = 0;
   cudaGetDevice(&dev);
@@ -830,18 +905,27 @@ int launch_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
   return kOk;
 }
 
-template <int NPAD>
-int dispatch_npad(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+template <int NPAD, int HD>
+int dispatch_mode(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
                   const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
   const int mode = a.analytic ? kMaskAnalytic : (a.mask ? kMaskDense : kMaskNone);
   if (a.dtype == kBF16) {
-    if (mode == kMaskDense) return launch_impl<NPAD, true, kMaskDense>(tq, tk, tv, kp, stream);
-    if (mode == kMaskAnalytic) return launch_impl<NPAD, true, kMaskAnalytic>(tq, tk, tv, kp, stream);
-    return launch_impl<NPAD, true, kMaskNone>(tq, tk, tv, kp, stream);
+    if (mode == kMaskDense) return launch_impl<NPAD, HD, true, kMaskDense>(tq, tk, tv, kp, stream);
+    if (mode == kMaskAnalytic)
+      return launch_impl<NPAD, HD, true, kMaskAnalytic>(tq, tk, tv, kp, stream);
+    return launch_impl<NPAD, HD, true, kMaskNone>(tq, tk, tv, kp, stream);
   }
-  if (mode == kMaskDense) return launch_impl<NPAD, false, kMaskDense>(tq, tk, tv, kp, stream);
-  if (mode == kMaskAnalytic) return launch_impl<NPAD, false, kMaskAnalytic>(tq, tk, tv, kp, stream);
-  return launch_impl<NPAD, false, kMaskNone>(tq, tk, tv, kp, stream);
+  if (mode == kMaskDense) return launch_impl<NPAD, HD, false, kMaskDense>(tq, tk, tv, kp, stream);
+  if (mode == kMaskAnalytic)
+    return launch_impl<NPAD, HD, false, kMaskAnalytic>(tq, tk, tv, kp, stream);
+  return launch_impl<NPAD, HD, false, kMaskNone>(tq, tk, tv, kp, stream);
+}
+
+template <int NPAD>
+int dispatch_npad(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+                  const CUtensorMap& tv, const KParams& kp, cudaStream_t stream) {
+  if (a.head_dim == 32) return dispatch_mode<NPAD, 32>(a, tq, tk, tv, kp, stream);
+  return dispatch_mode<NPAD, 16>(a, tq, tk, tv, kp, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -855,7 +939,8 @@ int set_attention_test_stall(int enable) { return g_test_stall.exchange(enable ?
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.dtype != kF16 && a.dtype != kBF16)
     return set_error(kErrUnsupported, "fused_swin_attention supports float16 and bfloat16");
-  if (a.head_dim != kHD) return set_error(kErrUnsupported, "fused_swin_attention requires head_dim 16");
+  if (a.head_dim != 16 && a.head_dim != 32)
+    return set_error(kErrUnsupported, "fused_swin_attention requires head_dim 16 or 32");
   if (a.N < 1 || a.N > 384) return set_error(kErrUnsupported, "fused_swin_attention supports 1 <= N <= 384");
   if (a.B < 0 || a.H < 1) return set_error(kErrInvalid, "B must be >= 0 and H >= 1");
   if (!(a.scale > 0.f) || !(a.scale < 1e30f))

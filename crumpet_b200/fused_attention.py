@@ -13,7 +13,7 @@ Python entry point with the signature of the reference Triton launcher
 ``repeat``) or ``None``; ``boundary``: per-window flag, mask rows are read only
 where it is non-zero.  ``block_m`` / ``block_n`` are accepted for API
 compatibility and ignored: the tile shape is fixed by the tcgen05 design
-(128 query rows x 64-key chunks).  fp16 and bf16, head_dim 16, N <= 384.
+(128 query rows x 64-key chunks).  fp16 and bf16, head_dim 16 or 32, N <= 384.
 """
 
 from __future__ import annotations
@@ -47,8 +47,8 @@ def fused_swin_attention(
         raise ValueError(f"relative_position_bias must have shape {(H, N, N)}")
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise TypeError("fused_swin_attention supports torch.float16 and torch.bfloat16")
-    if D != 16:
-        raise ValueError("fused_swin_attention requires head_dim 16")
+    if D not in (16, 32):
+        raise ValueError("fused_swin_attention requires head_dim 16 or 32")
     if scale is None:
         scale = 1.0 / (D ** 0.5)
     if not 0.0 < float(scale) < float("inf"):
@@ -111,8 +111,8 @@ def swin_window_attention_qkv(
     if qkv.ndim != 5 or qkv.shape[2] != 3:
         raise ValueError("qkv must have shape [B, N, 3, H, head_dim]")
     B, N, _, H, D = (int(s) for s in qkv.shape)
-    if D != 16:
-        raise ValueError("swin_window_attention_qkv requires head_dim 16")
+    if D not in (16, 32):
+        raise ValueError("swin_window_attention_qkv requires head_dim 16 or 32")
     if qkv.dtype not in (torch.float16, torch.bfloat16):
         raise TypeError("swin_window_attention_qkv supports torch.float16 and torch.bfloat16")
     if window_size is None:

@@ -17,8 +17,8 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   (reference :201-232);
 * ``WindowAttention.forward``: qkv Linear -> fused tcgen05 window attention ->
   proj Linear (reference :117-198), falling back to the module's own eager
-  forward in training, with attention dropout, for head_dim != 16 or for
-  fp32 activations;
+  forward in training, with attention dropout, for head dims other than 16
+  and 32, or for fp32 activations;
 
 returns True when it installs the patch and False when it is already active;
 ``unpatch_monai_swin_unetr`` restores the originals.  It raises RuntimeError
@@ -210,7 +210,7 @@ def _patched_window_attention_forward(original):
         heads = self.num_heads
         head_dim = c // heads
         qkv = self.qkv(x)
-        if head_dim != 16 or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
+        if head_dim not in (16, 32) or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
             return original(self, x, mask)
         geometry = None if mask is None else getattr(mask, _GEOMETRY_ATTR, None)
         if mask is None or geometry is not None:

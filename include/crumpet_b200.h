@@ -116,7 +116,7 @@ CRUMPET_API int crumpet_compute_attn_mask_3d(void* output, int dtype, int64_t D,
  * or NULL.  When boundary is given, mask rows are read only for windows with
  * boundary[b] != 0 (the others are treated as unmasked); when it is NULL and a
  * mask is given, every window reads its mask.  dtype: F16 or BF16 (all tensors
- * share it); head_dim == 16; 1 <= N <= 384.
+ * share it); head_dim 16 or 32; 1 <= N <= 384.
  * Replaces crumpet.fused_attention.fused_swin_attention
  *   (torch-ext/crumpet/fused_attention.py:149-226; kernel :48-146), which the
  *   reference exposes only as a Python/Triton function.
@@ -140,7 +140,7 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
  *   ws_*  window size (ws_d*ws_h*ws_w == N); ss_* cyclic shift (all 0: no mask)
  * The mask equals crumpet_compute_attn_mask_3d's on the padded grid; masked
  * scores are dropped exactly (e^-100 and e^-inf are both 0 in fp32).
- * dtype F16 or BF16, head_dim == 16, N <= 384.
+ * dtype F16 or BF16, head_dim 16 or 32, N <= 384.
  * Replaces the eager glue of torch-ext/crumpet/monai_patch.py:152-196 (q/k/v
  * split and .contiguous() copies, bias gather and permute, mask repeat, the
  * per-call mask abs().amax() scan, the output transpose) plus

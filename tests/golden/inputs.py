@@ -50,15 +50,24 @@ ATTENTION_CASES = [
     ("a_n343_h3_small_f16", 4, 3, (7, 7, 7), (7, 7, 7), None, None, "float16", 22, 0.15),
     ("a_n216_h6_quirk_f16", 2, 6, (6, 6, 6), (7, 7, 7), None, None, "float16", 24, 1.0),
     ("a_n64_h2_mask_f16", 8, 2, (4, 4, 4), (4, 4, 4), (8, 8, 8), (2, 2, 2), "float16", 25, 1.0),
+    # head_dim 32 (feature size 96 models): an optional 11th field
+    ("a_n64_h2_d32_mask_f16", 8, 2, (4, 4, 4), (4, 4, 4), (8, 8, 8), (2, 2, 2), "float16", 31,
+     1.0, 32),
+    ("a_n125_h3_d32_f16", 3, 3, (5, 5, 5), (5, 5, 5), None, None, "float16", 32, 1.0, 32),
 ]
 
 # Checked against the oracle only: the Triton CPU interpreter does not model
-# bfloat16 (numpy has no such type), so these have no reference-kernel golden.
+# bfloat16 (numpy has no such type), and it crashes on the N=343 head_dim 32
+# launch, so these have no reference-kernel golden.
 ORACLE_ONLY_ATTENTION_CASES = [
+    ("a_n343_h2_d32_mask_f16", 8, 2, (7, 7, 7), (7, 7, 7), (14, 14, 14), (3, 3, 3), "float16", 34,
+     1.0, 32),
     ("a_n343_h3_mask_bf16", 8, 3, (7, 7, 7), (7, 7, 7), (14, 14, 14), (3, 3, 3), "bfloat16", 23, 1.0),
     ("a_n125_h4_f16", 3, 4, (5, 5, 5), (5, 5, 5), None, None, "float16", 26, 1.0),
     ("a_n8_h1_f16", 5, 1, (2, 2, 2), (2, 2, 2), None, None, "float16", 27, 1.0),
     ("a_n343_h12_f16", 8, 12, (7, 7, 7), (7, 7, 7), (14, 14, 14), (3, 3, 3), "float16", 28, 1.0),
+    ("a_n343_h2_d32_mask_bf16", 8, 2, (7, 7, 7), (7, 7, 7), (14, 14, 14), (3, 3, 3), "bfloat16",
+     33, 1.0, 32),
 ]
 
 
@@ -83,18 +92,20 @@ def relative_index(window) -> np.ndarray:
 
 
 def attention_inputs(case, mask_fn=None):
-    """q, k, v [B,H,N,16]; bias [H,N,N]; mask [nW,N,N] or None; boundary [B] or None.
+    """q, k, v [B,H,N,hd] (hd 16 unless the case gives it); bias [H,N,N]; mask [nW,N,N] or None;
+    boundary [B] or None.
 
     The bias follows the MONAI quirk: the table and index belong to the
     configured window and are sliced [:N, :N] when the runtime window is
     smaller.  ``mask_fn(D, H, W, window, shift)`` -> float32 numpy mask
     defaults to the test oracle.
     """
-    name, B, H, window, cfg, mvol, mshift, dtype, seed, qscale = case
+    name, B, H, window, cfg, mvol, mshift, dtype, seed, qscale = case[:10]
+    hd = case[10] if len(case) > 10 else 16
     n = window[0] * window[1] * window[2]
-    q = (randn(seed, (B, H, n, 16), "float32") * qscale).to(getattr(torch, dtype))
-    k = (randn(seed + 1, (B, H, n, 16), "float32") * qscale).to(getattr(torch, dtype))
-    v = randn(seed + 2, (B, H, n, 16), dtype)
+    q = (randn(seed, (B, H, n, hd), "float32") * qscale).to(getattr(torch, dtype))
+    k = (randn(seed + 1, (B, H, n, hd), "float32") * qscale).to(getattr(torch, dtype))
+    v = randn(seed + 2, (B, H, n, hd), dtype)
     table = randn(seed + 3, ((2 * cfg[0] - 1) * (2 * cfg[1] - 1) * (2 * cfg[2] - 1), H), "float32")
     table = table * 0.5
     idx = relative_index(cfg)[:n, :n]

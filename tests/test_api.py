@@ -48,7 +48,7 @@ def test_capi_rejects_bad_arguments_without_touching_the_device():
     rc = lib.crumpet_fused_shift_partition_3d(null, null, 1, 0, 14, 14, 14, 4, 7, 7, 7, 3, 3, 3, null)
     assert rc == 0
     # attention: unsupported head_dim / N, and an empty batch
-    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 343, 32, 0.25, null)
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 343, 64, 0.25, null)
     assert rc == 3 and "head_dim" in _ops.last_error()
     rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 1000, 16, 0.25, null)
     assert rc == 3

@@ -4,6 +4,8 @@ the C ABI."""
 
 from __future__ import annotations
 
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -17,7 +19,8 @@ from oracle import mechanics as OM
 
 pytestmark = pytest.mark.gpu
 
-# (name, grid dims (padded), window, shift, heads, batch repeats, configured window, dtype)
+# (name, grid dims (padded), window, shift, heads, batch repeats, configured window, dtype
+#  [, head_dim (default 16)])
 CASES = [
     ("shift_n343_h3", (14, 14, 14), (7, 7, 7), (3, 3, 3), 3, 2, (7, 7, 7), "float16"),
     ("shift_n343_h6_28", (28, 28, 28), (7, 7, 7), (3, 3, 3), 6, 1, (7, 7, 7), "float16"),
@@ -26,17 +29,21 @@ CASES = [
     ("mixed_shift", (14, 21, 7), (7, 7, 7), (3, 0, 2), 3, 1, (7, 7, 7), "float16"),
     ("shift_n64_h2", (8, 8, 8), (4, 4, 4), (2, 2, 2), 2, 2, (4, 4, 4), "float16"),
     ("shift_n343_bf16", (14, 14, 14), (7, 7, 7), (3, 3, 3), 3, 1, (7, 7, 7), "bfloat16"),
+    ("shift_n343_h3_d32", (14, 14, 14), (7, 7, 7), (3, 3, 3), 3, 2, (7, 7, 7), "float16", 32),
+    ("quirk_n216_h12_d32", (6, 6, 6), (6, 6, 6), (0, 0, 0), 12, 2, (7, 7, 7), "float16", 32),
+    ("shift_n343_d32_bf16", (14, 14, 14), (7, 7, 7), (3, 3, 3), 2, 1, (7, 7, 7), "bfloat16", 32),
 ]
 
 
 def make_case(case, dev, table_dtype=torch.float32):
-    name, dims, ws, ss, H, reps, cfg, dtype = case
-    g = torch.Generator().manual_seed(abs(hash(name)) % (2**31))
+    name, dims, ws, ss, H, reps, cfg, dtype = case[:8]
+    hd = case[8] if len(case) > 8 else 16
+    g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
     nw = tuple(d // w for d, w in zip(dims, ws))
     nwin = nw[0] * nw[1] * nw[2]
     B, N = nwin * reps, ws[0] * ws[1] * ws[2]
     dt = getattr(torch, dtype)
-    qkv = torch.randn((B, N, 3, H, 16), generator=g).to(dt)
+    qkv = torch.randn((B, N, 3, H, hd), generator=g).to(dt)
     ncfg = cfg[0] * cfg[1] * cfg[2]
     table = (torch.randn(((2 * cfg[0] - 1) * (2 * cfg[1] - 1) * (2 * cfg[2] - 1), H), generator=g)
              * 0.5).to(table_dtype)
@@ -50,7 +57,7 @@ def make_case(case, dev, table_dtype=torch.float32):
     q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3))
     want = OA.window_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
                                bias.float().numpy(), mask)
-    want = np.transpose(want, (0, 2, 1, 3)).reshape(B, N, H * 16)
+    want = np.transpose(want, (0, 2, 1, 3)).reshape(B, N, H * hd)
     return (qkv.to(dev), table.to(dev), index.to(dev), nw, ws, ss), want
 
 
@@ -61,7 +68,7 @@ def tol(dtype):
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_packed_attention_matches_oracle(case, cuda_device):
     (qkv, table, index, nw, ws, ss), want = make_case(case, cuda_device)
-    out = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
+    out = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, qkv.shape[-1] ** -0.5)
     torch.cuda.synchronize()
     err = np.abs(out.float().cpu().numpy() - want).max()
     assert err <= tol(qkv.dtype), err

@@ -70,3 +70,17 @@ def test_sliding_window_patched_vs_eager(cuda_device):
     agree = (seg_p == seg_e).float().mean().item()
     assert agree >= 0.999, agree
     assert (logit_p - logit_e).abs().max().item() < 5e-2
+
+
+def test_head_dim_32_network_argmax_agreement(cuda_device):
+    # feature size 96: heads (3, 6, 12, 24) of head_dim 32 at every stage
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 96).to(cuda_device).eval()
+    x = torch.rand((1, 1, 64, 64, 64), device=cuda_device)
+    before = profiling.counters["swin_window_attention_qkv"]
+    patched = _run(model, x, True)
+    assert profiling.counters["swin_window_attention_qkv"] > before
+    eager = _run(model, x, False)
+    agree = (patched.argmax(1) == eager.argmax(1)).float().mean().item()
+    assert agree >= 0.999, agree
+    assert (patched - eager).abs().max().item() < 5e-2
