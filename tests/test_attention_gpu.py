@@ -109,3 +109,22 @@ def test_attention_deterministic(cuda_device):
     a, _ = run(case, cuda_device)
     b, _ = run(case, cuda_device)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("head_dim", [16, 32])
+def test_many_windows_per_cta_stay_in_step(head_dim, cuda_device):
+    """600 windows x 3 heads: every CTA walks hundreds of tiles through the shared
+    stage ring with all three warpgroups (head_dim 32 has a 2-stage ring), so a
+    warpgroup racing ahead of the ring would read another tile's K/V."""
+    g = torch.Generator().manual_seed(11)
+    B, H, N = 600, 3, 343
+    q, k, v = (torch.randn((B, H, N, head_dim), generator=g).half() for _ in range(3))
+    bias = (torch.randn((H, N, N), generator=g) * 0.1).half()
+    out = crumpet.fused_swin_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                                       bias.to(cuda_device), None)
+    torch.cuda.synchronize()
+    sel = [0, 1, 2, 149, 299, 450, 598, 599]
+    want = OA.window_attention(q[sel].float().numpy(), k[sel].float().numpy(),
+                               v[sel].float().numpy(), bias.float().numpy(), None)
+    assert np.abs(out[sel].float().cpu().numpy() - want).max() <= FP16_TOL
+    assert _ops.capi().crumpet_device_status(1) == 0
