@@ -74,7 +74,7 @@ def norm_shift_partition_3d(
     norm, so padded tokens are exact zeros) and the result is
     ``[B * num_windows, volume, C]`` in ``out_dtype`` (default ``x.dtype``).
     The norm is computed in fp32 with a biased variance, as ``nn.LayerNorm``;
-    C must be a multiple of 8 and at most 384.
+    C must be a multiple of 8 and at most 768.
     """
     if x.ndim != 5:
         raise ValueError("x must have shape [B, D, H, W, C]")
@@ -85,8 +85,8 @@ def norm_shift_partition_3d(
     out_dtype = x.dtype if out_dtype is None else out_dtype
     _check_dtype(out_dtype)
     B, D, H, W, C = (int(v) for v in x.shape)
-    if C % 8 or C > 384 or C == 0:
-        raise ValueError("norm_shift_partition_3d needs C a multiple of 8 and at most 384")
+    if C % 8 or C > 768 or C == 0:
+        raise ValueError("norm_shift_partition_3d needs C a multiple of 8 and at most 768")
     if tuple(weight.shape) != (C,) or tuple(bias.shape) != (C,):
         raise ValueError("weight and bias must have shape [C]")
     _, num_windows, volume = padded_geometry(D, H, W, window_size)

@@ -36,7 +36,7 @@ constexpr int kThreads = 256;
 // kTokensPerGroup tokens with all their loads in flight before any arithmetic.
 constexpr int kGroupsPerLane = 3;
 constexpr int kTokensPerGroup = 2;
-constexpr int kMaxC = 16 * kGroupsPerLane * 8;  // L <= 16: C <= 384
+constexpr int kMaxC = 32 * kGroupsPerLane * 8;  // L <= 32: C <= 768
 
 struct BlockGeom {
   uint32_t D, H, W;        // unpadded volume
@@ -358,7 +358,8 @@ cudaError_t launch_norm(void* out, const void* x, const float* gamma, const floa
     case 2: norm_shift_partition_kernel<TIn, TOut, 2><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
     case 4: norm_shift_partition_kernel<TIn, TOut, 4><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
     case 8: norm_shift_partition_kernel<TIn, TOut, 8><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    default: norm_shift_partition_kernel<TIn, TOut, 16><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 16: norm_shift_partition_kernel<TIn, TOut, 16><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    default: norm_shift_partition_kernel<TIn, TOut, 32><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
   }
   return cudaGetLastError();
 }
@@ -403,7 +404,7 @@ int launch_norm_shift_partition(void* out, int out_dtype, const void* x, int in_
   if (int e = check_geometry(B, D, H, W, C, ws, ss)) return e;
   if (C == 0 || C % 8 != 0 || C > kMaxC)
     return set_error(kErrUnsupported,
-                     "norm_shift_partition_3d needs C a multiple of 8 and at most 384");
+                     "norm_shift_partition_3d needs C a multiple of 8 and at most 768");
   if (ws[0] * ws[1] * ws[2] > 4096) return set_error(kErrInvalid, "window volume above 4096");
   if (B == 0) return kOk;
   if (!out || !x || !gamma || !beta) return set_error(kErrInvalid, "null tensor pointer");

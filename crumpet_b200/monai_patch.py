@@ -115,7 +115,7 @@ def _norm_fusable(norm, x: torch.Tensor) -> bool:
         and norm.bias is not None
         and tuple(norm.normalized_shape) == (c,)
         and c % 8 == 0
-        and c <= 384
+        and c <= 768
         and x.is_cuda
         and x.dtype in _FUSED_DTYPES
         and _no_grad_needed(x, norm.weight, norm.bias)

@@ -162,7 +162,7 @@ CRUMPET_API int crumpet_swin_window_attention_qkv(
  * mod padded dim when s lies inside the volume, and exactly 0 in the padding.
  * LN = (v - mean) / sqrt(var + eps) * weight + bias over C, fp32 arithmetic,
  * biased variance, one rounding to out_dtype.  weight, bias: fp32 [C].
- * C a multiple of 8, at most 384; all pointers 16-byte aligned.
+ * C a multiple of 8, at most 768; all pointers 16-byte aligned.
  * Replaces norm1 -> F.pad -> crumpet_ops::fused_shift_partition_3d, and the fp16
  * cast autocast inserts before the qkv Linear, in
  *   torch-ext/crumpet/monai_patch.py:79-97 (the reference runs them as separate

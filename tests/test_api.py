@@ -178,10 +178,10 @@ def test_block_fusion_capi_validation():
     lib = _ops.capi()
     null = ctypes.c_void_p(0)
     norm = lib.crumpet_norm_shift_partition_3d
-    # C not a multiple of 8 / above 384
+    # C not a multiple of 8 / above 768
     rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 44, 7, 7, 7, 3, 3, 3, null)
     assert rc == 3 and "multiple of 8" in _ops.last_error()
-    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 392, 7, 7, 7, 3, 3, 3, null)
+    rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 776, 7, 7, 7, 3, 3, 3, null)
     assert rc == 3
     # shift >= window, bad dtype, null pointers, empty batch
     rc = norm(null, 1, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 7, 3, 3, null)

@@ -38,8 +38,9 @@ STAGES = [
     (4, 12, 12, 12, 192, (7, 7, 7), (3, 3, 3)),
     (4, 6, 6, 6, 384, (7, 7, 7), (3, 3, 3)),
     (3, 17, 5, 23, 64, (7, 7, 7), (3, 3, 3)),
+    (2, 4, 4, 4, 768, (7, 7, 7), (3, 3, 3)),  # last stage of a feature-size-96 network
 ]
-STAGE_IDS = ["s48_C48", "s24_C96", "s12_C192", "s6_C384", "ragged_C64"]
+STAGE_IDS = ["s48_C48", "s24_C96", "s12_C192", "s6_C384", "ragged_C64", "s4_C768"]
 
 
 # |got - want| <= rel * |want| + abs: one rounding to the output type (fp16/bf16:
