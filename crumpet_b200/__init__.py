@@ -47,6 +47,7 @@ _OP_NAMES = (
     "swin_window_attention_qkv",
     "norm_shift_partition_3d",
     "unshift_unpartition_crop_3d",
+    "unshift_unpartition_crop_norm_3d",
 )
 
 
@@ -267,7 +268,11 @@ def fused_unshift_unpartition_3d(
 
 
 from .fused_attention import fused_swin_attention, swin_window_attention_qkv  # noqa: E402
-from .block_fusion import norm_shift_partition_3d, unshift_unpartition_crop_3d  # noqa: E402
+from .block_fusion import (  # noqa: E402
+    norm_shift_partition_3d,
+    unshift_unpartition_crop_3d,
+    unshift_unpartition_crop_norm_3d,
+)
 
 
 def patch_monai_swin_unetr(swin_module=None) -> bool:
@@ -297,6 +302,7 @@ __all__ = [
     "swin_window_attention_qkv",
     "norm_shift_partition_3d",
     "unshift_unpartition_crop_3d",
+    "unshift_unpartition_crop_norm_3d",
     "patch_monai_swin_unetr",
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",

@@ -10,7 +10,9 @@ on either side of the attention:
   + roll by ``-shift`` + window partition, written in the dtype the qkv Linear
   consumes;
 * :func:`unshift_unpartition_crop_3d` -- window reverse on the padded grid +
-  roll by ``+shift`` + crop, optionally adding the block's residual.
+  roll by ``+shift`` + crop, optionally adding the block's residual;
+* :func:`unshift_unpartition_crop_norm_3d` -- the same plus the LayerNorm of the
+  result (the block's ``norm2``, which opens its MLP half).
 
 Both are inference ops (no backward): they raise when autograd would need a
 gradient through them.  The MONAI patch uses them only outside autograd.
@@ -160,3 +162,74 @@ def unshift_unpartition_crop_3d(
                                                   *window_size, *shift_size)
     _prof.count("unshift_unpartition_crop_3d")
     return out
+
+
+def unshift_unpartition_crop_norm_3d(
+    windows: torch.Tensor,
+    B: int,
+    D: int,
+    H: int,
+    W: int,
+    C: int,
+    window_size: Sequence[int],
+    shift_size: Sequence[int],
+    weight: torch.Tensor,
+    bias: torch.Tensor,
+    eps: float,
+    residual: torch.Tensor | None = None,
+    norm_dtype: torch.dtype | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """:func:`unshift_unpartition_crop_3d` and the LayerNorm of its result in one pass.
+
+    Returns ``(out, normed)``: ``out`` as :func:`unshift_unpartition_crop_3d`
+    (dtype of ``windows``), ``normed = layer_norm(out, weight, bias, eps)`` over C
+    in fp32 arithmetic, written in ``norm_dtype`` (default: the dtype of
+    ``windows``).  In a Swin block this is the residual add of the attention half
+    and the ``norm2`` that opens the MLP half.  C must be a multiple of 8, at most
+    768.
+    """
+    if windows.ndim != 3:
+        raise ValueError("windows must have shape [B * num_windows, window_volume, C]")
+    window_size = _triple("window_size", window_size)
+    shift_size = _triple("shift_size", shift_size)
+    _check_window(window_size, shift_size)
+    _check_dtype(windows.dtype)
+    norm_dtype = windows.dtype if norm_dtype is None else norm_dtype
+    _check_dtype(norm_dtype)
+    B, D, H, W, C = int(B), int(D), int(H), int(W), int(C)
+    if min(D, H, W) <= 0 or B < 0:
+        raise ValueError("D, H and W must be positive")
+    if C % 8 or C > 768 or C == 0:
+        raise ValueError("unshift_unpartition_crop_norm_3d needs C a multiple of 8 and at most 768")
+    if tuple(weight.shape) != (C,) or tuple(bias.shape) != (C,):
+        raise ValueError("weight and bias must have shape [C]")
+    _, num_windows, volume = padded_geometry(D, H, W, window_size)
+    expected = (B * num_windows, volume, C)
+    if tuple(int(v) for v in windows.shape) != expected:
+        raise ValueError(f"windows must have shape {expected}")
+    if residual is not None:
+        if tuple(residual.shape) != (B, D, H, W, C):
+            raise ValueError(f"residual must have shape {(B, D, H, W, C)}")
+        if residual.dtype != windows.dtype:
+            raise TypeError("residual must have the dtype of windows")
+    shape = (B, D, H, W, C)
+    if windows.device.type == "meta":
+        return (torch.empty(shape, dtype=windows.dtype, device=windows.device),
+                torch.empty(shape, dtype=norm_dtype, device=windows.device))
+    if windows.device.type != "cuda":
+        raise RuntimeError("crumpet_b200 runs unshift_unpartition_crop_norm_3d on CUDA devices only "
+                           f"(got {windows.device})")
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad
+                                       for t in (windows, residual, weight, bias)):
+        raise RuntimeError("unshift_unpartition_crop_norm_3d has no backward; call it under "
+                           "torch.no_grad()")
+    out = torch.empty(shape, dtype=windows.dtype, device=windows.device)
+    normed = torch.empty(shape, dtype=norm_dtype, device=windows.device)
+    w = _aligned(weight.detach().to(device=windows.device, dtype=torch.float32), 16)
+    b = _aligned(bias.detach().to(device=windows.device, dtype=torch.float32), 16)
+    res = None if residual is None else _aligned(residual, 16)
+    _native.require().unshift_unpartition_crop_norm_3d(out, normed, _aligned(windows, 16), res, w, b,
+                                                       float(eps), B, D, H, W, C, *window_size,
+                                                       *shift_size)
+    _prof.count("unshift_unpartition_crop_norm_3d")
+    return out, normed

@@ -220,6 +220,21 @@ int crumpet_unshift_unpartition_crop_3d(void* output, const void* windows, const
                                          static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_unshift_unpartition_crop_norm_3d(void* output, void* normed, int norm_dtype,
+                                             const void* windows, const void* residual, int dtype,
+                                             const float* weight, const float* bias, float eps,
+                                             int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                                             int64_t ws_d, int64_t ws_h, int64_t ws_w,
+                                             int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                             void* stream) {
+  if (int e = check_dtype(dtype)) return e;
+  if (int e = check_dtype(norm_dtype)) return e;
+  const int64_t ws[3] = {ws_d, ws_h, ws_w}, ss[3] = {ss_d, ss_h, ss_w};
+  return launch_unshift_unpartition_crop_norm(output, normed, norm_dtype, windows, residual, dtype,
+                                              weight, bias, eps, B, D, H, W, C, ws, ss,
+                                              static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_roi_gather(void* out, int out_dtype, const void* volume, int in_dtype, int64_t C,
                        int64_t D, int64_t H, int64_t W, const int64_t* roi_starts, int64_t n,
                        int64_t rd, int64_t rh, int64_t rw, void* stream) {

@@ -45,6 +45,14 @@ int launch_unshift_unpartition_crop(void* out, const void* windows, const void* 
                                     int64_t C, const int64_t* ws, const int64_t* ss,
                                     cudaStream_t stream);
 
+// Unpartition + roll back + crop (+ residual) as above, plus normed = LayerNorm(out)
+// (fp32 gamma/beta, written in norm_dtype) in the same pass.
+int launch_unshift_unpartition_crop_norm(void* out, void* normed, int norm_dtype,
+                                         const void* windows, const void* residual, int dtype,
+                                         const float* gamma, const float* beta, float eps,
+                                         int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                                         const int64_t* ws, const int64_t* ss, cudaStream_t stream);
+
 // Sliding-window ROI inference: crop a batch of ROIs, accumulate their predictions,
 // normalise by the ROI count and take the arg-max.  `starts` is a HOST array of
 // n (z, y, x) triples (n <= 64), passed to the kernels by value.

@@ -43,8 +43,9 @@ struct BlockGeom {
   uint32_t Dp, Hp, Wp;     // padded grid (window multiples)
   uint32_t wd, wh, ww, sd, sh, sw;
   uint32_t nwh, nww, nw, N, C, groups;  // groups = C / 8
-  uint32_t tokens;         // output tokens of this launch (B_slice * nW * N)
+  uint32_t tokens;         // output tokens of this launch (B_slice * nW * N, or B_slice * D*H*W)
   DivMod32 f_N, f_nw, f_nww, f_nwh, f_ww, f_wh, f_wd;
+  DivMod32 f_W, f_H, f_D;  // unpadded volume
   float eps;
 };
 
@@ -296,6 +297,120 @@ unshift_unpartition_crop_kernel(typename VecT<VB>::type* __restrict__ out,
   stg(out + o, val);
 }
 
+// Rounds an fp32 value to T and back (the value a T tensor would hold).
+template <typename T>
+__device__ __forceinline__ float round_to(float v);
+template <>
+__device__ __forceinline__ float round_to<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float round_to<__half>(float v) {
+  return __half2float(__float2half_rn(v));
+}
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Unpartition + roll back + crop + residual, and the LayerNorm of the result (the
+// MLP half's norm2) in the same pass.  One output token (b, d, h, w) of the cropped
+// volume per L-lane group, kTokensPerGroup tokens per group with all loads in
+// flight first.  out = T(residual + window row), normed = LN(out) in TN, where the
+// norm reads the rounded T values, as a separate norm over the stored tensor would.
+template <typename T, typename TN, int L>
+__global__ void __launch_bounds__(kThreads)
+unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
+                         const T* __restrict__ windows, const T* __restrict__ residual,
+                         const float* __restrict__ gamma, const float* __restrict__ beta,
+                         const BlockGeom g) {
+  constexpr uint32_t kGroups = kThreads / L;
+  const uint32_t sub = threadIdx.x % L;
+  const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
+  uint32_t token[kTokensPerGroup];
+  uint64_t src[kTokensPerGroup];
+  typename Io<T>::Raw rw[kTokensPerGroup][kGroupsPerLane], rr[kTokensPerGroup][kGroupsPerLane];
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    token[j] = first + j * kGroups;
+    src[j] = 0;
+    if (token[j] < g.tokens) {
+      uint32_t t, w, t2, h, b, d, id, ld, ih, lh, iw, lw;
+      g.f_W.divmod(token[j], t, w);
+      g.f_H.divmod(t, t2, h);
+      g.f_D.divmod(t2, b, d);
+      d = (d >= g.sd) ? d - g.sd : d + g.Dp - g.sd;
+      h = (h >= g.sh) ? h - g.sh : h + g.Hp - g.sh;
+      w = (w >= g.sw) ? w - g.sw : w + g.Wp - g.sw;
+      g.f_wd.divmod(d, id, ld);
+      g.f_wh.divmod(h, ih, lh);
+      g.f_ww.divmod(w, iw, lw);
+      const uint32_t win = (id * g.nwh + ih) * g.nww + iw;
+      const uint32_t loc = (ld * g.wh + lh) * g.ww + lw;
+      src[j] = (uint64_t(b) * g.nw + win) * g.N + loc;
+#pragma unroll
+      for (int k = 0; k < kGroupsPerLane; ++k) {
+        const uint32_t grp = sub + k * L;
+        if (grp < g.groups) {
+          rw[j][k] = Io<T>::load(windows + src[j] * g.C + grp * 8);
+          if (residual) rr[j][k] = Io<T>::load(residual + uint64_t(token[j]) * g.C + grp * 8);
+        }
+      }
+    }
+  }
+  const float inv_c = 1.f / float(g.C);
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    const bool live = token[j] < g.tokens;
+    float v[kGroupsPerLane][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (live && grp < g.groups) {
+        Io<T>::to_float(rw[j][k], v[k]);
+        if (residual) {
+          float r[8];
+          Io<T>::to_float(rr[j][k], r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[k][e] = round_to<T>(r[e] + v[k][e]);
+        }
+        Io<T>::store8(out + uint64_t(token[j]) * g.C + grp * 8, v[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += v[k][e];
+      }
+    }
+    const float mean = group_sum<L>(sum) * inv_c;
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (live && grp < g.groups) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float dv = v[k][e] - mean;
+          sq = fmaf(dv, dv, sq);
+        }
+      }
+    }
+    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
+    if (!live) continue;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (grp >= g.groups) continue;
+      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
+      const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
+      const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
+      Io<TN>::store8(normed + uint64_t(token[j]) * g.C + grp * 8, y);
+    }
+  }
+}
+
 int check_geometry(int64_t B, int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
                    const int64_t* ss) {
   const int64_t dims[3] = {D, H, W};
@@ -341,6 +456,9 @@ BlockGeom make_geom(int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* w
   g.f_ww = DivMod32::make(g.ww);
   g.f_wh = DivMod32::make(g.wh);
   g.f_wd = DivMod32::make(g.wd);
+  g.f_W = DivMod32::make(g.W);
+  g.f_H = DivMod32::make(g.H);
+  g.f_D = DivMod32::make(g.D);
   return g;
 }
 
@@ -480,6 +598,90 @@ int launch_unshift_unpartition_crop(void* out, const void* windows, const void* 
       err = launch_crop_vb<__nv_bfloat16, true>(vb, os, wsrc, rs, g, cv, uint32_t(nb), stream);
     }
     if (err != cudaSuccess) return set_cuda_error(err, "unshift_unpartition_crop launch");
+  }
+  return kOk;
+}
+
+
+namespace {
+
+template <typename T, typename TN>
+cudaError_t launch_crop_norm_t(void* out, void* normed, const void* windows, const void* residual,
+                               const float* gamma, const float* beta, const BlockGeom& g,
+                               cudaStream_t stream) {
+  int lanes = 1;
+  while (uint32_t(lanes * kGroupsPerLane) < g.groups) lanes *= 2;
+  const uint32_t per_block = uint32_t(kThreads / lanes) * kTokensPerGroup;
+  const uint32_t blocks = (g.tokens + per_block - 1) / per_block;
+  auto o = static_cast<T*>(out);
+  auto n = static_cast<TN*>(normed);
+  auto wi = static_cast<const T*>(windows);
+  auto re = static_cast<const T*>(residual);
+  switch (lanes) {
+    case 1: unshift_crop_norm_kernel<T, TN, 1><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+    case 2: unshift_crop_norm_kernel<T, TN, 2><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+    case 4: unshift_crop_norm_kernel<T, TN, 4><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+    case 8: unshift_crop_norm_kernel<T, TN, 8><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+    case 16: unshift_crop_norm_kernel<T, TN, 16><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+    default: unshift_crop_norm_kernel<T, TN, 32><<<blocks, kThreads, 0, stream>>>(o, n, wi, re, gamma, beta, g); break;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_crop_norm_n(int norm_dtype, void* out, void* normed, const void* windows,
+                               const void* residual, const float* gamma, const float* beta,
+                               const BlockGeom& g, cudaStream_t stream) {
+  if (norm_dtype == kF32)
+    return launch_crop_norm_t<T, float>(out, normed, windows, residual, gamma, beta, g, stream);
+  if (norm_dtype == kF16)
+    return launch_crop_norm_t<T, __half>(out, normed, windows, residual, gamma, beta, g, stream);
+  return launch_crop_norm_t<T, __nv_bfloat16>(out, normed, windows, residual, gamma, beta, g,
+                                               stream);
+}
+
+}  // namespace
+
+int launch_unshift_unpartition_crop_norm(void* out, void* normed, int norm_dtype,
+                                         const void* windows, const void* residual, int dtype,
+                                         const float* gamma, const float* beta, float eps,
+                                         int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                                         const int64_t* ws, const int64_t* ss,
+                                         cudaStream_t stream) {
+  if (int e = check_geometry(B, D, H, W, C, ws, ss)) return e;
+  if (C == 0 || C % 8 != 0 || C > kMaxC)
+    return set_error(kErrUnsupported,
+                     "unshift_unpartition_crop_norm_3d needs C a multiple of 8 and at most 768");
+  if (B == 0) return kOk;
+  if (!out || !normed || !windows || !gamma || !beta)
+    return set_error(kErrInvalid, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(normed) |
+       reinterpret_cast<uintptr_t>(windows) | reinterpret_cast<uintptr_t>(residual) |
+       reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15u)
+    return set_error(kErrInvalid, "tensors must be 16-byte aligned");
+  BlockGeom g = make_geom(D, H, W, C, ws, ss);
+  g.eps = eps;
+  const uint64_t per_batch = uint64_t(D) * H * W;
+  const uint64_t bmax = ((uint64_t(1) << 31) - 1) / per_batch;
+  if (bmax == 0) return set_error(kErrInvalid, "one batch entry is too large for one launch");
+  const int64_t row = C * dtype_size(dtype), nrow = C * dtype_size(norm_dtype);
+  for (int64_t b0 = 0; b0 < B; b0 += int64_t(bmax)) {
+    const uint64_t nb = uint64_t(B - b0) < bmax ? uint64_t(B - b0) : bmax;
+    g.tokens = uint32_t(nb * per_batch);
+    void* os = static_cast<uint8_t*>(out) + uint64_t(b0) * per_batch * row;
+    void* ns = static_cast<uint8_t*>(normed) + uint64_t(b0) * per_batch * nrow;
+    const void* wsrc =
+        static_cast<const uint8_t*>(windows) + uint64_t(b0) * g.nw * g.N * uint64_t(row);
+    const void* rs =
+        residual ? static_cast<const uint8_t*>(residual) + uint64_t(b0) * per_batch * row : nullptr;
+    cudaError_t err;
+    if (dtype == kF32)
+      err = launch_crop_norm_n<float>(norm_dtype, os, ns, wsrc, rs, gamma, beta, g, stream);
+    else if (dtype == kF16)
+      err = launch_crop_norm_n<__half>(norm_dtype, os, ns, wsrc, rs, gamma, beta, g, stream);
+    else
+      err = launch_crop_norm_n<__nv_bfloat16>(norm_dtype, os, ns, wsrc, rs, gamma, beta, g, stream);
+    if (err != cudaSuccess) return set_cuda_error(err, "unshift_unpartition_crop_norm launch");
   }
   return kOk;
 }

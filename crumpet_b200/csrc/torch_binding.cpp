@@ -247,6 +247,45 @@ void unshift_unpartition_crop_3d(at::Tensor& output, const at::Tensor& windows,
                                                ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
 }
 
+void unshift_unpartition_crop_norm_3d(at::Tensor& output, at::Tensor& normed,
+                                      const at::Tensor& windows,
+                                      const c10::optional<at::Tensor>& residual,
+                                      const at::Tensor& weight, const at::Tensor& bias, double eps,
+                                      int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
+                                      int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+                                      int64_t ss_h, int64_t ss_w) {
+  check_cuda_contig(windows, "windows");
+  check_cuda_contig(output, "output");
+  check_cuda_contig(normed, "normed");
+  check_cuda_contig(weight, "weight");
+  check_cuda_contig(bias, "bias");
+  TORCH_CHECK(output.scalar_type() == windows.scalar_type(), "output and windows dtypes differ");
+  TORCH_CHECK(weight.scalar_type() == at::kFloat && bias.scalar_type() == at::kFloat &&
+                  weight.numel() == C && bias.numel() == C,
+              "weight and bias must be float32 tensors of C elements");
+  const c10::cuda::CUDAGuard guard(windows.device());
+  const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
+                                 ws_w);
+  TORCH_CHECK(windows.dim() == 3 && windows.size(0) == B * nw &&
+                  windows.size(1) == ws_d * ws_h * ws_w && windows.size(2) == C,
+              "windows must have shape [B * num_windows(padded), volume, C]");
+  TORCH_CHECK(output.numel() == B * D * H * W * C && normed.numel() == B * D * H * W * C,
+              "output and normed must have B*D*H*W*C elements");
+  const void* res = nullptr;
+  if (residual.has_value() && residual->defined()) {
+    check_cuda_contig(*residual, "residual");
+    TORCH_CHECK(residual->scalar_type() == windows.scalar_type(),
+                "residual must have the dtype of windows");
+    TORCH_CHECK(residual->numel() == B * D * H * W * C, "residual must have B*D*H*W*C elements");
+    res = residual->data_ptr();
+  }
+  if (output.numel() == 0) return;
+  check_rc(crumpet_unshift_unpartition_crop_norm_3d(
+      output.data_ptr(), normed.data_ptr(), dtype_code(normed), windows.data_ptr(), res,
+      dtype_code(windows), weight.data_ptr<float>(), bias.data_ptr<float>(), static_cast<float>(eps),
+      B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
+}
+
 std::vector<int64_t> roi_list(at::IntArrayRef starts, at::IntArrayRef roi) {
   TORCH_CHECK(roi.size() == 3, "roi takes three values");
   TORCH_CHECK(starts.size() % 3 == 0, "starts must hold (z, y, x) triples");
@@ -360,6 +399,11 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "unshift_unpartition_crop_3d(Tensor! output, Tensor windows, Tensor? residual, int B, int D, "
       "int H, int W, int C, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
       kTags);
+  ops.def(
+      "unshift_unpartition_crop_norm_3d(Tensor(a!) output, Tensor(b!) normed, Tensor windows, "
+      "Tensor? residual, Tensor weight, Tensor bias, float eps, int B, int D, int H, int W, int C, "
+      "int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
+      kTags);
   ops.def("roi_gather(Tensor! out, Tensor volume, int[] starts, int[] roi) -> ()", kTags);
   ops.def("roi_accumulate(Tensor! acc, Tensor pred, int[] starts, int[] roi) -> ()", kTags);
   ops.def(
@@ -381,6 +425,7 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
   ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
+  ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);
   ops.impl("roi_gather", &roi_gather);
   ops.impl("roi_accumulate", &roi_accumulate);
   ops.impl("roi_argmax", &roi_argmax);

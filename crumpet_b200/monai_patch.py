@@ -10,8 +10,9 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   and the unpartition, roll back and crop in another
   (``unshift_unpartition_crop_3d``);
 * ``SwinTransformerBlock.forward`` (not patched by the reference): in eval
-  mode without checkpointing, the residual add of the attention half is folded
-  into the unpartition + crop kernel;
+  mode without checkpointing, the residual add of the attention half and the
+  block's norm2 are folded into the unpartition + crop kernel
+  (``unshift_unpartition_crop_norm_3d``), which hands norm2(x) to the MLP;
 * ``BasicLayer.forward``: channels-last permute, the cached shifted-window mask
   from ``compute_attn_mask_3d`` on the padded grid, blocks, downsample
   (reference :201-232);
@@ -49,7 +50,11 @@ import torch
 import torch.nn.functional as F
 
 from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpartition_3d
-from .block_fusion import norm_shift_partition_3d, unshift_unpartition_crop_3d
+from .block_fusion import (
+    norm_shift_partition_3d,
+    unshift_unpartition_crop_3d,
+    unshift_unpartition_crop_norm_3d,
+)
 from .fused_attention import fused_swin_attention, swin_window_attention_qkv
 
 _STATE: dict[str, Any] = {}
@@ -140,9 +145,12 @@ def _crop_fusable(windows: torch.Tensor) -> bool:
     )
 
 
-def _attention_branch(self, x, mask_matrix, swin, residual=None):
+def _attention_branch(self, x, mask_matrix, swin, residual=None, next_norm=None):
     """norm1 -> pad -> roll + partition -> attn -> unpartition + roll back -> crop
-    (reference monai_patch.py:72-114), plus ``residual +`` when given."""
+    (reference monai_patch.py:72-114), plus ``residual +`` when given.
+
+    With ``next_norm`` (the block's norm2) the result is ``(out, next_norm(out))``
+    when both come out of one fused kernel, else just ``out``."""
     b, d, h, w, c = x.shape
     window_size, shift_size = swin.get_window_size((d, h, w), self.window_size, self.shift_size)
     window_size = _as_triple(window_size)
@@ -161,6 +169,12 @@ def _attention_branch(self, x, mask_matrix, swin, residual=None):
     if _crop_fusable(attn_windows):
         fuse_res = (residual is not None and residual.dtype == attn_windows.dtype
                     and residual.device == attn_windows.device and _no_grad_needed(residual))
+        if (next_norm is not None and (fuse_res or residual is None)
+                and _norm_fusable(next_norm, attn_windows)):
+            return unshift_unpartition_crop_norm_3d(
+                attn_windows, b, d, h, w, c, window_size, shift_size, next_norm.weight,
+                next_norm.bias, next_norm.eps, residual=residual,
+                norm_dtype=_norm_out_dtype(attn_windows))
         out = unshift_unpartition_crop_3d(attn_windows, b, d, h, w, c, window_size, shift_size,
                                           residual=residual if fuse_res else None)
         if residual is not None and not fuse_res:
@@ -187,7 +201,8 @@ def _patched_block_forward(original, swin):
     """``x + attention_branch(x)`` with the residual folded into the crop, then the MLP half.
 
     Inference only (eval mode, no activation checkpointing): there drop_path is
-    the identity and the block is ``x = x + part1(x); x = x + part2(x)``.
+    the identity and the block is ``x = x + part1(x); x = x + mlp(norm2(x))``.  The
+    crop kernel also writes ``norm2(x)`` when norm2 is a LayerNorm it can fuse.
     """
 
     @functools.wraps(original)
@@ -195,8 +210,12 @@ def _patched_block_forward(original, swin):
         if (x.dim() != 5 or self.training or getattr(self, "use_checkpoint", False)
                 or not _block_fusion_enabled()):
             return original(self, x, mask_matrix)
-        x = _attention_branch(self, x, mask_matrix, swin, residual=x)
-        return x + self.forward_part2(x)
+        norm2 = getattr(self, "norm2", None) if hasattr(self, "mlp") else None
+        out = _attention_branch(self, x, mask_matrix, swin, residual=x, next_norm=norm2)
+        if isinstance(out, tuple):
+            x, x_norm2 = out
+            return x + self.mlp(x_norm2)
+        return out + self.forward_part2(out)
 
     return forward
 

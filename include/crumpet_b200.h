@@ -195,6 +195,23 @@ CRUMPET_API int crumpet_unshift_unpartition_crop_3d(void* output, const void* wi
                                                     void* stream);
 
 /*
+ * crumpet_unshift_unpartition_crop_3d followed by the LayerNorm of its result, in
+ * one pass: output = unpartition(windows)[:, :D, :H, :W] (+ residual), rounded to
+ * dtype, and normed = LN(output) over C with fp32 weight/bias and eps, written in
+ * norm_dtype (the LN reads the rounded output values).  In a Swin block this is
+ * the residual add of the attention half and the norm2 that opens the MLP half.
+ * All pointers 16-byte aligned, C a multiple of 8 and at most 768; residual may be
+ * NULL.  No reference counterpart: the reference leaves the crop, the residual add
+ * and norm2 to eager torch (torch-ext/crumpet/monai_patch.py:108-111 and the MONAI
+ * block around it).
+ */
+CRUMPET_API int crumpet_unshift_unpartition_crop_norm_3d(
+    void* output, void* normed, int norm_dtype, const void* windows, const void* residual,
+    int dtype, const float* weight, const float* bias, float eps, int64_t B, int64_t D,
+    int64_t H, int64_t W, int64_t C, int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d,
+    int64_t ss_h, int64_t ss_w, void* stream);
+
+/*
  * Sliding-window ROI inference around the network forward.  The reference drives
  * its patched network with MONAI's sliding_window_inference (a third-party
  * Python function, called at torch-ext/crumpet/demo_btcv.py:98-129 with

@@ -68,6 +68,7 @@ def test_dispatcher_ops_keep_reference_schemas():
     assert str(ops.norm_shift_partition_3d.default._schema) == (
         "crumpet_ops::norm_shift_partition_3d(Tensor($0! -> ) output, Tensor x, Tensor weight, "
         "Tensor bias, float eps, int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()")
+    assert "Tensor(b!) normed" in str(ops.unshift_unpartition_crop_norm_3d.default._schema)
     assert str(ops.unshift_unpartition_crop_3d.default._schema) == (
         "crumpet_ops::unshift_unpartition_crop_3d(Tensor($0! -> ) output, Tensor windows, "
         "Tensor? residual, int B, int D, int H, int W, int C, int ws_d, int ws_h, int ws_w, "
@@ -207,6 +208,13 @@ def test_block_fusion_capi_validation():
     assert rc == 3
     rc = crop(null, null, null, 1, 0, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
     assert rc == 0
+    cnorm = lib.crumpet_unshift_unpartition_crop_norm_3d
+    rc = cnorm(null, null, 1, null, null, 1, null, null, 1e-5, 1, 13, 10, 9, 44, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 3 and "multiple of 8" in _ops.last_error()
+    rc = cnorm(null, null, 1, null, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = cnorm(null, null, 9, null, null, 1, null, null, 1e-5, 1, 13, 10, 9, 48, 7, 7, 7, 3, 3, 3, null)
+    assert rc == 1 and "float32" in _ops.last_error()
 
 
 def test_block_fusion_wrappers_validate_and_have_no_cpu_path():

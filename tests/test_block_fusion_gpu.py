@@ -192,3 +192,56 @@ def test_patched_block_matches_unfused_glue(shift, cuda_device, monkeypatch):
     diff = (fused.float() - unfused.float()).abs()
     # only the LayerNorm's last-place rounding differs between the two glues
     assert diff.max().item() < 2e-2 and diff.mean().item() < 1e-4
+
+
+@pytest.mark.parametrize("norm_dtype", [torch.float16, torch.float32], ids=["norm_f16", "norm_f32"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16", "bf16"])
+@pytest.mark.parametrize("stage", STAGES, ids=STAGE_IDS)
+def test_unpartition_crop_residual_norm(stage, dtype, norm_dtype, cuda_device):
+    """The residual add of the attention half and norm2 in the crop pass: ``out``
+    bit-exact (torch's add), ``normed`` the float64 LayerNorm of ``out`` within
+    one unit in the last place."""
+    B, D, H, W, C, window, shift = stage
+    if C >= 192 and dtype != torch.float16:
+        pytest.skip("dtype matrix covered at the smaller stages")
+    ws, ss = OB.window_geometry((D, H, W), window, shift)
+    (Dp, Hp, Wp), nw, n = crumpet.block_fusion.padded_geometry(D, H, W, ws)
+    windows = I.randn(90 + C, (B * nw, n, C), "float32").to(dtype)
+    residual = I.randn(91 + C, (B, D, H, W, C), "float32").to(dtype)
+    w = 1.0 + 0.2 * I.randn(92 + C, (C,), "float32")
+    b = 0.1 * I.randn(93 + C, (C,), "float32")
+    raw = windows.view(torch.int16) if dtype == torch.bfloat16 else windows
+    crop = torch.from_numpy(OB.unshift_unpartition_crop(raw.numpy(), B, D, H, W, C, ws, ss))
+    crop = crop.view(torch.bfloat16) if dtype == torch.bfloat16 else crop
+    out, normed = crumpet.unshift_unpartition_crop_norm_3d(
+        windows.to(cuda_device), B, D, H, W, C, ws, ss, w.to(cuda_device), b.to(cuda_device), 1e-5,
+        residual=residual.to(cuda_device), norm_dtype=norm_dtype)
+    torch.cuda.synchronize()
+    want_out = residual + crop
+    assert torch.equal(out.cpu(), want_out)
+    want = OB.layer_norm(want_out.double().numpy(), w.numpy(), b.numpy(), 1e-5)
+    g = normed.double().cpu().numpy()
+    rel, atol = TOL[norm_dtype]
+    bad = np.abs(g - want) > np.abs(want) * rel + atol
+    assert not bad.any(), (np.abs(g - want).max(), int(bad.sum()))
+
+
+def test_unpartition_crop_norm_through_the_c_abi(cuda_device):
+    B, D, H, W, C = 2, 13, 10, 9, 48
+    ws, ss = (7, 7, 7), (3, 3, 3)
+    (Dp, Hp, Wp), nw, n = crumpet.block_fusion.padded_geometry(D, H, W, ws)
+    windows = torch.randn((B * nw, n, C), device=cuda_device).half()
+    res = torch.randn((B, D, H, W, C), device=cuda_device).half()
+    w = torch.rand(C, device=cuda_device) + 0.5
+    b = torch.randn(C, device=cuda_device) * 0.1
+    want_out, want_norm = crumpet.unshift_unpartition_crop_norm_3d(windows, B, D, H, W, C, ws, ss, w,
+                                                                   b, 1e-5, residual=res)
+    out, normed = torch.empty_like(res), torch.empty_like(res)
+    rc = _ops.capi().crumpet_unshift_unpartition_crop_norm_3d(
+        ptr(out), ptr(normed), DTYPE_CODE[torch.float16], ptr(windows), ptr(res),
+        DTYPE_CODE[torch.float16], ptr(w), ptr(b), 1e-5, B, D, H, W, C, *ws, *ss, stream_ptr())
+    assert rc == 0, _ops.last_error()
+    assert torch.equal(out, want_out) and torch.equal(normed, want_norm)
+    # norm2 of the block, computed the eager way, agrees to fp16 rounding
+    eager = torch.nn.functional.layer_norm(want_out.float(), (C,), w, b, 1e-5).half()
+    assert (normed.float() - eager.float()).abs().max().item() <= 4e-3
