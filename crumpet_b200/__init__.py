@@ -48,6 +48,7 @@ _OP_NAMES = (
     "norm_shift_partition_3d",
     "unshift_unpartition_crop_3d",
     "unshift_unpartition_crop_norm_3d",
+    "patch_merge_norm_3d",
 )
 
 
@@ -272,6 +273,7 @@ from .block_fusion import (  # noqa: E402
     norm_shift_partition_3d,
     unshift_unpartition_crop_3d,
     unshift_unpartition_crop_norm_3d,
+    patch_merge_norm_3d,
 )
 
 
@@ -303,6 +305,7 @@ __all__ = [
     "norm_shift_partition_3d",
     "unshift_unpartition_crop_3d",
     "unshift_unpartition_crop_norm_3d",
+    "patch_merge_norm_3d",
     "patch_monai_swin_unetr",
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",

@@ -12,7 +12,9 @@ on either side of the attention:
 * :func:`unshift_unpartition_crop_3d` -- window reverse on the padded grid +
   roll by ``+shift`` + crop, optionally adding the block's residual;
 * :func:`unshift_unpartition_crop_norm_3d` -- the same plus the LayerNorm of the
-  result (the block's ``norm2``, which opens its MLP half).
+  result (the block's ``norm2``, which opens its MLP half);
+* :func:`patch_merge_norm_3d` -- the 2x2x2 neighbour concatenation of a stage's
+  patch merging and its LayerNorm (the reduction Linear follows as a GEMM).
 
 Both are inference ops (no backward): they raise when autograd would need a
 gradient through them.  The MONAI patch uses them only outside autograd.
@@ -233,3 +235,53 @@ def unshift_unpartition_crop_norm_3d(
                                                        *shift_size)
     _prof.count("unshift_unpartition_crop_norm_3d")
     return out, normed
+
+
+# Neighbour order of the concatenation in patch merging: (i, j, k) offsets along
+# (D, H, W) for the eight parts.  itertools.product order (MONAI's PatchMergingV2
+# and the bundled network's PatchMerging).
+PRODUCT_ORDER = tuple((i, j, k) for i in range(2) for j in range(2) for k in range(2))
+
+
+def patch_merge_norm_3d(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor,
+    eps: float,
+    order=PRODUCT_ORDER,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """``layer_norm(cat([x[:, i::2, j::2, k::2] for (i, j, k) in order], -1))`` in one pass.
+
+    ``x`` is ``[B, D, H, W, C]``; odd dims are zero-padded at the far end (as the
+    merging module's ``F.pad``); the result is ``[B, ceil(D/2), ceil(H/2),
+    ceil(W/2), 8C]`` in ``out_dtype`` (default ``x.dtype``), the norm computed in
+    fp32.  C must be a multiple of 8 with 8C at most 768.
+    """
+    if x.ndim != 5:
+        raise ValueError("x must have shape [B, D, H, W, C]")
+    order = tuple(tuple(int(v) for v in o) for o in order)
+    if len(order) != 8 or any(len(o) != 3 or min(o) < 0 or max(o) > 1 for o in order):
+        raise ValueError("order must hold eight (i, j, k) offsets in {0, 1}")
+    _check_dtype(x.dtype)
+    out_dtype = x.dtype if out_dtype is None else out_dtype
+    _check_dtype(out_dtype)
+    B, D, H, W, C = (int(v) for v in x.shape)
+    if C % 8 or 8 * C > 768 or C == 0:
+        raise ValueError("patch_merge_norm_3d needs C a multiple of 8 and 8C at most 768")
+    if tuple(weight.shape) != (8 * C,) or tuple(bias.shape) != (8 * C,):
+        raise ValueError("weight and bias must have shape [8C]")
+    shape = (B, -(-D // 2), -(-H // 2), -(-W // 2), 8 * C)
+    if x.device.type == "meta":
+        return torch.empty(shape, dtype=out_dtype, device=x.device)
+    if x.device.type != "cuda":
+        raise RuntimeError(f"crumpet_b200 runs patch_merge_norm_3d on CUDA devices only (got {x.device})")
+    if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad or bias.requires_grad):
+        raise RuntimeError("patch_merge_norm_3d has no backward; call it under torch.no_grad()")
+    out = torch.empty(shape, dtype=out_dtype, device=x.device)
+    w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
+    b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
+    codes = [i | (j << 1) | (k << 2) for i, j, k in order]
+    _native.require().patch_merge_norm_3d(out, _aligned(x, 16), w, b, float(eps), codes)
+    _prof.count("patch_merge_norm_3d")
+    return out

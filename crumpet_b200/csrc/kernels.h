@@ -53,6 +53,13 @@ int launch_unshift_unpartition_crop_norm(void* out, void* normed, int norm_dtype
                                          int64_t B, int64_t D, int64_t H, int64_t W, int64_t C,
                                          const int64_t* ws, const int64_t* ss, cudaStream_t stream);
 
+// Patch merging: out [B, ceil(D/2), ceil(H/2), ceil(W/2), 8C] = LayerNorm over the 8
+// neighbours' channels concatenated in the order parts[0..7] (code i | j<<1 | k<<2 for
+// the offset (i, j, k)), zero rows past odd dims.  fp32 gamma/beta of 8C.
+int launch_patch_merge_norm(void* out, int out_dtype, const void* x, int in_dtype,
+                            const float* gamma, const float* beta, float eps, int64_t B, int64_t D,
+                            int64_t H, int64_t W, int64_t C, const int* parts, cudaStream_t stream);
+
 // Sliding-window ROI inference: crop a batch of ROIs, accumulate their predictions,
 // normalise by the ROI count and take the arg-max.  `starts` is a HOST array of
 // n (z, y, x) triples (n <= 64), passed to the kernels by value.

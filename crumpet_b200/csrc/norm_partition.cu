@@ -411,6 +411,106 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
   }
 }
 
+// Patch merging: out[b, d2, h2, w2, :] = LN(cat_p x[b, 2 d2 + i_p, 2 h2 + j_p, 2 w2 + k_p, :])
+// over the 8C concatenated channels (part order from `parts`, zero rows past odd
+// dims, as the module's F.pad).  One output voxel per L-lane group.
+struct MergeGeom {
+  uint32_t D, H, W, C, D2, H2, W2, groups, part_groups;  // groups = 8C/8, part_groups = C/8
+  uint32_t tokens;
+  DivMod32 f_W2, f_H2, f_D2, f_pg;
+  uint32_t parts;  // 3 bits (i | j << 1 | k << 2) per part, part p at bits 3p..3p+2
+  float eps;
+};
+
+template <typename TIn, typename TOut, int L>
+__global__ void __launch_bounds__(kThreads)
+patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
+                        const float* __restrict__ gamma, const float* __restrict__ beta,
+                        const MergeGeom g) {
+  constexpr uint32_t kGroups = kThreads / L;
+  const uint32_t sub = threadIdx.x % L;
+  const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
+  uint32_t token[kTokensPerGroup];
+  uint32_t inb[kTokensPerGroup];  // bit k: channel group sub + k*L lies inside the volume
+  typename Io<TIn>::Raw raw[kTokensPerGroup][kGroupsPerLane];
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    token[j] = first + j * kGroups;
+    inb[j] = 0;
+    if (token[j] < g.tokens) {
+      uint32_t t, w2, t2, h2, b, d2;
+      g.f_W2.divmod(token[j], t, w2);
+      g.f_H2.divmod(t, t2, h2);
+      g.f_D2.divmod(t2, b, d2);
+#pragma unroll
+      for (int k = 0; k < kGroupsPerLane; ++k) {
+        const uint32_t grp = sub + k * L;
+        if (grp < g.groups) {
+          uint32_t part, cg;
+          g.f_pg.divmod(grp, part, cg);
+          const uint32_t code = (g.parts >> (3 * part)) & 7u;
+          const uint32_t d = 2 * d2 + (code & 1u), h = 2 * h2 + ((code >> 1) & 1u),
+                         w = 2 * w2 + ((code >> 2) & 1u);
+          if (d < g.D && h < g.H && w < g.W) {
+            const uint64_t v = ((uint64_t(b) * g.D + d) * g.H + h) * g.W + w;
+            raw[j][k] = Io<TIn>::load(x + v * g.C + cg * 8);
+            inb[j] |= 1u << k;
+          }
+        }
+      }
+    }
+  }
+  const float inv_c = 1.f / float(8 * g.C);
+#pragma unroll
+  for (int j = 0; j < kTokensPerGroup; ++j) {
+    float v[kGroupsPerLane][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      if ((inb[j] >> k) & 1u) {
+        Io<TIn>::to_float(raw[j][k], v[k]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[k][e] = 0.f;  // padding rows (and unused groups)
+      }
+      if (sub + k * L < g.groups) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sum += v[k][e];
+      }
+    }
+    const float mean = group_sum<L>(sum) * inv_c;
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      if (sub + k * L < g.groups) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float dv = v[k][e] - mean;
+          sq = fmaf(dv, dv, sq);
+        }
+      }
+    }
+    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
+    if (token[j] >= g.tokens) continue;
+    TOut* dst = out + uint64_t(token[j]) * (8 * g.C);
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (grp >= g.groups) continue;
+      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
+      const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
+      const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
+      Io<TOut>::store8(dst + grp * 8, y);
+    }
+  }
+}
+
 int check_geometry(int64_t B, int64_t D, int64_t H, int64_t W, int64_t C, const int64_t* ws,
                    const int64_t* ss) {
   const int64_t dims[3] = {D, H, W};
@@ -682,6 +782,93 @@ int launch_unshift_unpartition_crop_norm(void* out, void* normed, int norm_dtype
     else
       err = launch_crop_norm_n<__nv_bfloat16>(norm_dtype, os, ns, wsrc, rs, gamma, beta, g, stream);
     if (err != cudaSuccess) return set_cuda_error(err, "unshift_unpartition_crop_norm launch");
+  }
+  return kOk;
+}
+
+
+namespace {
+
+template <typename TIn, typename TOut>
+cudaError_t launch_merge_t(void* out, const void* x, const float* gamma, const float* beta,
+                           const MergeGeom& g, cudaStream_t stream) {
+  int lanes = 1;
+  while (uint32_t(lanes * kGroupsPerLane) < g.groups) lanes *= 2;
+  const uint32_t per_block = uint32_t(kThreads / lanes) * kTokensPerGroup;
+  const uint32_t blocks = (g.tokens + per_block - 1) / per_block;
+  auto o = static_cast<TOut*>(out);
+  auto xi = static_cast<const TIn*>(x);
+  switch (lanes) {
+    case 1: patch_merge_norm_kernel<TIn, TOut, 1><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 2: patch_merge_norm_kernel<TIn, TOut, 2><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 4: patch_merge_norm_kernel<TIn, TOut, 4><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 8: patch_merge_norm_kernel<TIn, TOut, 8><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 16: patch_merge_norm_kernel<TIn, TOut, 16><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    default: patch_merge_norm_kernel<TIn, TOut, 32><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+  }
+  return cudaGetLastError();
+}
+
+template <typename TIn>
+cudaError_t launch_merge_out(int out_dtype, void* out, const void* x, const float* gamma,
+                             const float* beta, const MergeGeom& g, cudaStream_t stream) {
+  if (out_dtype == kF32) return launch_merge_t<TIn, float>(out, x, gamma, beta, g, stream);
+  if (out_dtype == kF16) return launch_merge_t<TIn, __half>(out, x, gamma, beta, g, stream);
+  return launch_merge_t<TIn, __nv_bfloat16>(out, x, gamma, beta, g, stream);
+}
+
+}  // namespace
+
+int launch_patch_merge_norm(void* out, int out_dtype, const void* x, int in_dtype,
+                            const float* gamma, const float* beta, float eps, int64_t B, int64_t D,
+                            int64_t H, int64_t W, int64_t C, const int* parts,
+                            cudaStream_t stream) {
+  if (B < 0 || D <= 0 || H <= 0 || W <= 0) return set_error(kErrInvalid, "bad volume dims");
+  if (C <= 0 || C % 8 != 0 || 8 * C > kMaxC)
+    return set_error(kErrUnsupported, "patch_merge_norm_3d needs C a multiple of 8 and 8C <= 768");
+  if (D * H * W >= (int64_t(1) << 31)) return set_error(kErrInvalid, "D*H*W must be below 2^31");
+  if (!parts) return set_error(kErrInvalid, "null part table");
+  MergeGeom g{};
+  g.parts = 0;
+  for (int p = 0; p < 8; ++p) {
+    if (parts[p] < 0 || parts[p] > 7) return set_error(kErrInvalid, "part codes are 0..7");
+    g.parts |= uint32_t(parts[p]) << (3 * p);
+  }
+  if (B == 0) return kOk;
+  if (!out || !x || !gamma || !beta) return set_error(kErrInvalid, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
+       reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15u)
+    return set_error(kErrInvalid, "tensors must be 16-byte aligned");
+  g.D = uint32_t(D);
+  g.H = uint32_t(H);
+  g.W = uint32_t(W);
+  g.C = uint32_t(C);
+  g.D2 = (g.D + 1) / 2;
+  g.H2 = (g.H + 1) / 2;
+  g.W2 = (g.W + 1) / 2;
+  g.groups = g.C;  // 8C channels in groups of 8
+  g.part_groups = g.C / 8;
+  g.f_W2 = DivMod32::make(g.W2);
+  g.f_H2 = DivMod32::make(g.H2);
+  g.f_D2 = DivMod32::make(g.D2);
+  g.f_pg = DivMod32::make(g.part_groups);
+  g.eps = eps;
+  const uint64_t per_batch = uint64_t(g.D2) * g.H2 * g.W2;
+  const uint64_t bmax = ((uint64_t(1) << 31) - 1) / per_batch;
+  const int64_t in_row = C * dtype_size(in_dtype), out_row = 8 * C * dtype_size(out_dtype);
+  for (int64_t b0 = 0; b0 < B; b0 += int64_t(bmax)) {
+    const uint64_t nb = uint64_t(B - b0) < bmax ? uint64_t(B - b0) : bmax;
+    g.tokens = uint32_t(nb * per_batch);
+    const void* xs = static_cast<const uint8_t*>(x) + uint64_t(b0) * D * H * W * in_row;
+    void* os = static_cast<uint8_t*>(out) + uint64_t(b0) * per_batch * out_row;
+    cudaError_t err;
+    if (in_dtype == kF32)
+      err = launch_merge_out<float>(out_dtype, os, xs, gamma, beta, g, stream);
+    else if (in_dtype == kF16)
+      err = launch_merge_out<__half>(out_dtype, os, xs, gamma, beta, g, stream);
+    else
+      err = launch_merge_out<__nv_bfloat16>(out_dtype, os, xs, gamma, beta, g, stream);
+    if (err != cudaSuccess) return set_cuda_error(err, "patch_merge_norm launch");
   }
   return kOk;
 }

@@ -286,6 +286,32 @@ void unshift_unpartition_crop_norm_3d(at::Tensor& output, at::Tensor& normed,
       B, D, H, W, C, ws_d, ws_h, ws_w, ss_d, ss_h, ss_w, cur_stream(windows)));
 }
 
+void patch_merge_norm_3d(at::Tensor& output, const at::Tensor& x, const at::Tensor& weight,
+                         const at::Tensor& bias, double eps, at::IntArrayRef parts) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(output, "output");
+  check_cuda_contig(weight, "weight");
+  check_cuda_contig(bias, "bias");
+  TORCH_CHECK(x.dim() == 5, "x must have shape [B, D, H, W, C]");
+  TORCH_CHECK(parts.size() == 8, "parts takes eight neighbour codes");
+  const int64_t B = x.size(0), D = x.size(1), H = x.size(2), W = x.size(3), C = x.size(4);
+  TORCH_CHECK(weight.scalar_type() == at::kFloat && bias.scalar_type() == at::kFloat &&
+                  weight.numel() == 8 * C && bias.numel() == 8 * C,
+              "weight and bias must be float32 tensors of 8C elements");
+  TORCH_CHECK(output.dim() == 5 && output.size(0) == B && output.size(1) == (D + 1) / 2 &&
+                  output.size(2) == (H + 1) / 2 && output.size(3) == (W + 1) / 2 &&
+                  output.size(4) == 8 * C,
+              "output must have shape [B, ceil(D/2), ceil(H/2), ceil(W/2), 8C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (output.numel() == 0) return;
+  int codes[8];
+  for (int p = 0; p < 8; ++p) codes[p] = static_cast<int>(parts[p]);
+  check_rc(crumpet_patch_merge_norm_3d(output.data_ptr(), dtype_code(output), x.data_ptr(),
+                                       dtype_code(x), weight.data_ptr<float>(),
+                                       bias.data_ptr<float>(), static_cast<float>(eps), B, D, H, W,
+                                       C, codes, cur_stream(x)));
+}
+
 std::vector<int64_t> roi_list(at::IntArrayRef starts, at::IntArrayRef roi) {
   TORCH_CHECK(roi.size() == 3, "roi takes three values");
   TORCH_CHECK(starts.size() % 3 == 0, "starts must hold (z, y, x) triples");
@@ -404,6 +430,10 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "Tensor? residual, Tensor weight, Tensor bias, float eps, int B, int D, int H, int W, int C, "
       "int ws_d, int ws_h, int ws_w, int ss_d, int ss_h, int ss_w) -> ()",
       kTags);
+  ops.def(
+      "patch_merge_norm_3d(Tensor! output, Tensor x, Tensor weight, Tensor bias, float eps, "
+      "int[] parts) -> ()",
+      kTags);
   ops.def("roi_gather(Tensor! out, Tensor volume, int[] starts, int[] roi) -> ()", kTags);
   ops.def("roi_accumulate(Tensor! acc, Tensor pred, int[] starts, int[] roi) -> ()", kTags);
   ops.def(
@@ -426,6 +456,7 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
   ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);
+  ops.impl("patch_merge_norm_3d", &patch_merge_norm_3d);
   ops.impl("roi_gather", &roi_gather);
   ops.impl("roi_accumulate", &roi_accumulate);
   ops.impl("roi_argmax", &roi_argmax);

@@ -15,7 +15,10 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   (``unshift_unpartition_crop_norm_3d``), which hands norm2(x) to the MLP;
 * ``BasicLayer.forward``: channels-last permute, the cached shifted-window mask
   from ``compute_attn_mask_3d`` on the padded grid, blocks, downsample
-  (reference :201-232);
+  (reference :201-232); a recognised patch merging (neighbour concatenation in
+  itertools.product order: MONAI's PatchMergingV2 or the bundled module) runs as
+  one gather + LayerNorm kernel and a channels-first reduction GEMM, which also
+  removes the final permute copy;
 * ``WindowAttention.forward``: qkv Linear -> fused tcgen05 window attention ->
   proj Linear (reference :117-198), falling back to the module's own eager
   forward in training, with attention dropout, for head dims other than 16
@@ -51,6 +54,8 @@ import torch.nn.functional as F
 
 from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpartition_3d
 from .block_fusion import (
+    PRODUCT_ORDER,
+    patch_merge_norm_3d,
     norm_shift_partition_3d,
     unshift_unpartition_crop_3d,
     unshift_unpartition_crop_norm_3d,
@@ -261,6 +266,47 @@ def _patched_window_attention_forward(original):
     return forward
 
 
+def _merge_order(ds):
+    """Neighbour order of a recognised patch-merging module, or None (then eager)."""
+    name = type(ds).__name__
+    if name == "PatchMergingV2" or (name == "PatchMerging"
+                                    and type(ds).__module__ == "crumpet_b200.swin_unetr"):
+        return PRODUCT_ORDER
+    return None
+
+
+def _merge_fusable(ds, x: torch.Tensor) -> bool:
+    norm, red = getattr(ds, "norm", None), getattr(ds, "reduction", None)
+    c = x.shape[-1]
+    return (
+        _block_fusion_enabled()
+        and _merge_order(ds) is not None
+        and isinstance(norm, torch.nn.LayerNorm)
+        and norm.weight is not None
+        and norm.bias is not None
+        and tuple(norm.normalized_shape) == (8 * c,)
+        and isinstance(red, torch.nn.Linear)
+        and red.bias is None
+        and red.in_features == 8 * c
+        and c % 8 == 0
+        and 8 * c <= 768
+        and x.is_cuda
+        and x.dtype in _FUSED_DTYPES
+        and _no_grad_needed(x, norm.weight, norm.bias, red.weight)
+    )
+
+
+def _merge_channels_first(ds, x: torch.Tensor) -> torch.Tensor:
+    """Patch merging of channels-last ``x`` returned channels-first: the neighbour
+    concatenation and LayerNorm in one kernel, then the reduction Linear computed as
+    ``W @ X^T`` so its output is already [B, 2C, D', H', W'] (no permute copy)."""
+    xm = patch_merge_norm_3d(x, ds.norm.weight, ds.norm.bias, ds.norm.eps, order=_merge_order(ds),
+                             out_dtype=_norm_out_dtype(x))
+    b, d2, h2, w2, c8 = xm.shape
+    out = torch.matmul(ds.reduction.weight, xm.view(b, d2 * h2 * w2, c8).transpose(1, 2))
+    return out.view(b, -1, d2, h2, w2)
+
+
 def _patched_basic_layer_forward(original, swin):
     @functools.wraps(original)
     def forward(self, x):
@@ -281,6 +327,8 @@ def _patched_basic_layer_forward(original, swin):
             x = blk(x, attn_mask)
         x = x.view(b, d, h, w, -1)
         if self.downsample is not None:
+            if _merge_fusable(self.downsample, x):
+                return _merge_channels_first(self.downsample, x)
             x = self.downsample(x)
         return x.permute(0, 4, 1, 2, 3).contiguous()
 

@@ -212,6 +212,22 @@ CRUMPET_API int crumpet_unshift_unpartition_crop_norm_3d(
     int64_t ss_h, int64_t ss_w, void* stream);
 
 /*
+ * Patch merging (the downsample of a Swin stage) up to its LayerNorm: for every
+ * output voxel (d2, h2, w2) of the half-resolution grid (odd dims round up), the
+ * eight neighbours x[b, 2 d2 + i, 2 h2 + j, 2 w2 + k, :] are concatenated in the
+ * order parts[0..7] (code i | j << 1 | k << 2; neighbours past an odd dim are zero
+ * rows) and normalised over the 8C channels with fp32 weight/bias of 8C elements:
+ *   x [B, D, H, W, C] (in_dtype) -> output [B, ceil(D/2), ceil(H/2), ceil(W/2), 8C] (out_dtype)
+ * C a multiple of 8 with 8C <= 768; pointers 16-byte aligned.  No reference
+ * counterpart: the reference's patched BasicLayer calls the MONAI downsample
+ * module eagerly (torch-ext/crumpet/monai_patch.py:228-230).
+ */
+CRUMPET_API int crumpet_patch_merge_norm_3d(void* output, int out_dtype, const void* x,
+                                            int in_dtype, const float* weight, const float* bias,
+                                            float eps, int64_t B, int64_t D, int64_t H, int64_t W,
+                                            int64_t C, const int* parts, void* stream);
+
+/*
  * Sliding-window ROI inference around the network forward.  The reference drives
  * its patched network with MONAI's sliding_window_inference (a third-party
  * Python function, called at torch-ext/crumpet/demo_btcv.py:98-129 with

@@ -242,6 +242,49 @@ def test_block_fusion_wrappers_validate_and_have_no_cpu_path():
     assert out.shape == (1, 13, 10, 9, 48)
 
 
+def test_patch_merge_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    merge = lib.crumpet_patch_merge_norm_3d
+    codes = (ctypes.c_int * 8)(*range(8))
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 12, codes, null)
+    assert rc == 3 and "multiple of 8" in _ops.last_error()
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 104, codes, null)
+    assert rc == 3
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 48, None, null)
+    assert rc == 1 and "part table" in _ops.last_error()
+    bad = (ctypes.c_int * 8)(0, 1, 2, 3, 4, 5, 6, 8)
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 48, bad, null)
+    assert rc == 1 and "0..7" in _ops.last_error()
+    rc = merge(null, 7, null, 1, null, null, 1e-5, 1, 8, 8, 8, 48, codes, null)
+    assert rc == 1 and "float32" in _ops.last_error()
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 48, codes, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = merge(ctypes.c_void_p(8), 1, ctypes.c_void_p(16), 1, ctypes.c_void_p(16),
+               ctypes.c_void_p(16), 1e-5, 1, 8, 8, 8, 48, codes, null)
+    assert rc == 1 and "aligned" in _ops.last_error()
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 0, 8, 8, 8, 48, codes, null)
+    assert rc == 0
+
+
+def test_patch_merge_wrapper_validates_and_has_no_cpu_path():
+    w, b = torch.ones(384), torch.zeros(384)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        crumpet.patch_merge_norm_3d(torch.randn(1, 4, 4, 4, 12), torch.ones(96), torch.zeros(96), 1e-5)
+    with pytest.raises(ValueError, match=r"\[8C\]"):
+        crumpet.patch_merge_norm_3d(torch.randn(1, 4, 4, 4, 48), torch.ones(48), torch.zeros(48), 1e-5)
+    with pytest.raises(ValueError, match="eight"):
+        crumpet.patch_merge_norm_3d(torch.randn(1, 4, 4, 4, 48), w, b, 1e-5, order=[(0, 0, 0)] * 7)
+    with pytest.raises(ValueError, match="eight"):
+        crumpet.patch_merge_norm_3d(torch.randn(1, 4, 4, 4, 48), w, b, 1e-5,
+                                    order=[(0, 0, 2)] + [(0, 0, 0)] * 7)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.patch_merge_norm_3d(torch.randn(1, 4, 4, 4, 48), w, b, 1e-5)
+    meta = crumpet.patch_merge_norm_3d(torch.empty(2, 7, 6, 5, 48, device="meta"), w, b, 1e-5,
+                                       out_dtype=torch.float16)
+    assert meta.shape == (2, 4, 3, 3, 384) and meta.dtype == torch.float16
+
+
 def test_roi_capi_validation():
     lib = _ops.capi()
     null = ctypes.c_void_p(0)

@@ -245,3 +245,53 @@ def test_unpartition_crop_norm_through_the_c_abi(cuda_device):
     # norm2 of the block, computed the eager way, agrees to fp16 rounding
     eager = torch.nn.functional.layer_norm(want_out.float(), (C,), w, b, 1e-5).half()
     assert (normed.float() - eager.float()).abs().max().item() <= 4e-3
+
+
+MERGE_CASES = [  # (B, D, H, W, C)
+    (8, 48, 48, 48, 48),   # stage 1 of an 8-ROI batch: 8C = 384
+    (2, 24, 24, 24, 96),   # stage 2: 8C = 768
+    (2, 7, 6, 5, 16),      # odd dims: zero-padded neighbours
+]
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32], ids=["out_f16", "out_f32"])
+@pytest.mark.parametrize("in_dtype", [torch.float16, torch.float32], ids=["in_f16", "in_f32"])
+@pytest.mark.parametrize("case", MERGE_CASES, ids=["s48_C48", "s24_C96", "odd_C16"])
+def test_patch_merge_norm_matches_eager(case, in_dtype, out_dtype, cuda_device):
+    """Neighbour concatenation + LayerNorm of patch merging against the module's eager
+    F.pad + strided slices + cat + layer_norm, in float64."""
+    B, D, H, W, C = case
+    x = (I.randn(100 + C, case, "float32") * 1.5 + 0.25).to(in_dtype)
+    w = 1.0 + 0.2 * I.randn(101 + C, (8 * C,), "float32")
+    b = 0.1 * I.randn(102 + C, (8 * C,), "float32")
+    got = crumpet.patch_merge_norm_3d(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device), 1e-5,
+                                      out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    xp = torch.nn.functional.pad(x.double(), (0, 0, 0, W % 2, 0, H % 2, 0, D % 2))
+    cat = torch.cat([xp[:, i::2, j::2, k::2, :] for i, j, k in crumpet.block_fusion.PRODUCT_ORDER], -1)
+    want = OB.layer_norm(cat.numpy(), w.numpy(), b.numpy(), 1e-5)
+    g = got.double().cpu().numpy()
+    assert g.shape == want.shape
+    rel, atol = TOL[out_dtype]
+    bad = np.abs(g - want) > np.abs(want) * rel + atol
+    assert not bad.any(), (np.abs(g - want).max(), int(bad.sum()))
+
+
+def test_patch_merge_custom_order_and_c_abi(cuda_device):
+    B, D, H, W, C = 1, 6, 6, 6, 8
+    order = [(1, 1, 1), (0, 0, 0), (1, 0, 0), (0, 1, 0), (0, 0, 1), (1, 1, 0), (1, 0, 1), (0, 1, 1)]
+    x = torch.randn((B, D, H, W, C), device=cuda_device).half()
+    w = torch.ones(8 * C, device=cuda_device)
+    b = torch.zeros(8 * C, device=cuda_device)
+    got = crumpet.patch_merge_norm_3d(x, w, b, 1e-5, order=order)
+    cat = torch.cat([x[:, i::2, j::2, k::2, :] for i, j, k in order], -1).float()
+    want = torch.nn.functional.layer_norm(cat, (8 * C,), w, b, 1e-5).half()
+    assert (got.float() - want.float()).abs().max().item() <= 4e-3
+    out = torch.empty_like(got)
+    import ctypes
+    codes = (ctypes.c_int * 8)(*[i | (j << 1) | (k << 2) for i, j, k in order])
+    rc = _ops.capi().crumpet_patch_merge_norm_3d(ptr(out), DTYPE_CODE[torch.float16], ptr(x),
+                                                 DTYPE_CODE[torch.float16], ptr(w), ptr(b), 1e-5, B,
+                                                 D, H, W, C, codes, stream_ptr())
+    assert rc == 0, _ops.last_error()
+    assert torch.equal(out, got)

@@ -48,6 +48,22 @@ def test_fused_attention_opt_out(monkeypatch):
         crumpet.unpatch_monai_swin_unetr()
 
 
+def test_merge_fusion_plumbing_on_meta():
+    """The channels-first patch-merging path: the module's own norm and reduction
+    parameters go to the fused op, and the output is [B, 2C, D', H', W']."""
+    ds = swin_unetr.PatchMerging(48, norm_layer=torch.nn.LayerNorm, spatial_dims=3)
+    assert monai_patch._merge_order(ds) == crumpet.block_fusion.PRODUCT_ORDER
+    x = torch.empty((2, 7, 6, 5, 48), device="meta")
+    out = monai_patch._merge_channels_first(ds.to("meta"), x)
+    assert out.shape == (2, 96, 4, 3, 3)
+    assert not monai_patch._merge_fusable(ds, x)  # meta tensors take the eager path
+
+    class Other(torch.nn.Module):
+        pass
+
+    assert monai_patch._merge_order(Other()) is None
+
+
 def test_swin_unetr_shapes_and_parameter_count():
     model = swin_unetr.SwinUNETR(1, 14, 48)
     assert sum(p.numel() for p in model.parameters()) == 62_187_296
