@@ -9,8 +9,8 @@ feature 48, depths 2,2,2,2, heads 3,6,12,24, window 7, patch 2), random init
 overlap over a synthetic 1x1x512x512x224 volume of uniform[-1000, 1000]
 intensities scaled to [0, 1]: 400 ROIs per step, batches of 8, arg-max
 segmentation.  A step is one full volume.  With N GPUs (torchrun, one process
-per GPU) the ROI batches are dealt round-robin to the ranks and one NCCL
-reduce merges the accumulators on rank 0 (total work fixed: strong scaling).
+per GPU) each rank takes a contiguous, balanced 1/N of the ROI grid and one
+NCCL reduce merges the accumulators on rank 0 (total work fixed: strong scaling).
 
 ``value``: ROIs/s with the volume resident in HBM and the segmentation left
 on the device, CUDA-event timed, max over ranks.  ``e2e``: the same with the
@@ -152,6 +152,7 @@ def time_kernels(device, peaks) -> dict:
     import crumpet_b200 as crumpet
 
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)
+    clean = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def timed(fn, iters=20, warm=3):
         for _ in range(warm):
@@ -159,7 +160,13 @@ def time_kernels(device, peaks) -> dict:
         torch.cuda.synchronize()
         times = []
         for _ in range(iters):
-            flush.zero_()  # evict L2 (126 MB) between iterations
+            # evict L2 (126 MB) between iterations: write a buffer larger than L2, then read
+            # another one so the write-backs of the dirty lines finish before the timed launch
+            # (left dirty, they cost a write-only-flushed copy kernel ~20 % of its time), then
+            # keep the stream busy ~150 us so the wrapper's host time never enters the events
+            flush.zero_()
+            clean.sum()
+            torch.cuda._sleep(300_000)
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
             s.record()
@@ -244,7 +251,22 @@ def time_kernels(device, peaks) -> dict:
     res["unshift_unpartition_crop_3d"] = {"config": "[2744,343,48] fp16 -> [8,48,48,48,48] + residual",
                                           "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
                                           "frac_hbm": nb / ms / 1e6 / hbm}
-    del flush
+    # the same pass with the next LayerNorm fused: writes the block output and norm2 of it
+    nb = 4 * nb_in
+    ms = timed(lambda: crumpet.unshift_unpartition_crop_norm_3d(wins, 8, 48, 48, 48, 48, ws, ss,
+                                                                gamma, beta, 1e-5, residual=xs))
+    res["unshift_unpartition_crop_norm_3d"] = {
+        "config": "[2744,343,48] fp16 + residual -> [8,48,48,48,48] out + LayerNorm(out)",
+        "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6, "frac_hbm": nb / ms / 1e6 / hbm}
+    # patch merging of that stage: 2x2x2 neighbours + LayerNorm(384) -> [8,24,24,24,384] fp16
+    g8 = torch.ones(384, device=device)
+    b8 = torch.zeros(384, device=device)
+    nb = 2 * nb_in
+    ms = timed(lambda: crumpet.patch_merge_norm_3d(xs, g8, b8, 1e-5))
+    res["patch_merge_norm_3d"] = {"config": "[8,48,48,48,48] fp16 -> [8,24,24,24,384] fp16",
+                                  "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
+                                  "frac_hbm": nb / ms / 1e6 / hbm}
+    del flush, clean
     return res
 
 
