@@ -266,6 +266,14 @@ def time_kernels(device, peaks) -> dict:
     res["patch_merge_norm_3d"] = {"config": "[8,48,48,48,48] fp16 -> [8,24,24,24,384] fp16",
                                   "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
                                   "frac_hbm": nb / ms / 1e6 / hbm}
+    # the trunk's hidden-state norm of the patch embedding (x0 of an 8-ROI batch):
+    # channels-first fp16 in, channels-last fp32 out (LayerNorm's autocast dtype)
+    xcf = xs.permute(0, 4, 1, 2, 3).contiguous()
+    nb = nb_in + 2 * nb_in
+    ms = timed(lambda: crumpet.proj_out_norm_3d(xcf, out_dtype=torch.float32))
+    res["proj_out_norm_3d"] = {"config": "[8,48,48,48,48] fp16 channels-first -> fp32 channels-last",
+                               "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
+                               "frac_hbm": nb / ms / 1e6 / hbm}
     del flush, clean
     return res
 

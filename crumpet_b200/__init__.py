@@ -49,6 +49,7 @@ _OP_NAMES = (
     "unshift_unpartition_crop_3d",
     "unshift_unpartition_crop_norm_3d",
     "patch_merge_norm_3d",
+    "proj_out_norm_3d",
 )
 
 
@@ -274,6 +275,7 @@ from .block_fusion import (  # noqa: E402
     unshift_unpartition_crop_3d,
     unshift_unpartition_crop_norm_3d,
     patch_merge_norm_3d,
+    proj_out_norm_3d,
 )
 
 
@@ -306,6 +308,7 @@ __all__ = [
     "unshift_unpartition_crop_3d",
     "unshift_unpartition_crop_norm_3d",
     "patch_merge_norm_3d",
+    "proj_out_norm_3d",
     "patch_monai_swin_unetr",
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",

@@ -14,9 +14,12 @@ on either side of the attention:
 * :func:`unshift_unpartition_crop_norm_3d` -- the same plus the LayerNorm of the
   result (the block's ``norm2``, which opens its MLP half);
 * :func:`patch_merge_norm_3d` -- the 2x2x2 neighbour concatenation of a stage's
-  patch merging and its LayerNorm (the reduction Linear follows as a GEMM).
+  patch merging and its LayerNorm (the reduction Linear follows as a GEMM);
+* :func:`proj_out_norm_3d` -- the Swin trunk's hidden-state normalisation
+  (MONAI ``SwinTransformer.proj_out``): LayerNorm over the channels of a
+  channels-first stage output, stored channels-last.
 
-Both are inference ops (no backward): they raise when autograd would need a
+All are inference ops (no backward): they raise when autograd would need a
 gradient through them.  The MONAI patch uses them only outside autograd.
 """
 
@@ -285,3 +288,58 @@ def patch_merge_norm_3d(
     _native.require().patch_merge_norm_3d(out, _aligned(x, 16), w, b, float(eps), codes)
     _prof.count("patch_merge_norm_3d")
     return out
+
+
+def proj_out_lanes(C: int) -> int:
+    """Lanes per voxel of the proj_out norm kernel for C channels (0: unsupported)."""
+    if C <= 0 or C > 768 or C % 8:
+        return 0
+    p = 1
+    while p * 24 < C:
+        p *= 2
+    return p if C % p == 0 else 0
+
+
+def proj_out_norm_3d(
+    x: torch.Tensor,
+    eps: float = 1e-5,
+    weight: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """``layer_norm(x.permute(0, 2, 3, 4, 1), [C], weight, bias, eps).permute(0, 4, 1, 2, 3)``.
+
+    ``x`` is a contiguous channels-first ``[B, C, D, H, W]`` volume.  The norm is
+    computed in fp32 and written channels-last in ``out_dtype`` (default
+    ``x.dtype``); the result is the ``[B, C, D, H, W]`` view of that storage, with
+    the strides MONAI's ``SwinTransformer.proj_out`` returns.  C must be a
+    multiple of 8, at most 768, and divisible by its lanes per voxel
+    (:func:`proj_out_lanes`).
+    """
+    if x.ndim != 5:
+        raise ValueError("x must have shape [B, C, D, H, W]")
+    _check_dtype(x.dtype)
+    out_dtype = x.dtype if out_dtype is None else out_dtype
+    _check_dtype(out_dtype)
+    B, C, D, H, W = (int(v) for v in x.shape)
+    if proj_out_lanes(C) == 0:
+        raise ValueError("proj_out_norm_3d needs C a multiple of 8, at most 768, divisible by "
+                         "its lanes per voxel")
+    if (weight is None) != (bias is None):
+        raise ValueError("weight and bias must both be given or both be None")
+    if weight is not None and (tuple(weight.shape) != (C,) or tuple(bias.shape) != (C,)):
+        raise ValueError("weight and bias must have shape [C]")
+    if x.device.type == "meta":
+        return torch.empty((B, D, H, W, C), dtype=out_dtype, device=x.device).permute(0, 4, 1, 2, 3)
+    if x.device.type != "cuda":
+        raise RuntimeError(f"crumpet_b200 runs proj_out_norm_3d on CUDA devices only (got {x.device})")
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, weight, bias)):
+        raise RuntimeError("proj_out_norm_3d has no backward; call it under torch.no_grad()")
+    out = torch.empty((B, D, H, W, C), dtype=out_dtype, device=x.device)
+    w = b = None
+    if weight is not None:
+        w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
+        b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
+    _native.require().proj_out_norm_3d(out, _aligned(x, 16), w, b, float(eps))
+    _prof.count("proj_out_norm_3d")
+    return out.permute(0, 4, 1, 2, 3)

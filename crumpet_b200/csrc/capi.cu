@@ -245,6 +245,15 @@ int crumpet_patch_merge_norm_3d(void* output, int out_dtype, const void* x, int 
                                  parts, static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_proj_out_norm_3d(void* output, int out_dtype, const void* x, int in_dtype,
+                             const float* weight, const float* bias, float eps, int64_t B,
+                             int64_t C, int64_t D, int64_t H, int64_t W, void* stream) {
+  if (int e = check_dtype(out_dtype)) return e;
+  if (int e = check_dtype(in_dtype)) return e;
+  return launch_proj_out_norm(output, out_dtype, x, in_dtype, weight, bias, eps, B, C, D, H, W,
+                              static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_roi_gather(void* out, int out_dtype, const void* volume, int in_dtype, int64_t C,
                        int64_t D, int64_t H, int64_t W, const int64_t* roi_starts, int64_t n,
                        int64_t rd, int64_t rh, int64_t rw, void* stream) {

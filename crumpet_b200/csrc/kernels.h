@@ -60,6 +60,14 @@ int launch_patch_merge_norm(void* out, int out_dtype, const void* x, int in_dtyp
                             const float* gamma, const float* beta, float eps, int64_t B, int64_t D,
                             int64_t H, int64_t W, int64_t C, const int* parts, cudaStream_t stream);
 
+// LayerNorm over the channels of a channels-first volume x [B, C, D, H, W], written
+// channels-last out [B, D, H, W, C]; fp32 gamma/beta of C, or both null (no affine).
+// proj_out_norm_lanes(C) is the lanes per voxel (0: C unsupported).
+int proj_out_norm_lanes(int64_t C);
+int launch_proj_out_norm(void* out, int out_dtype, const void* x, int in_dtype,
+                         const float* gamma, const float* beta, float eps, int64_t B, int64_t C,
+                         int64_t D, int64_t H, int64_t W, cudaStream_t stream);
+
 // Sliding-window ROI inference: crop a batch of ROIs, accumulate their predictions,
 // normalise by the ROI count and take the arg-max.  `starts` is a HOST array of
 // n (z, y, x) triples (n <= 64), passed to the kernels by value.

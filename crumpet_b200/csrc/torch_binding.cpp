@@ -312,6 +312,36 @@ void patch_merge_norm_3d(at::Tensor& output, const at::Tensor& x, const at::Tens
                                        C, codes, cur_stream(x)));
 }
 
+void proj_out_norm_3d(at::Tensor& output, const at::Tensor& x,
+                      const c10::optional<at::Tensor>& weight,
+                      const c10::optional<at::Tensor>& bias, double eps) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(output, "output");
+  TORCH_CHECK(x.dim() == 5, "x must have shape [B, C, D, H, W]");
+  const int64_t B = x.size(0), C = x.size(1), D = x.size(2), H = x.size(3), W = x.size(4);
+  TORCH_CHECK(weight.has_value() == bias.has_value(),
+              "weight and bias must both be given or both be None");
+  const float* w = nullptr;
+  const float* b = nullptr;
+  if (weight.has_value()) {
+    check_cuda_contig(*weight, "weight");
+    check_cuda_contig(*bias, "bias");
+    TORCH_CHECK(weight->scalar_type() == at::kFloat && bias->scalar_type() == at::kFloat &&
+                    weight->numel() == C && bias->numel() == C,
+                "weight and bias must be float32 tensors of C elements");
+    w = weight->data_ptr<float>();
+    b = bias->data_ptr<float>();
+  }
+  TORCH_CHECK(output.dim() == 5 && output.size(0) == B && output.size(1) == D &&
+                  output.size(2) == H && output.size(3) == W && output.size(4) == C,
+              "output must have shape [B, D, H, W, C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (output.numel() == 0) return;
+  check_rc(crumpet_proj_out_norm_3d(output.data_ptr(), dtype_code(output), x.data_ptr(),
+                                    dtype_code(x), w, b, static_cast<float>(eps), B, C, D, H, W,
+                                    cur_stream(x)));
+}
+
 std::vector<int64_t> roi_list(at::IntArrayRef starts, at::IntArrayRef roi) {
   TORCH_CHECK(roi.size() == 3, "roi takes three values");
   TORCH_CHECK(starts.size() % 3 == 0, "starts must hold (z, y, x) triples");
@@ -434,6 +464,9 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "patch_merge_norm_3d(Tensor! output, Tensor x, Tensor weight, Tensor bias, float eps, "
       "int[] parts) -> ()",
       kTags);
+  ops.def(
+      "proj_out_norm_3d(Tensor! output, Tensor x, Tensor? weight, Tensor? bias, float eps) -> ()",
+      kTags);
   ops.def("roi_gather(Tensor! out, Tensor volume, int[] starts, int[] roi) -> ()", kTags);
   ops.def("roi_accumulate(Tensor! acc, Tensor pred, int[] starts, int[] roi) -> ()", kTags);
   ops.def(
@@ -457,6 +490,7 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
   ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);
   ops.impl("patch_merge_norm_3d", &patch_merge_norm_3d);
+  ops.impl("proj_out_norm_3d", &proj_out_norm_3d);
   ops.impl("roi_gather", &roi_gather);
   ops.impl("roi_accumulate", &roi_accumulate);
   ops.impl("roi_argmax", &roi_argmax);

@@ -23,6 +23,11 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   proj Linear (reference :117-198), falling back to the module's own eager
   forward in training, with attention dropout, for head dims other than 16
   and 32, or for fp32 activations;
+* ``SwinTransformer.proj_out`` (not patched by the reference; only when the
+  module has it): the hidden-state LayerNorm of every stage output runs as one
+  kernel that reads the channels-first volume and writes the channels-last
+  normalised result (``proj_out_norm_3d``) instead of a permute, an autocast
+  cast, a contiguous copy and torch's LayerNorm;
 
 returns True when it installs the patch and False when it is already active;
 ``unpatch_monai_swin_unetr`` restores the originals.  It raises RuntimeError
@@ -46,6 +51,7 @@ once per mask.
 from __future__ import annotations
 
 import functools
+import inspect
 import os
 from typing import Any
 
@@ -56,6 +62,8 @@ from . import compute_attn_mask_3d, fused_shift_partition_3d, fused_unshift_unpa
 from .block_fusion import (
     PRODUCT_ORDER,
     patch_merge_norm_3d,
+    proj_out_lanes,
+    proj_out_norm_3d,
     norm_shift_partition_3d,
     unshift_unpartition_crop_3d,
     unshift_unpartition_crop_norm_3d,
@@ -63,6 +71,7 @@ from .block_fusion import (
 from .fused_attention import fused_swin_attention, swin_window_attention_qkv
 
 _STATE: dict[str, Any] = {}
+_MISSING = object()
 _BOUNDARY_ATTR = "_crumpet_boundary"
 _GEOMETRY_ATTR = "_crumpet_geometry"
 
@@ -335,6 +344,39 @@ def _patched_basic_layer_forward(original, swin):
     return forward
 
 
+def _proj_out_fusable(x: torch.Tensor) -> bool:
+    return (
+        _block_fusion_enabled()
+        and x.dim() == 5
+        and x.is_cuda
+        and x.dtype in _FUSED_DTYPES
+        and x.is_contiguous()
+        and proj_out_lanes(int(x.shape[1])) > 0
+        and _no_grad_needed(x)
+    )
+
+
+def _patched_proj_out(raw):
+    """``proj_out(x, normalize)`` with the 5D LayerNorm branch as one kernel.
+
+    MONAI's version (an instance method; a static method in the bundled network)
+    permutes x to channels-last, applies ``F.layer_norm(x, [C])`` -- fp32 under
+    autocast -- and permutes back; the result here has the same values up to fp32
+    LayerNorm rounding, the same dtype and the same (channels-last) strides.
+    """
+    static = isinstance(raw, staticmethod)
+    fn = raw.__func__ if static else raw
+
+    @functools.wraps(fn)
+    def proj_out(self, x, normalize=False):
+        if normalize and _proj_out_fusable(x):
+            out_dtype = torch.float32 if torch.is_autocast_enabled(x.device.type) else x.dtype
+            return proj_out_norm_3d(x, out_dtype=out_dtype)
+        return fn(x, normalize) if static else fn(self, x, normalize)
+
+    return proj_out
+
+
 def patch_monai_swin_unetr(swin_module=None) -> bool:
     """Install the patch; True on the installing call, False if already active."""
     if _STATE.get("patched"):
@@ -353,6 +395,10 @@ def patch_monai_swin_unetr(swin_module=None) -> bool:
     if _fused_attn_enabled():
         _STATE["window_attention_forward"] = swin.WindowAttention.forward
         swin.WindowAttention.forward = _patched_window_attention_forward(swin.WindowAttention.forward)
+    trunk = getattr(swin, "SwinTransformer", None)
+    if trunk is not None and hasattr(trunk, "proj_out"):
+        _STATE["proj_out"] = (trunk, trunk.__dict__.get("proj_out", _MISSING))
+        trunk.proj_out = _patched_proj_out(inspect.getattr_static(trunk, "proj_out"))
     return True
 
 
@@ -366,5 +412,11 @@ def unpatch_monai_swin_unetr() -> bool:
     swin.BasicLayer.forward = _STATE["basic_layer_forward"]
     if "window_attention_forward" in _STATE:
         swin.WindowAttention.forward = _STATE["window_attention_forward"]
+    if "proj_out" in _STATE:
+        trunk, raw = _STATE["proj_out"]
+        if raw is _MISSING:
+            delattr(trunk, "proj_out")
+        else:
+            setattr(trunk, "proj_out", raw)
     _STATE.clear()
     return True

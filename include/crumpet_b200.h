@@ -228,6 +228,25 @@ CRUMPET_API int crumpet_patch_merge_norm_3d(void* output, int out_dtype, const v
                                             int64_t C, const int* parts, void* stream);
 
 /*
+ * Hidden-state normalisation of the Swin trunk: LayerNorm over the channels of a
+ * channels-first volume, written channels-last,
+ *   x [B, C, D, H, W] (in_dtype)  ->  output [B, D, H, W, C] (out_dtype),
+ *   output[b, d, h, w, :] = LN(x[b, :, d, h, w]) over C in fp32 arithmetic,
+ * with fp32 weight/bias of C elements, or both NULL for no affine (MONAI's
+ * SwinTransformer.proj_out calls F.layer_norm without one).  The channels-last
+ * result viewed as [B, C, D, H, W] is what proj_out returns.  C a multiple of 8,
+ * at most 768, divisible by the lanes per voxel (C / 24 rounded up to a power of
+ * two: every C = 24 * 2^k, 48 * 2^k, ...); pointers 16-byte aligned.  No
+ * reference counterpart: the reference's end-to-end runs (benchmarks/bench_e2e.py,
+ * torch-ext/crumpet/demo_btcv.py:98-129) execute MONAI's proj_out eagerly
+ * (permute, fp32 cast under autocast, contiguous copy, LayerNorm).
+ */
+CRUMPET_API int crumpet_proj_out_norm_3d(void* output, int out_dtype, const void* x, int in_dtype,
+                                         const float* weight, const float* bias, float eps,
+                                         int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                                         void* stream);
+
+/*
  * Sliding-window ROI inference around the network forward.  The reference drives
  * its patched network with MONAI's sliding_window_inference (a third-party
  * Python function, called at torch-ext/crumpet/demo_btcv.py:98-129 with

@@ -285,6 +285,54 @@ def test_patch_merge_wrapper_validates_and_has_no_cpu_path():
     assert meta.shape == (2, 4, 3, 3, 384) and meta.dtype == torch.float16
 
 
+def test_proj_out_norm_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    pn = lib.crumpet_proj_out_norm_3d
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 1, 44, 4, 4, 4, null)
+    assert rc == 3 and "multiple of 8" in _ops.last_error()
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 1, 776, 4, 4, 4, null)
+    assert rc == 3
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 1, 200, 4, 4, 4, null)  # 200 / 16 lanes
+    assert rc == 3 and "lanes" in _ops.last_error()
+    rc = pn(null, 0, null, 1, ctypes.c_void_p(16), null, 1e-5, 1, 48, 4, 4, 4, null)
+    assert rc == 1 and "both" in _ops.last_error()
+    rc = pn(null, 0, null, 6, null, null, 1e-5, 1, 48, 4, 4, 4, null)
+    assert rc == 1 and "float32" in _ops.last_error()
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 1, 48, 4, 0, 4, null)
+    assert rc == 1 and "dims" in _ops.last_error()
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 1, 48, 4, 4, 4, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = pn(ctypes.c_void_p(16), 0, ctypes.c_void_p(18), 1, null, null, 1e-5, 1, 48, 4, 4, 4, null)
+    assert rc == 1 and "aligned" in _ops.last_error()
+    rc = pn(null, 0, null, 1, null, null, 1e-5, 0, 48, 4, 4, 4, null)
+    assert rc == 0
+
+
+def test_proj_out_norm_wrapper_validates_and_keeps_monai_strides():
+    from crumpet_b200.block_fusion import proj_out_lanes
+
+    assert [proj_out_lanes(c) for c in (24, 48, 96, 192, 384, 768, 64, 200, 12)] == \
+        [1, 2, 4, 8, 16, 32, 4, 0, 0]
+    with pytest.raises(ValueError, match="multiple of 8"):
+        crumpet.proj_out_norm_3d(torch.randn(1, 12, 4, 4, 4))
+    with pytest.raises(ValueError, match="both"):
+        crumpet.proj_out_norm_3d(torch.randn(1, 48, 4, 4, 4), weight=torch.ones(48))
+    with pytest.raises(ValueError, match=r"\[C\]"):
+        crumpet.proj_out_norm_3d(torch.randn(1, 48, 4, 4, 4), weight=torch.ones(8),
+                                 bias=torch.zeros(8))
+    with pytest.raises(TypeError):
+        crumpet.proj_out_norm_3d(torch.zeros(1, 48, 4, 4, 4, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.proj_out_norm_3d(torch.randn(1, 48, 4, 4, 4))
+    x = torch.empty(2, 96, 7, 6, 5, device="meta", dtype=torch.float16)
+    got = crumpet.proj_out_norm_3d(x, out_dtype=torch.float32)
+    want = torch.nn.functional.layer_norm(torch.empty(2, 96, 7, 6, 5).permute(0, 2, 3, 4, 1),
+                                          [96]).permute(0, 4, 1, 2, 3)
+    assert got.shape == want.shape and got.stride() == want.stride()
+    assert got.dtype == torch.float32
+
+
 def test_roi_capi_validation():
     lib = _ops.capi()
     null = ctypes.c_void_p(0)

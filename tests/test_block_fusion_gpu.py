@@ -295,3 +295,77 @@ def test_patch_merge_custom_order_and_c_abi(cuda_device):
                                                  D, H, W, C, codes, stream_ptr())
     assert rc == 0, _ops.last_error()
     assert torch.equal(out, got)
+
+
+# (B, C, D, H, W): the hidden states of an 8-ROI batch of feature size 48 (x0 .. x4),
+# plus a partial last tile (343 voxels), C = 24 / 64 (1 and 4 lanes) and a volume
+# smaller than one tile
+PROJ_CASES = [
+    (8, 48, 48, 48, 48),
+    (8, 96, 24, 24, 24),
+    (8, 192, 12, 12, 12),
+    (8, 384, 6, 6, 6),
+    (8, 768, 3, 3, 3),
+    (2, 96, 7, 7, 7),
+    (1, 24, 5, 6, 7),
+    (3, 64, 9, 3, 5),
+]
+PROJ_IDS = [f"B{b}_C{c}_{d}x{h}x{w}" for b, c, d, h, w in PROJ_CASES]
+
+
+@pytest.mark.parametrize("out_dtype", DTYPES, ids=["out_f32", "out_f16", "out_bf16"])
+@pytest.mark.parametrize("in_dtype", [torch.float16, torch.float32], ids=["in_f16", "in_f32"])
+@pytest.mark.parametrize("case", PROJ_CASES, ids=PROJ_IDS)
+def test_proj_out_norm_matches_eager(case, in_dtype, out_dtype, cuda_device):
+    """proj_out's permute + layer_norm + permute back, against float64 on the same
+    input values; the result has the eager path's shape and strides."""
+    B, C, D, H, W = case
+    x = (I.randn(300 + C + D, case, "float32") * 1.7 - 0.3).to(in_dtype)
+    got = crumpet.proj_out_norm_3d(x.to(cuda_device), out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    eager = torch.nn.functional.layer_norm(x.float().permute(0, 2, 3, 4, 1), [C]).permute(0, 4, 1, 2, 3)
+    assert got.shape == eager.shape and got.stride() == eager.stride()
+    assert got.dtype == out_dtype
+    cl = x.double().permute(0, 2, 3, 4, 1).numpy()
+    want = OB.layer_norm(cl, np.ones(C), np.zeros(C), 1e-5)
+    g = got.permute(0, 2, 3, 4, 1).double().cpu().numpy()
+    rel, atol = TOL[out_dtype]
+    bad = np.abs(g - want) > np.abs(want) * rel + atol
+    assert not bad.any(), (np.abs(g - want).max(), int(bad.sum()))
+
+
+def test_proj_out_norm_affine_and_c_abi(cuda_device):
+    B, C, D, H, W = 2, 96, 10, 9, 11
+    x = torch.randn((B, C, D, H, W), device=cuda_device).half()
+    w = 1.0 + 0.3 * torch.randn(C, device=cuda_device)
+    b = 0.2 * torch.randn(C, device=cuda_device)
+    got = crumpet.proj_out_norm_3d(x, 1e-6, w, b, out_dtype=torch.float32)
+    want = torch.nn.functional.layer_norm(x.float().permute(0, 2, 3, 4, 1), [C], w, b, 1e-6)
+    assert (got.permute(0, 2, 3, 4, 1) - want).abs().max().item() <= 2e-5
+    out = torch.empty((B, D, H, W, C), dtype=torch.float32, device=cuda_device)
+    rc = _ops.capi().crumpet_proj_out_norm_3d(ptr(out), DTYPE_CODE[torch.float32], ptr(x),
+                                              DTYPE_CODE[torch.float16], ptr(w), ptr(b), 1e-6, B, C,
+                                              D, H, W, stream_ptr())
+    assert rc == 0, _ops.last_error()
+    assert torch.equal(out, got.permute(0, 2, 3, 4, 1))
+    ops_out = torch.empty_like(out)
+    _ops.require().proj_out_norm_3d(ops_out, x, None, None, 1e-5)
+    plain = torch.nn.functional.layer_norm(x.float().permute(0, 2, 3, 4, 1), [C])
+    assert (ops_out - plain).abs().max().item() <= 2e-5
+
+
+def test_patched_proj_out_under_autocast(cuda_device):
+    """The patched trunk's hidden-state norm returns what MONAI's proj_out returns
+    under fp16 autocast: fp32, channels-last strides, the same values."""
+    trunk = swin_unetr.SwinTransformer(1, 48, (7, 7, 7), (2, 2, 2), (1, 1, 1, 1), (3, 3, 3, 3))
+    x = torch.randn((2, 48, 24, 24, 24), device=cuda_device).half()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.float16):
+        want = trunk.proj_out(x, True)
+        assert crumpet.patch_monai_swin_unetr(swin_unetr)
+        try:
+            got = trunk.proj_out(x, True)
+        finally:
+            crumpet.unpatch_monai_swin_unetr()
+    assert got.dtype == want.dtype == torch.float32
+    assert got.stride() == want.stride()
+    assert (got - want).abs().max().item() <= 2e-5

@@ -17,7 +17,8 @@ from oracle import mechanics as OM
 def test_patch_unpatch_repeated_safe():
     def current():
         return (swin_unetr.SwinTransformerBlock.forward_part1, swin_unetr.SwinTransformerBlock.forward,
-                swin_unetr.BasicLayer.forward, swin_unetr.WindowAttention.forward)
+                swin_unetr.BasicLayer.forward, swin_unetr.WindowAttention.forward,
+                swin_unetr.SwinTransformer.__dict__["proj_out"])
 
     originals = current()
     assert crumpet.patch_monai_swin_unetr(swin_unetr) is True
@@ -46,6 +47,21 @@ def test_fused_attention_opt_out(monkeypatch):
         assert swin_unetr.WindowAttention.forward is original
     finally:
         crumpet.unpatch_monai_swin_unetr()
+
+
+def test_patched_proj_out_keeps_eager_semantics_off_gpu():
+    """The patched hidden-state norm works as a bound method of the trunk and hands
+    anything the kernel does not take (CPU tensors, normalize=False) to the original."""
+    trunk = swin_unetr.SwinTransformer(1, 24, (7, 7, 7), (2, 2, 2), (1, 1, 1, 1), (3, 3, 3, 3))
+    x = torch.randn(1, 24, 5, 6, 7)
+    assert crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        assert trunk.proj_out(x, False) is x
+        want = torch.nn.functional.layer_norm(x.permute(0, 2, 3, 4, 1), [24]).permute(0, 4, 1, 2, 3)
+        assert torch.equal(trunk.proj_out(x, True), want)
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+    assert isinstance(swin_unetr.SwinTransformer.__dict__["proj_out"], staticmethod)
 
 
 def test_merge_fusion_plumbing_on_meta():
