@@ -297,15 +297,19 @@ def test_patch_merge_custom_order_and_c_abi(cuda_device):
     assert torch.equal(out, got)
 
 
-# (B, C, D, H, W): the hidden states of an 8-ROI batch of feature size 48 (x0 .. x4),
-# plus a partial last tile (343 voxels), C = 24 / 64 (1 and 4 lanes) and a volume
-# smaller than one tile
+# (B, C, D, H, W): the hidden states of an 8-ROI batch of feature size 48 (x0 .. x4);
+# volumes whose plane rows are 16-byte multiples take the cp.async kernel (also with
+# partial last tiles: 1200 and 240 voxels, C = 40 and 64), the others (343, 210,
+# 135 and 27 voxels) the one-tile-per-CTA kernel
 PROJ_CASES = [
     (8, 48, 48, 48, 48),
     (8, 96, 24, 24, 24),
     (8, 192, 12, 12, 12),
     (8, 384, 6, 6, 6),
     (8, 768, 3, 3, 3),
+    (2, 96, 10, 10, 12),
+    (3, 64, 8, 5, 6),
+    (2, 40, 4, 4, 4),
     (2, 96, 7, 7, 7),
     (1, 24, 5, 6, 7),
     (3, 64, 9, 3, 5),
@@ -334,8 +338,10 @@ def test_proj_out_norm_matches_eager(case, in_dtype, out_dtype, cuda_device):
     assert not bad.any(), (np.abs(g - want).max(), int(bad.sum()))
 
 
-def test_proj_out_norm_affine_and_c_abi(cuda_device):
-    B, C, D, H, W = 2, 96, 10, 9, 11
+@pytest.mark.parametrize("shape", [(2, 96, 10, 9, 11), (2, 96, 10, 10, 12)],
+                         ids=["scalar_loads", "cp_async"])
+def test_proj_out_norm_affine_and_c_abi(shape, cuda_device):
+    B, C, D, H, W = shape
     x = torch.randn((B, C, D, H, W), device=cuda_device).half()
     w = 1.0 + 0.3 * torch.randn(C, device=cuda_device)
     b = 0.2 * torch.randn(C, device=cuda_device)
