@@ -303,6 +303,20 @@ def cpu_baseline(roi: int, budget_s: float = 12.0) -> dict:
                       f"{dt:.1f} s"}
 
 
+def workload_config(args, world: int) -> dict:
+    """The workload both arms report."""
+    from crumpet_b200.inferer import roi_grid
+
+    spatial = tuple(args.volume)
+    n_rois = len(roi_grid(spatial, (args.roi,) * 3, args.overlap))
+    return {"workload": "swin_unetr_sliding_window", "volume": list(spatial),
+            "roi": [args.roi] * 3, "overlap": args.overlap, "sw_batch": args.sw_batch,
+            "rois_per_step": n_rois, "feature_size": 48, "depths": [2, 2, 2, 2],
+            "heads": [3, 6, 12, 24], "window": 7, "classes": 14,
+            "parallelism": f"roi-shard x{world}",
+            "l2": "inputs larger than L2 (235 MB volume, 3.3 GB fp32 accumulator)"}
+
+
 def run_reference(args) -> None:
     import torch
 
@@ -331,11 +345,11 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "swin_unetr_sliding_window_rois", "roi": [args.roi] * 3,
-                   "feature_size": 48, "step": "one ROI forward (bounded CPU sample)"},
+        "config": workload_config(args, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"1 ROI per step, unpatched eager network, fp32, {threads} threads"},
+                         "sample": (f"each step: 1 of the workload's ROIs ({args.roi}^3) through the "
+                                    f"unpatched eager network, fp32, {threads} threads")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -483,12 +497,7 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "swin_unetr_sliding_window", "volume": list(spatial),
-                       "roi": [args.roi] * 3, "overlap": args.overlap, "sw_batch": args.sw_batch,
-                       "rois_per_step": n_rois, "feature_size": 48, "depths": [2, 2, 2, 2],
-                       "heads": [3, 6, 12, 24], "window": 7, "classes": 14,
-                       "parallelism": f"roi-shard x{world}",
-                       "l2": "inputs larger than L2 (235 MB volume, 3.3 GB fp32 accumulator)"},
+            "config": workload_config(args, world),
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": host.numel() * host.element_size() * world,
                     "d2h_bytes_per_step": seg_host.numel()},
