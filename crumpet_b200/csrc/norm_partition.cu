@@ -154,6 +154,84 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
+// (mean, rstd) of one token whose channels are spread over an L-lane group: this
+// lane holds up to kGroupsPerLane 8-channel groups (bit k of `valid`: group k holds
+// data; the others count as zeros).  Sums in packed fp32 pairs, then the lane
+// group's shuffles; biased variance, as torch.nn.LayerNorm.
+template <int L>
+__device__ __forceinline__ float2 token_stats(const float (&v)[kGroupsPerLane][8], uint32_t valid,
+                                              float inv_c, float eps) {
+  float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < kGroupsPerLane; ++k)
+    if ((valid >> k) & 1u)
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) s = __fadd2_rn(s, make_float2(v[k][e], v[k][e + 1]));
+  const float mean = group_sum<L>(s.x + s.y) * inv_c;
+  const float2 nm = make_float2(-mean, -mean);
+  float2 q = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < kGroupsPerLane; ++k)
+    if ((valid >> k) & 1u)
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float2 d = __fadd2_rn(make_float2(v[k][e], v[k][e + 1]), nm);
+        q = __ffma2_rn(d, d, q);
+      }
+  return make_float2(mean, rsqrtf(group_sum<L>(q.x + q.y) * inv_c + eps));
+}
+
+// y = (v - mean) * rstd * gamma + beta for one 8-channel group, in packed pairs
+// (each lane of a pair rounds exactly as the scalar expression would).
+__device__ __forceinline__ void normalize8(const float (&v)[8], float2 st,
+                                           const float* __restrict__ gamma8,
+                                           const float* __restrict__ beta8, float (&y)[8]) {
+  const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma8));
+  const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma8) + 1);
+  const float4 ba = __ldg(reinterpret_cast<const float4*>(beta8));
+  const float4 bb = __ldg(reinterpret_cast<const float4*>(beta8) + 1);
+  const float2 gm[4] = {make_float2(ga.x, ga.y), make_float2(ga.z, ga.w), make_float2(gb.x, gb.y),
+                        make_float2(gb.z, gb.w)};
+  const float2 bt[4] = {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
+                        make_float2(bb.z, bb.w)};
+  const float2 nm = make_float2(-st.x, -st.x), rs = make_float2(st.y, st.y);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __fmul2_rn(__fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), nm), rs);
+    const float2 r = __ffma2_rn(t, gm[i], bt[i]);
+    y[2 * i] = r.x;
+    y[2 * i + 1] = r.y;
+  }
+}
+
+// The index math of a lane group's kTokensPerGroup tokens (first + j * stride) is
+// done once per token -- by lane j of the group for token j -- and broadcast to the
+// group's other lanes, instead of by every lane.  `fn(token, payload)` returns
+// whether the token has a source and sets its 64-bit payload.  All 32 lanes of
+// the warp must call this.
+template <int L, typename SourceFn>
+__device__ __forceinline__ void group_sources(uint32_t first, uint32_t stride, SourceFn fn,
+                                              uint64_t (&payload)[kTokensPerGroup],
+                                              bool (&ok)[kTokensPerGroup]) {
+  if constexpr (L >= kTokensPerGroup) {
+    const uint32_t lane = threadIdx.x & 31u, sub = lane % L;
+    uint64_t mine = 0;
+    int mine_ok = 0;
+    if (sub < uint32_t(kTokensPerGroup)) mine_ok = fn(first + sub * stride, mine) ? 1 : 0;
+#pragma unroll
+    for (int j = 0; j < kTokensPerGroup; ++j) {
+      payload[j] = __shfl_sync(0xffffffffu, mine, int(lane - sub) + j);
+      ok[j] = __shfl_sync(0xffffffffu, mine_ok, int(lane - sub) + j) != 0;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kTokensPerGroup; ++j) {
+      payload[j] = 0;
+      ok[j] = fn(first + j * stride, payload[j]);
+    }
+  }
+}
+
 // Lane `sub` of an L-lane group owns channel groups sub, sub + L, sub + 2L of
 // its tokens; the group's tokens in one block step are consecutive output
 // tokens, so a warp reads and writes contiguous rows.
@@ -165,65 +243,44 @@ norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
   constexpr uint32_t kGroups = kThreads / L;  // lane groups per block
   const uint32_t sub = threadIdx.x % L;
   const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
-  uint32_t token[kTokensPerGroup];
+  uint64_t src[kTokensPerGroup];
   bool inside[kTokensPerGroup];
+  group_sources<L>(first, kGroups,
+                   [&](uint32_t t, uint64_t& s) { return t < g.tokens && token_source(g, t, s); },
+                   src, inside);
   typename Io<TIn>::Raw raw[kTokensPerGroup][kGroupsPerLane];
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
-    token[j] = first + j * kGroups;
-    uint64_t src = 0;
-    inside[j] = token[j] < g.tokens && token_source(g, token[j], src);
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
-      if (inside[j] && grp < g.groups) raw[j][k] = Io<TIn>::load(x + src * g.C + grp * 8);
+      if (inside[j] && grp < g.groups) raw[j][k] = Io<TIn>::load(x + src[j] * g.C + grp * 8);
     }
   }
   const float inv_c = 1.f / float(g.C);
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
+    const uint32_t token = first + j * kGroups;
     float v[kGroupsPerLane][8];
-    float sum = 0.f;
+    uint32_t valid = 0;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
-      const uint32_t grp = sub + k * L;
-      if (inside[j] && grp < g.groups) {
+      if (inside[j] && sub + k * L < g.groups) {
         Io<TIn>::to_float(raw[j][k], v[k]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sum += v[k][e];
+        valid |= 1u << k;
       }
     }
     // every lane takes part in the shuffles (padding and dead tokens add zeros)
-    const float mean = group_sum<L>(sum) * inv_c;
-    float sq = 0.f;
-#pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
-      const uint32_t grp = sub + k * L;
-      if (inside[j] && grp < g.groups) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = v[k][e] - mean;
-          sq = fmaf(d, d, sq);
-        }
-      }
-    }
-    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
-    if (token[j] >= g.tokens) continue;
-    TOut* dst = out + uint64_t(token[j]) * g.C;
+    const float2 st = token_stats<L>(v, valid, inv_c, g.eps);
+    if (token >= g.tokens) continue;
+    TOut* dst = out + uint64_t(token) * g.C;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
       if (grp >= g.groups) continue;
       float y[8];
       if (inside[j]) {
-        const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
-        const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
-        const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
-        const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-        const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
+        normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = 0.f;  // F.pad after the norm: zeros
@@ -325,47 +382,51 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
   constexpr uint32_t kGroups = kThreads / L;
   const uint32_t sub = threadIdx.x % L;
   const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
-  uint32_t token[kTokensPerGroup];
   uint64_t src[kTokensPerGroup];
+  bool live[kTokensPerGroup];
+  group_sources<L>(
+      first, kGroups,
+      [&](uint32_t token, uint64_t& s) {
+        if (token >= g.tokens) return false;
+        uint32_t t, w, t2, h, b, d, id, ld, ih, lh, iw, lw;
+        g.f_W.divmod(token, t, w);
+        g.f_H.divmod(t, t2, h);
+        g.f_D.divmod(t2, b, d);
+        d = (d >= g.sd) ? d - g.sd : d + g.Dp - g.sd;
+        h = (h >= g.sh) ? h - g.sh : h + g.Hp - g.sh;
+        w = (w >= g.sw) ? w - g.sw : w + g.Wp - g.sw;
+        g.f_wd.divmod(d, id, ld);
+        g.f_wh.divmod(h, ih, lh);
+        g.f_ww.divmod(w, iw, lw);
+        const uint32_t win = (id * g.nwh + ih) * g.nww + iw;
+        const uint32_t loc = (ld * g.wh + lh) * g.ww + lw;
+        s = (uint64_t(b) * g.nw + win) * g.N + loc;
+        return true;
+      },
+      src, live);
   typename Io<T>::Raw rw[kTokensPerGroup][kGroupsPerLane], rr[kTokensPerGroup][kGroupsPerLane];
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
-    token[j] = first + j * kGroups;
-    src[j] = 0;
-    if (token[j] < g.tokens) {
-      uint32_t t, w, t2, h, b, d, id, ld, ih, lh, iw, lw;
-      g.f_W.divmod(token[j], t, w);
-      g.f_H.divmod(t, t2, h);
-      g.f_D.divmod(t2, b, d);
-      d = (d >= g.sd) ? d - g.sd : d + g.Dp - g.sd;
-      h = (h >= g.sh) ? h - g.sh : h + g.Hp - g.sh;
-      w = (w >= g.sw) ? w - g.sw : w + g.Wp - g.sw;
-      g.f_wd.divmod(d, id, ld);
-      g.f_wh.divmod(h, ih, lh);
-      g.f_ww.divmod(w, iw, lw);
-      const uint32_t win = (id * g.nwh + ih) * g.nww + iw;
-      const uint32_t loc = (ld * g.wh + lh) * g.ww + lw;
-      src[j] = (uint64_t(b) * g.nw + win) * g.N + loc;
+    const uint32_t token = first + j * kGroups;
 #pragma unroll
-      for (int k = 0; k < kGroupsPerLane; ++k) {
-        const uint32_t grp = sub + k * L;
-        if (grp < g.groups) {
-          rw[j][k] = Io<T>::load(windows + src[j] * g.C + grp * 8);
-          if (residual) rr[j][k] = Io<T>::load(residual + uint64_t(token[j]) * g.C + grp * 8);
-        }
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (live[j] && grp < g.groups) {
+        rw[j][k] = Io<T>::load(windows + src[j] * g.C + grp * 8);
+        if (residual) rr[j][k] = Io<T>::load(residual + uint64_t(token) * g.C + grp * 8);
       }
     }
   }
   const float inv_c = 1.f / float(g.C);
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
-    const bool live = token[j] < g.tokens;
+    const uint32_t token = first + j * kGroups;
     float v[kGroupsPerLane][8];
-    float sum = 0.f;
+    uint32_t valid = 0;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
-      if (live && grp < g.groups) {
+      if (live[j] && grp < g.groups) {
         Io<T>::to_float(rw[j][k], v[k]);
         if (residual) {
           float r[8];
@@ -373,40 +434,19 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[k][e] = round_to<T>(r[e] + v[k][e]);
         }
-        Io<T>::store8(out + uint64_t(token[j]) * g.C + grp * 8, v[k]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sum += v[k][e];
+        Io<T>::store8(out + uint64_t(token) * g.C + grp * 8, v[k]);
+        valid |= 1u << k;
       }
     }
-    const float mean = group_sum<L>(sum) * inv_c;
-    float sq = 0.f;
-#pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
-      const uint32_t grp = sub + k * L;
-      if (live && grp < g.groups) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float dv = v[k][e] - mean;
-          sq = fmaf(dv, dv, sq);
-        }
-      }
-    }
-    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
-    if (!live) continue;
+    const float2 st = token_stats<L>(v, valid, inv_c, g.eps);
+    if (!live[j]) continue;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
       if (grp >= g.groups) continue;
-      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
-      const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
-      const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
-      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
       float y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
-      Io<TN>::store8(normed + uint64_t(token[j]) * g.C + grp * 8, y);
+      normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
+      Io<TN>::store8(normed + uint64_t(token) * g.C + grp * 8, y);
     }
   }
 }
@@ -430,32 +470,42 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
   constexpr uint32_t kGroups = kThreads / L;
   const uint32_t sub = threadIdx.x % L;
   const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
-  uint32_t token[kTokensPerGroup];
+  // per output voxel: the input voxel index of its (0, 0, 0) neighbour, with bits
+  // 61..63 set when the +1 neighbour along D / H / W lies inside the volume
+  uint64_t base[kTokensPerGroup];
+  bool live[kTokensPerGroup];
+  group_sources<L>(
+      first, kGroups,
+      [&](uint32_t token, uint64_t& s) {
+        if (token >= g.tokens) return false;
+        uint32_t t, w2, t2, h2, b, d2;
+        g.f_W2.divmod(token, t, w2);
+        g.f_H2.divmod(t, t2, h2);
+        g.f_D2.divmod(t2, b, d2);
+        const uint64_t edges = uint64_t(2 * d2 + 1 < g.D) | (uint64_t(2 * h2 + 1 < g.H) << 1) |
+                               (uint64_t(2 * w2 + 1 < g.W) << 2);
+        s = (((uint64_t(b) * g.D + 2 * d2) * g.H + 2 * h2) * g.W + 2 * w2) | (edges << 61);
+        return true;
+      },
+      base, live);
   uint32_t inb[kTokensPerGroup];  // bit k: channel group sub + k*L lies inside the volume
   typename Io<TIn>::Raw raw[kTokensPerGroup][kGroupsPerLane];
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
-    token[j] = first + j * kGroups;
     inb[j] = 0;
-    if (token[j] < g.tokens) {
-      uint32_t t, w2, t2, h2, b, d2;
-      g.f_W2.divmod(token[j], t, w2);
-      g.f_H2.divmod(t, t2, h2);
-      g.f_D2.divmod(t2, b, d2);
+    const uint32_t edges = uint32_t(base[j] >> 61);
+    const uint64_t v0 = base[j] & ((uint64_t(1) << 61) - 1);
 #pragma unroll
-      for (int k = 0; k < kGroupsPerLane; ++k) {
-        const uint32_t grp = sub + k * L;
-        if (grp < g.groups) {
-          uint32_t part, cg;
-          g.f_pg.divmod(grp, part, cg);
-          const uint32_t code = (g.parts >> (3 * part)) & 7u;
-          const uint32_t d = 2 * d2 + (code & 1u), h = 2 * h2 + ((code >> 1) & 1u),
-                         w = 2 * w2 + ((code >> 2) & 1u);
-          if (d < g.D && h < g.H && w < g.W) {
-            const uint64_t v = ((uint64_t(b) * g.D + d) * g.H + h) * g.W + w;
-            raw[j][k] = Io<TIn>::load(x + v * g.C + cg * 8);
-            inb[j] |= 1u << k;
-          }
+    for (int k = 0; k < kGroupsPerLane; ++k) {
+      const uint32_t grp = sub + k * L;
+      if (live[j] && grp < g.groups) {
+        uint32_t part, cg;
+        g.f_pg.divmod(grp, part, cg);
+        const uint32_t code = (g.parts >> (3 * part)) & 7u;
+        if ((code & ~edges) == 0) {  // every +1 offset of this part stays inside the volume
+          const uint64_t v = v0 + ((code & 1u) * g.H + ((code >> 1) & 1u)) * g.W + (code >> 2);
+          raw[j][k] = Io<TIn>::load(x + v * g.C + cg * 8);
+          inb[j] |= 1u << k;
         }
       }
     }
@@ -463,8 +513,9 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
   const float inv_c = 1.f / float(8 * g.C);
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
+    const uint32_t token = first + j * kGroups;
     float v[kGroupsPerLane][8];
-    float sum = 0.f;
+    uint32_t valid = 0;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       if ((inb[j] >> k) & 1u) {
@@ -473,39 +524,17 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[k][e] = 0.f;  // padding rows (and unused groups)
       }
-      if (sub + k * L < g.groups) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sum += v[k][e];
-      }
+      if (sub + k * L < g.groups) valid |= 1u << k;
     }
-    const float mean = group_sum<L>(sum) * inv_c;
-    float sq = 0.f;
-#pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
-      if (sub + k * L < g.groups) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float dv = v[k][e] - mean;
-          sq = fmaf(dv, dv, sq);
-        }
-      }
-    }
-    const float rstd = rsqrtf(group_sum<L>(sq) * inv_c + g.eps);
-    if (token[j] >= g.tokens) continue;
-    TOut* dst = out + uint64_t(token[j]) * (8 * g.C);
+    const float2 st = token_stats<L>(v, valid, inv_c, g.eps);
+    if (!live[j]) continue;
+    TOut* dst = out + uint64_t(token) * (8 * g.C);
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
       if (grp >= g.groups) continue;
-      const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8));
-      const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma + grp * 8) + 1);
-      const float4 ba = __ldg(reinterpret_cast<const float4*>(beta + grp * 8));
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + grp * 8) + 1);
-      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
       float y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = fmaf((v[k][e] - mean) * rstd, gm[e], bt[e]);
+      normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
       Io<TOut>::store8(dst + grp * 8, y);
     }
   }
