@@ -259,7 +259,7 @@ def patch_merge_norm_3d(
     ``x`` is ``[B, D, H, W, C]``; odd dims are zero-padded at the far end (as the
     merging module's ``F.pad``); the result is ``[B, ceil(D/2), ceil(H/2),
     ceil(W/2), 8C]`` in ``out_dtype`` (default ``x.dtype``), the norm computed in
-    fp32.  C must be a multiple of 8 with 8C at most 768.
+    fp32.  C must be a multiple of 8 with 8C at most 3072.
     """
     if x.ndim != 5:
         raise ValueError("x must have shape [B, D, H, W, C]")
@@ -270,8 +270,8 @@ def patch_merge_norm_3d(
     out_dtype = x.dtype if out_dtype is None else out_dtype
     _check_dtype(out_dtype)
     B, D, H, W, C = (int(v) for v in x.shape)
-    if C % 8 or 8 * C > 768 or C == 0:
-        raise ValueError("patch_merge_norm_3d needs C a multiple of 8 and 8C at most 768")
+    if C % 8 or 8 * C > 3072 or C == 0:
+        raise ValueError("patch_merge_norm_3d needs C a multiple of 8 and 8C at most 3072")
     if tuple(weight.shape) != (8 * C,) or tuple(bias.shape) != (8 * C,):
         raise ValueError("weight and bias must have shape [8C]")
     shape = (B, -(-D // 2), -(-H // 2), -(-W // 2), 8 * C)

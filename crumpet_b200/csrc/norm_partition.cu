@@ -37,6 +37,9 @@ constexpr int kThreads = 256;
 constexpr int kGroupsPerLane = 3;
 constexpr int kTokensPerGroup = 2;
 constexpr int kMaxC = 32 * kGroupsPerLane * 8;  // L <= 32: C <= 768
+// Patch merging normalises 8C channels; above 768 it runs 32 lanes per token
+// with 6 or 12 groups per lane (8C <= 1536 / 3072) and one token per lane group.
+constexpr int kMaxMergeC = 32 * 12 * 8;  // 8C <= 3072
 
 struct BlockGeom {
   uint32_t D, H, W;        // unpadded volume
@@ -155,15 +158,15 @@ __device__ __forceinline__ float group_sum(float v) {
 }
 
 // (mean, rstd) of one token whose channels are spread over an L-lane group: this
-// lane holds up to kGroupsPerLane 8-channel groups (bit k of `valid`: group k holds
+// lane holds up to G 8-channel groups (bit k of `valid`: group k holds
 // data; the others count as zeros).  Sums in packed fp32 pairs, then the lane
 // group's shuffles; biased variance, as torch.nn.LayerNorm.
-template <int L>
-__device__ __forceinline__ float2 token_stats(const float (&v)[kGroupsPerLane][8], uint32_t valid,
-                                              float inv_c, float eps) {
+template <int L, int G>
+__device__ __forceinline__ float2 token_stats(const float (&v)[G][8], uint32_t valid, float inv_c,
+                                              float eps) {
   float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int k = 0; k < kGroupsPerLane; ++k)
+  for (int k = 0; k < G; ++k)
     if ((valid >> k) & 1u)
 #pragma unroll
       for (int e = 0; e < 8; e += 2) s = __fadd2_rn(s, make_float2(v[k][e], v[k][e + 1]));
@@ -171,7 +174,7 @@ __device__ __forceinline__ float2 token_stats(const float (&v)[kGroupsPerLane][8
   const float2 nm = make_float2(-mean, -mean);
   float2 q = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int k = 0; k < kGroupsPerLane; ++k)
+  for (int k = 0; k < G; ++k)
     if ((valid >> k) & 1u)
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
@@ -204,28 +207,27 @@ __device__ __forceinline__ void normalize8(const float (&v)[8], float2 st,
   }
 }
 
-// The index math of a lane group's kTokensPerGroup tokens (first + j * stride) is
+// The index math of a lane group's NT tokens (first + j * stride) is
 // done once per token -- by lane j of the group for token j -- and broadcast to the
 // group's other lanes, instead of by every lane.  `fn(token, payload)` returns
 // whether the token has a source and sets its 64-bit payload.  All 32 lanes of
 // the warp must call this.
-template <int L, typename SourceFn>
+template <int L, int NT, typename SourceFn>
 __device__ __forceinline__ void group_sources(uint32_t first, uint32_t stride, SourceFn fn,
-                                              uint64_t (&payload)[kTokensPerGroup],
-                                              bool (&ok)[kTokensPerGroup]) {
-  if constexpr (L >= kTokensPerGroup) {
+                                              uint64_t (&payload)[NT], bool (&ok)[NT]) {
+  if constexpr (L >= NT) {
     const uint32_t lane = threadIdx.x & 31u, sub = lane % L;
     uint64_t mine = 0;
     int mine_ok = 0;
-    if (sub < uint32_t(kTokensPerGroup)) mine_ok = fn(first + sub * stride, mine) ? 1 : 0;
+    if (sub < uint32_t(NT)) mine_ok = fn(first + sub * stride, mine) ? 1 : 0;
 #pragma unroll
-    for (int j = 0; j < kTokensPerGroup; ++j) {
+    for (int j = 0; j < NT; ++j) {
       payload[j] = __shfl_sync(0xffffffffu, mine, int(lane - sub) + j);
       ok[j] = __shfl_sync(0xffffffffu, mine_ok, int(lane - sub) + j) != 0;
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < kTokensPerGroup; ++j) {
+    for (int j = 0; j < NT; ++j) {
       payload[j] = 0;
       ok[j] = fn(first + j * stride, payload[j]);
     }
@@ -462,18 +464,19 @@ struct MergeGeom {
   float eps;
 };
 
-template <typename TIn, typename TOut, int L>
+// G groups of 8 channels per lane, NT tokens per L-lane group.
+template <typename TIn, typename TOut, int L, int G, int NT>
 __global__ void __launch_bounds__(kThreads)
 patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
                         const float* __restrict__ gamma, const float* __restrict__ beta,
                         const MergeGeom g) {
   constexpr uint32_t kGroups = kThreads / L;
   const uint32_t sub = threadIdx.x % L;
-  const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
+  const uint32_t first = blockIdx.x * (kGroups * NT) + threadIdx.x / L;
   // per output voxel: the input voxel index of its (0, 0, 0) neighbour, with bits
   // 61..63 set when the +1 neighbour along D / H / W lies inside the volume
-  uint64_t base[kTokensPerGroup];
-  bool live[kTokensPerGroup];
+  uint64_t base[NT];
+  bool live[NT];
   group_sources<L>(
       first, kGroups,
       [&](uint32_t token, uint64_t& s) {
@@ -488,15 +491,15 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
         return true;
       },
       base, live);
-  uint32_t inb[kTokensPerGroup];  // bit k: channel group sub + k*L lies inside the volume
-  typename Io<TIn>::Raw raw[kTokensPerGroup][kGroupsPerLane];
+  uint32_t inb[NT];  // bit k: channel group sub + k*L lies inside the volume
+  typename Io<TIn>::Raw raw[NT][G];
 #pragma unroll
-  for (int j = 0; j < kTokensPerGroup; ++j) {
+  for (int j = 0; j < NT; ++j) {
     inb[j] = 0;
     const uint32_t edges = uint32_t(base[j] >> 61);
     const uint64_t v0 = base[j] & ((uint64_t(1) << 61) - 1);
 #pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
+    for (int k = 0; k < G; ++k) {
       const uint32_t grp = sub + k * L;
       if (live[j] && grp < g.groups) {
         uint32_t part, cg;
@@ -512,12 +515,12 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
   }
   const float inv_c = 1.f / float(8 * g.C);
 #pragma unroll
-  for (int j = 0; j < kTokensPerGroup; ++j) {
+  for (int j = 0; j < NT; ++j) {
     const uint32_t token = first + j * kGroups;
-    float v[kGroupsPerLane][8];
+    float v[G][8];
     uint32_t valid = 0;
 #pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
+    for (int k = 0; k < G; ++k) {
       if ((inb[j] >> k) & 1u) {
         Io<TIn>::to_float(raw[j][k], v[k]);
       } else {
@@ -530,7 +533,7 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
     if (!live[j]) continue;
     TOut* dst = out + uint64_t(token) * (8 * g.C);
 #pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
+    for (int k = 0; k < G; ++k) {
       const uint32_t grp = sub + k * L;
       if (grp >= g.groups) continue;
       float y[8];
@@ -821,6 +824,17 @@ namespace {
 template <typename TIn, typename TOut>
 cudaError_t launch_merge_t(void* out, const void* x, const float* gamma, const float* beta,
                            const MergeGeom& g, cudaStream_t stream) {
+  if (g.groups > uint32_t(32 * kGroupsPerLane)) {  // 8C > 768: 32 lanes, one token per group
+    const uint32_t per_block = kThreads / 32;
+    const uint32_t blocks = (g.tokens + per_block - 1) / per_block;
+    auto o = static_cast<TOut*>(out);
+    auto xi = static_cast<const TIn*>(x);
+    if (g.groups <= 32 * 6)
+      patch_merge_norm_kernel<TIn, TOut, 32, 6, 1><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g);
+    else
+      patch_merge_norm_kernel<TIn, TOut, 32, 12, 1><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g);
+    return cudaGetLastError();
+  }
   int lanes = 1;
   while (uint32_t(lanes * kGroupsPerLane) < g.groups) lanes *= 2;
   const uint32_t per_block = uint32_t(kThreads / lanes) * kTokensPerGroup;
@@ -828,12 +842,12 @@ cudaError_t launch_merge_t(void* out, const void* x, const float* gamma, const f
   auto o = static_cast<TOut*>(out);
   auto xi = static_cast<const TIn*>(x);
   switch (lanes) {
-    case 1: patch_merge_norm_kernel<TIn, TOut, 1><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    case 2: patch_merge_norm_kernel<TIn, TOut, 2><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    case 4: patch_merge_norm_kernel<TIn, TOut, 4><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    case 8: patch_merge_norm_kernel<TIn, TOut, 8><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    case 16: patch_merge_norm_kernel<TIn, TOut, 16><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
-    default: patch_merge_norm_kernel<TIn, TOut, 32><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 1: patch_merge_norm_kernel<TIn, TOut, 1, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 2: patch_merge_norm_kernel<TIn, TOut, 2, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 4: patch_merge_norm_kernel<TIn, TOut, 4, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 8: patch_merge_norm_kernel<TIn, TOut, 8, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    case 16: patch_merge_norm_kernel<TIn, TOut, 16, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
+    default: patch_merge_norm_kernel<TIn, TOut, 32, kGroupsPerLane, kTokensPerGroup><<<blocks, kThreads, 0, stream>>>(o, xi, gamma, beta, g); break;
   }
   return cudaGetLastError();
 }
@@ -853,8 +867,8 @@ int launch_patch_merge_norm(void* out, int out_dtype, const void* x, int in_dtyp
                             int64_t H, int64_t W, int64_t C, const int* parts,
                             cudaStream_t stream) {
   if (B < 0 || D <= 0 || H <= 0 || W <= 0) return set_error(kErrInvalid, "bad volume dims");
-  if (C <= 0 || C % 8 != 0 || 8 * C > kMaxC)
-    return set_error(kErrUnsupported, "patch_merge_norm_3d needs C a multiple of 8 and 8C <= 768");
+  if (C <= 0 || C % 8 != 0 || 8 * C > kMaxMergeC)
+    return set_error(kErrUnsupported, "patch_merge_norm_3d needs C a multiple of 8 and 8C <= 3072");
   if (D * H * W >= (int64_t(1) << 31)) return set_error(kErrInvalid, "D*H*W must be below 2^31");
   if (!parts) return set_error(kErrInvalid, "null part table");
   MergeGeom g{};

@@ -298,7 +298,7 @@ def _merge_fusable(ds, x: torch.Tensor) -> bool:
         and red.bias is None
         and red.in_features == 8 * c
         and c % 8 == 0
-        and 8 * c <= 768
+        and 8 * c <= 3072
         and x.is_cuda
         and x.dtype in _FUSED_DTYPES
         and _no_grad_needed(x, norm.weight, norm.bias, red.weight)

@@ -218,7 +218,7 @@ CRUMPET_API int crumpet_unshift_unpartition_crop_norm_3d(
  * order parts[0..7] (code i | j << 1 | k << 2; neighbours past an odd dim are zero
  * rows) and normalised over the 8C channels with fp32 weight/bias of 8C elements:
  *   x [B, D, H, W, C] (in_dtype) -> output [B, ceil(D/2), ceil(H/2), ceil(W/2), 8C] (out_dtype)
- * C a multiple of 8 with 8C <= 768; pointers 16-byte aligned.  No reference
+ * C a multiple of 8 with 8C <= 3072; pointers 16-byte aligned.  No reference
  * counterpart: the reference's patched BasicLayer calls the MONAI downsample
  * module eagerly (torch-ext/crumpet/monai_patch.py:228-230).
  */

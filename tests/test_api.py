@@ -249,7 +249,7 @@ def test_patch_merge_capi_validation():
     codes = (ctypes.c_int * 8)(*range(8))
     rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 12, codes, null)
     assert rc == 3 and "multiple of 8" in _ops.last_error()
-    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 104, codes, null)
+    rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 392, codes, null)  # 8C = 3136
     assert rc == 3
     rc = merge(null, 1, null, 1, null, null, 1e-5, 1, 8, 8, 8, 48, None, null)
     assert rc == 1 and "part table" in _ops.last_error()

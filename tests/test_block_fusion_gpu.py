@@ -251,12 +251,16 @@ MERGE_CASES = [  # (B, D, H, W, C)
     (8, 48, 48, 48, 48),   # stage 1 of an 8-ROI batch: 8C = 384
     (2, 24, 24, 24, 96),   # stage 2: 8C = 768
     (2, 7, 6, 5, 16),      # odd dims: zero-padded neighbours
+    (8, 12, 12, 12, 192),  # stage 3: 8C = 1536 (32 lanes, 6 groups each)
+    (8, 6, 6, 6, 384),     # stage 4: 8C = 3072 (32 lanes, 12 groups each)
+    (2, 5, 7, 3, 384),     # wide and odd
 ]
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32], ids=["out_f16", "out_f32"])
 @pytest.mark.parametrize("in_dtype", [torch.float16, torch.float32], ids=["in_f16", "in_f32"])
-@pytest.mark.parametrize("case", MERGE_CASES, ids=["s48_C48", "s24_C96", "odd_C16"])
+@pytest.mark.parametrize("case", MERGE_CASES,
+                         ids=["s48_C48", "s24_C96", "odd_C16", "s12_C192", "s6_C384", "odd_C384"])
 def test_patch_merge_norm_matches_eager(case, in_dtype, out_dtype, cuda_device):
     """Neighbour concatenation + LayerNorm of patch merging against the module's eager
     F.pad + strided slices + cat + layer_norm, in float64."""
