@@ -102,3 +102,39 @@ def test_packed_matches_dense_kernel(cuda_device):
     dense = crumpet.fused_swin_attention(q, k, v, bias, mask, None, 0.25)
     dense = dense.transpose(1, 2).reshape(B, N, H * D)
     assert (packed.float() - dense.float()).abs().max().item() <= 2e-3
+
+
+def test_cfg3_full_size_sampled_windows(cuda_device):
+    """The BASELINE attention workload at full size: 2744 windows x 3 heads of a 98^3 stage
+    (ws 7, ss 3), through the dense-mask kernel (mask [2744, 343, 343] + boundary flags) and
+    the packed on-chip-mask kernel.  Sampled interior and boundary windows against the float64
+    oracle; the two kernels against each other on every window; no device error."""
+    import crumpet_b200 as crumpet
+    from crumpet_b200.monai_patch import boundary_flags
+
+    g = torch.Generator().manual_seed(33)
+    B, N, H, D = 2744, 343, 3, 16
+    ws, ss, nw = (7, 7, 7), (3, 3, 3), (14, 14, 14)
+    qkv = torch.randn((B, N, 3, H, D), generator=g).half().to(cuda_device)
+    table = (0.5 * torch.randn((13 ** 3, H), generator=g)).to(cuda_device)
+    index = torch.from_numpy(I.relative_index(ws)).to(cuda_device)
+    scale = D ** -0.5
+    packed = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, scale)
+    bias = table[index.reshape(-1)].reshape(N, N, H).permute(2, 0, 1).contiguous().half()
+    mask = crumpet.compute_attn_mask_3d(98, 98, 98, ws, ss, torch.float16, cuda_device)
+    boundary = boundary_flags((98, 98, 98), ws, ss, cuda_device)
+    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).contiguous() for i in range(3))
+    dense = crumpet.fused_swin_attention(q, k, v, bias, mask, boundary, scale)
+    torch.cuda.synchronize()
+    assert _ops.capi().crumpet_device_status(1) == 0
+    dense_bnc = dense.transpose(1, 2).reshape(B, N, H * D)
+    assert (packed.float() - dense_bnc.float()).abs().max().item() <= 2e-3
+    # interior windows and windows on the roll seam of one, two and three axes
+    sel = [0, 1, 100, 1000, 13, 13 * 14, 13 * 196, 13 + 13 * 14, 2743]
+    assert all(boundary[s].item() == (1 if s in (13, 182, 2548, 195, 2743) else 0) for s in sel)
+    want = OA.window_attention(q[sel].float().cpu().numpy(), k[sel].float().cpu().numpy(),
+                               v[sel].float().cpu().numpy(), bias.float().cpu().numpy(),
+                               mask[sel].float().cpu().numpy(), None, scale)
+    assert np.abs(dense[sel].float().cpu().numpy() - want).max() <= 2e-3
+    got = packed[sel].reshape(len(sel), N, H, D).permute(0, 2, 1, 3)
+    assert np.abs(got.float().cpu().numpy() - want).max() <= 2e-3
