@@ -84,3 +84,73 @@ def test_head_dim_32_network_argmax_agreement(cuda_device):
     agree = (patched.argmax(1) == eager.argmax(1)).float().mean().item()
     assert agree >= 0.999, agree
     assert (patched - eager).abs().max().item() < 5e-2
+
+
+def test_every_fusion_engages_in_the_patched_network(cuda_device):
+    """One fp16-autocast forward of the patched feature-size-48 network launches each fused
+    op: packed attention, norm1 + partition, crop + residual + norm2, patch merging (all four
+    stages) and the hidden-state norms (all five outputs)."""
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    x = torch.rand((1, 1, 96, 96, 96), device=cuda_device)
+    names = ["swin_window_attention_qkv", "norm_shift_partition_3d",
+             "unshift_unpartition_crop_norm_3d", "patch_merge_norm_3d", "proj_out_norm_3d"]
+    before = {n: profiling.counters[n] for n in names}
+    _run(model, x, True)
+    got = {n: profiling.counters[n] - before[n] for n in names}
+    assert got == {"swin_window_attention_qkv": 8, "norm_shift_partition_3d": 8,
+                   "unshift_unpartition_crop_norm_3d": 8, "patch_merge_norm_3d": 4,
+                   "proj_out_norm_3d": 5}, got
+
+
+def test_network_bf16_autocast(cuda_device):
+    """bf16 autocast: the patched network is as faithful to the fp32 eager network as the
+    eager bf16 network is (random-init logits have small class margins, so bf16 rounding
+    alone flips ~1 % of the arg-maxes either way)."""
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    x = torch.rand((1, 1, 96, 96, 96), device=cuda_device)
+
+    def run(patched, dtype):
+        if patched:
+            crumpet.patch_monai_swin_unetr(swin_unetr)
+        try:
+            with torch.no_grad(), torch.autocast("cuda", dtype=dtype, enabled=dtype is not None):
+                return model(x).float()
+        finally:
+            crumpet.unpatch_monai_swin_unetr()
+
+    ref = run(False, None)
+    eager, patched = run(False, torch.bfloat16), run(True, torch.bfloat16)
+    agree = lambda a: (a.argmax(1) == ref.argmax(1)).float().mean().item()
+    a_e, a_p = agree(eager), agree(patched)
+    d_e, d_p = (eager - ref).abs().max().item(), (patched - ref).abs().max().item()
+    print(f"vs fp32: eager bf16 agree {a_e:.5f} diff {d_e:.4f}; patched bf16 agree {a_p:.5f} "
+          f"diff {d_p:.4f}")
+    assert a_p >= a_e - 0.005, (a_p, a_e)
+    assert d_p <= 1.5 * d_e + 1e-2, (d_p, d_e)
+
+
+def test_network_fp32_without_autocast(cuda_device):
+    """fp32 activations: attention runs the module's eager forward, the fused norms,
+    partition, merge and hidden-state kernels run in fp32.  cuDNN runs the UNETR
+    convolutions in TF32 by default, which turns the norms' last-bit differences into
+    ~1e-3 logit differences (1.4e-3 measured)."""
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    x = torch.rand((1, 1, 64, 64, 64), device=cuda_device)
+    before = profiling.counters["norm_shift_partition_3d"]
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        with torch.no_grad():
+            patched = model(x)
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+    assert profiling.counters["norm_shift_partition_3d"] > before
+    with torch.no_grad():
+        eager = model(x)
+    agree = (patched.argmax(1) == eager.argmax(1)).float().mean().item()
+    diff = (patched - eager).abs().max().item()
+    print(f"fp32 agreement {agree:.5f} max logit diff {diff:.2e}")
+    assert agree >= 0.999, agree
+    assert diff < 5e-3, diff
