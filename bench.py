@@ -274,6 +274,19 @@ def time_kernels(device, peaks) -> dict:
     res["proj_out_norm_3d"] = {"config": "[8,48,48,48,48] fp16 channels-first -> fp32 channels-last",
                                "ms": ms, "bytes": nb, "gbs": nb / ms / 1e6,
                                "frac_hbm": nb / ms / 1e6 / hbm}
+    # the window attention's qkv / proj Linears at the same stage (941,192 window tokens),
+    # with torch's F.linear (cuBLAS) on the same operands beside them
+    del xcf
+    tok = wins.reshape(-1, 48)
+    for name, n_out in (("window_linear_qkv", 144), ("window_linear_proj", 48)):
+        w = (torch.randn((n_out, 48), device=device, generator=g) * 0.15).half()
+        b = (torch.randn((n_out,), device=device, generator=g) * 0.1).half()
+        nb = tok.numel() * 2 + tok.shape[0] * n_out * 2
+        ms = timed(lambda: crumpet.window_linear(tok, w, b))
+        ms_ref = timed(lambda: torch.nn.functional.linear(tok, w, b))
+        res[name] = {"config": f"[941192,48] x [48,{n_out}] + bias fp16", "ms": ms, "bytes": nb,
+                     "gbs": nb / ms / 1e6, "frac_hbm": nb / ms / 1e6 / hbm,
+                     "cublas_ms": ms_ref, "cublas_frac_hbm": nb / ms_ref / 1e6 / hbm}
     del flush, clean
     return res
 

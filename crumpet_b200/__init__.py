@@ -50,6 +50,7 @@ _OP_NAMES = (
     "unshift_unpartition_crop_norm_3d",
     "patch_merge_norm_3d",
     "proj_out_norm_3d",
+    "window_linear",
 )
 
 
@@ -269,7 +270,11 @@ def fused_unshift_unpartition_3d(
         return out
 
 
-from .fused_attention import fused_swin_attention, swin_window_attention_qkv  # noqa: E402
+from .fused_attention import (  # noqa: E402
+    fused_swin_attention,
+    swin_window_attention_qkv,
+    window_linear,
+)
 from .block_fusion import (  # noqa: E402
     norm_shift_partition_3d,
     unshift_unpartition_crop_3d,
@@ -309,6 +314,7 @@ __all__ = [
     "unshift_unpartition_crop_norm_3d",
     "patch_merge_norm_3d",
     "proj_out_norm_3d",
+    "window_linear",
     "patch_monai_swin_unetr",
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",

@@ -82,6 +82,8 @@ def capi() -> ctypes.CDLL:
         lib.crumpet_proj_out_norm_3d.argtypes = (
             [vp, i32, vp, i32, vp, vp, ctypes.c_float] + [i64] * 5 + [vp])
         lib.crumpet_proj_out_norm_3d.restype = i32
+        lib.crumpet_window_linear.argtypes = [vp, vp, vp, vp, i32] + [i64] * 3 + [vp]
+        lib.crumpet_window_linear.restype = i32
         roi = [i64] * 3
         lib.crumpet_roi_gather.argtypes = [vp, i32, vp, i32] + [i64] * 4 + [vp, i64] + roi + [vp]
         lib.crumpet_roi_gather.restype = i32

@@ -1023,7 +1023,9 @@ int read_device_error(bool clear) {
     const int zero = 0;
     cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
   }
-  return v;
+  const int lin = read_linear_error(clear);  // the Linear kernel's own word
+  if (lin < 0) return -1;
+  return v | lin;
 }
 
 }  // namespace crumpet

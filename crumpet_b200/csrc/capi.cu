@@ -245,6 +245,13 @@ int crumpet_patch_merge_norm_3d(void* output, int out_dtype, const void* x, int 
                                  parts, static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_window_linear(void* out, const void* x, const void* weight, const float* bias,
+                          int dtype, int64_t M, int64_t K, int64_t N, void* stream) {
+  if (int e = check_dtype(dtype)) return e;
+  return launch_window_linear(out, x, weight, bias, dtype, M, K, N,
+                              static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_proj_out_norm_3d(void* output, int out_dtype, const void* x, int in_dtype,
                              const float* weight, const float* bias, float eps, int64_t B,
                              int64_t C, int64_t D, int64_t H, int64_t W, void* stream) {

@@ -64,6 +64,13 @@ int launch_patch_merge_norm(void* out, int out_dtype, const void* x, int in_dtyp
 // channels-last out [B, D, H, W, C]; fp32 gamma/beta of C, or both null (no affine).
 // proj_out_norm_lanes(C) is the lanes per voxel (0: C unsupported).
 int proj_out_norm_lanes(int64_t C);
+
+// out[M, N] = x[M, K] * w[N, K]^T + bias[N] on the tensor cores (fp16 / bf16 operands,
+// fp32 accumulation, fp32 bias or null); K = 48 (N <= 256) or 96 (N <= 160), N % 16 == 0.
+bool window_linear_supported(int64_t K, int64_t N);
+int launch_window_linear(void* out, const void* x, const void* w, const float* bias, int dtype,
+                         int64_t M, int64_t K, int64_t N, cudaStream_t stream);
+int read_linear_error(bool clear);
 int launch_proj_out_norm(void* out, int out_dtype, const void* x, int in_dtype,
                          const float* gamma, const float* beta, float eps, int64_t B, int64_t C,
                          int64_t D, int64_t H, int64_t W, cudaStream_t stream);

@@ -1,7 +1,7 @@
 // crumpet_b200: thin inline-PTX wrappers for the Blackwell (sm_100a) async
-// machinery used by the attention kernel: mbarriers with bounded waits, tiled
-// TMA loads (no multicast), and tcgen05 tensor-memory allocation, MMA, commit,
-// load/store and fences.
+// machinery used by the attention and Linear kernels: mbarriers with bounded
+// waits, tiled TMA loads (no multicast) and stores, bulk-group waits, and tcgen05
+// tensor-memory allocation, MMA, commit, load/store and fences.
 #pragma once
 
 #include <cstdint>
@@ -88,6 +88,39 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// 2D tiled load global -> shared (no multicast), completion counted on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 2D tiled store shared -> global (rows past the tensor's end are not written).
+// Callers start at x = 0 and a non-negative row.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          map),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// All but the newest N bulk groups of this thread have finished reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// All bulk groups of this thread are complete (writes visible).
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // --------------------------------------------------------------- tcgen05

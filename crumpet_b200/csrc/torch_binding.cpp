@@ -342,6 +342,30 @@ void proj_out_norm_3d(at::Tensor& output, const at::Tensor& x,
                                     cur_stream(x)));
 }
 
+void window_linear(at::Tensor& out, const at::Tensor& x, const at::Tensor& weight,
+                   const c10::optional<at::Tensor>& bias) {
+  check_cuda_contig(x, "x");
+  check_cuda_contig(out, "out");
+  check_cuda_contig(weight, "weight");
+  TORCH_CHECK(x.dim() == 2 && weight.dim() == 2, "x must be [M, K] and weight [N, K]");
+  const int64_t M = x.size(0), K = x.size(1), N = weight.size(0);
+  TORCH_CHECK(weight.size(1) == K, "weight must be [N, K]");
+  TORCH_CHECK(weight.scalar_type() == x.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "x, weight and out must share one dtype");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N, "out must be [M, N]");
+  const float* b = nullptr;
+  if (bias.has_value()) {
+    check_cuda_contig(*bias, "bias");
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N,
+                "bias must be a float32 tensor of N elements");
+    b = bias->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  if (out.numel() == 0) return;
+  check_rc(crumpet_window_linear(out.data_ptr(), x.data_ptr(), weight.data_ptr(), b,
+                                 dtype_code(x), M, K, N, cur_stream(x)));
+}
+
 std::vector<int64_t> roi_list(at::IntArrayRef starts, at::IntArrayRef roi) {
   TORCH_CHECK(roi.size() == 3, "roi takes three values");
   TORCH_CHECK(starts.size() % 3 == 0, "starts must hold (z, y, x) triples");
@@ -467,6 +491,7 @@ TORCH_LIBRARY(crumpet_ops, ops) {
   ops.def(
       "proj_out_norm_3d(Tensor! output, Tensor x, Tensor? weight, Tensor? bias, float eps) -> ()",
       kTags);
+  ops.def("window_linear(Tensor! out, Tensor x, Tensor weight, Tensor? bias) -> ()", kTags);
   ops.def("roi_gather(Tensor! out, Tensor volume, int[] starts, int[] roi) -> ()", kTags);
   ops.def("roi_accumulate(Tensor! acc, Tensor pred, int[] starts, int[] roi) -> ()", kTags);
   ops.def(
@@ -491,6 +516,7 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);
   ops.impl("patch_merge_norm_3d", &patch_merge_norm_3d);
   ops.impl("proj_out_norm_3d", &proj_out_norm_3d);
+  ops.impl("window_linear", &window_linear);
   ops.impl("roi_gather", &roi_gather);
   ops.impl("roi_accumulate", &roi_accumulate);
   ops.impl("roi_argmax", &roi_argmax);

@@ -145,3 +145,51 @@ def swin_window_attention_qkv(
 
 
 __all__ = ["fused_swin_attention", "swin_window_attention_qkv"]
+
+
+def window_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(x, weight, bias)`` for float16 / bfloat16 window tokens on the tensor cores.
+
+    ``x [..., K]``, ``weight [N, K]`` (cast to ``x.dtype``, as autocast does for
+    ``nn.Linear``), ``bias [N]`` (rounded to ``x.dtype``, added in fp32 before the one
+    rounding of the output); the shapes of :func:`window_linear_supported`.
+    """
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("window_linear takes float16 or bfloat16 tokens")
+    K = int(x.shape[-1])
+    if weight.ndim != 2 or int(weight.shape[1]) != K:
+        raise ValueError("weight must have shape [N, K]")
+    N = int(weight.shape[0])
+    if not window_linear_supported(K, N):
+        raise ValueError("window_linear supports K = 48 (N <= 256) or K = 96 (N <= 160), "
+                         "N a multiple of 16")
+    if bias is not None and tuple(bias.shape) != (N,):
+        raise ValueError("bias must have shape [N]")
+    if x.device.type == "meta":
+        return torch.empty((*x.shape[:-1], N), dtype=x.dtype, device=x.device)
+    if x.device.type != "cuda":
+        raise RuntimeError(f"crumpet_b200 runs window_linear on CUDA devices only (got {x.device})")
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, weight, bias)):
+        raise RuntimeError("window_linear has no backward; call it under torch.no_grad()")
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    if x2.data_ptr() % 16:
+        x2 = x2.clone()
+    w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    b = None
+    if bias is not None:
+        b = bias.detach().to(device=x.device, dtype=x.dtype).to(torch.float32).contiguous()
+    out = torch.empty((x2.shape[0], N), dtype=x.dtype, device=x.device)
+    _native.require().window_linear(out, x2, w, b)
+    _prof.count("window_linear")
+    return out.view(*x.shape[:-1], N)
+
+
+def window_linear_supported(K: int, N: int) -> bool:
+    """Shapes :func:`window_linear` runs: K = 48 with N <= 256, or K = 96 with N <= 160; N a
+    multiple of 16 (the qkv and proj Linears of feature-size-48 stages 1 and 2, except the
+    stage-2 qkv with N = 288)."""
+    if N < 16 or N % 16:
+        return False
+    return (K == 48 and N <= 256) or (K == 96 and N <= 160)

@@ -68,7 +68,12 @@ from .block_fusion import (
     unshift_unpartition_crop_3d,
     unshift_unpartition_crop_norm_3d,
 )
-from .fused_attention import fused_swin_attention, swin_window_attention_qkv
+from .fused_attention import (
+    fused_swin_attention,
+    swin_window_attention_qkv,
+    window_linear,
+    window_linear_supported,
+)
 
 _STATE: dict[str, Any] = {}
 _MISSING = object()
@@ -234,6 +239,24 @@ def _patched_block_forward(original, swin):
     return forward
 
 
+def _linear(mod, x: torch.Tensor) -> torch.Tensor:
+    """``mod(x)`` for the qkv / proj ``nn.Linear`` of a window attention; on the tensor-core
+    GEMM (:func:`window_linear`) when it applies -- float16 / bfloat16 tokens already in the
+    dtype the Linear would compute in (the autocast dtype, else the tokens' own), K = 48 or 96,
+    N within :func:`window_linear_supported`, no gradient -- else through the module."""
+    if (isinstance(mod, torch.nn.Linear)
+            and x.is_cuda
+            and x.dtype in (torch.float16, torch.bfloat16)
+            and window_linear_supported(int(x.shape[-1]), int(mod.out_features))
+            and _no_grad_needed(x, mod.weight, mod.bias)):
+        compute = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else None
+        if compute is None:
+            compute = x.dtype if mod.weight.dtype == x.dtype else None
+        if compute == x.dtype:
+            return window_linear(x, mod.weight, mod.bias)
+    return mod(x)
+
+
 def _patched_window_attention_forward(original):
     @functools.wraps(original)
     def forward(self, x, mask):
@@ -242,7 +265,7 @@ def _patched_window_attention_forward(original):
         b, n, c = x.shape
         heads = self.num_heads
         head_dim = c // heads
-        qkv = self.qkv(x)
+        qkv = _linear(self.qkv, x)
         if head_dim not in (16, 32) or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
             return original(self, x, mask)
         geometry = None if mask is None else getattr(mask, _GEOMETRY_ATTR, None)
@@ -253,7 +276,7 @@ def _patched_window_attention_forward(original):
             out = swin_window_attention_qkv(
                 qkv.view(b, n, 3, heads, head_dim), self.relative_position_bias_table,
                 self.relative_position_index, num_windows, window_size, shift_size, self.scale)
-            return self.proj_drop(self.proj(out))
+            return self.proj_drop(_linear(self.proj, out))
         # A mask from elsewhere: dense mask path.
         qkv = qkv.reshape(b, n, 3, heads, head_dim).permute(2, 0, 3, 1, 4)
         q, k, v = qkv[0], qkv[1], qkv[2]
@@ -270,7 +293,7 @@ def _patched_window_attention_forward(original):
         out = fused_swin_attention(q.contiguous(), k.contiguous(), v.contiguous(), rel_bias, mask,
                                    boundary, scale=self.scale)
         out = out.transpose(1, 2).reshape(b, n, c)
-        return self.proj_drop(self.proj(out))
+        return self.proj_drop(_linear(self.proj, out))
 
     return forward
 

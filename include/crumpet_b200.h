@@ -241,6 +241,21 @@ CRUMPET_API int crumpet_patch_merge_norm_3d(void* output, int out_dtype, const v
  * torch-ext/crumpet/demo_btcv.py:98-129) execute MONAI's proj_out eagerly
  * (permute, fp32 cast under autocast, contiguous copy, LayerNorm).
  */
+/*
+ * Linear projection of window tokens on the tensor cores:
+ *   out[m, n] = sum_k x[m, k] * weight[n, k] + bias[n]
+ *   x [M, K], weight [N, K] (nn.Linear layout), out [M, N]: float16 or bfloat16
+ *   (dtype), fp32 accumulation, one rounding; bias fp32 [N] or NULL.
+ * K = 48 with N <= 256, or K = 96 with N <= 160; N a multiple of 16; pointers 16-byte
+ * aligned.  Replaces
+ * the qkv and proj nn.Linear calls of MONAI's WindowAttention around the
+ * attention kernel (torch-ext/crumpet/monai_patch.py:154-197 runs them through
+ * cuBLAS); a tcgen05 GEMM with TMA loads/stores and the bias add in its epilogue.
+ */
+CRUMPET_API int crumpet_window_linear(void* out, const void* x, const void* weight,
+                                      const float* bias, int dtype, int64_t M, int64_t K,
+                                      int64_t N, void* stream);
+
 CRUMPET_API int crumpet_proj_out_norm_3d(void* output, int out_dtype, const void* x, int in_dtype,
                                          const float* weight, const float* bias, float eps,
                                          int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,

@@ -333,6 +333,44 @@ def test_proj_out_norm_wrapper_validates_and_keeps_monai_strides():
     assert got.dtype == torch.float32
 
 
+def test_window_linear_capi_validation():
+    lib = _ops.capi()
+    null = ctypes.c_void_p(0)
+    lin = lib.crumpet_window_linear
+    rc = lin(null, null, null, null, 0, 100, 48, 144, null)  # float32 operands
+    assert rc == 1 and "float16" in _ops.last_error()
+    rc = lin(null, null, null, null, 1, 100, 64, 144, null)  # K = 64
+    assert rc == 3 and "K = 48" in _ops.last_error()
+    rc = lin(null, null, null, null, 1, 100, 96, 288, null)  # stage-2 qkv: does not fit
+    assert rc == 3
+    rc = lin(null, null, null, null, 1, 100, 48, 100, null)  # N not a multiple of 16
+    assert rc == 3
+    rc = lin(null, null, null, null, 1, 100, 48, 144, null)
+    assert rc == 1 and "null" in _ops.last_error()
+    rc = lin(ctypes.c_void_p(16), ctypes.c_void_p(24), ctypes.c_void_p(16), null, 1, 100, 48, 144,
+             null)
+    assert rc == 1 and "aligned" in _ops.last_error()
+    rc = lin(null, null, null, null, 1, 0, 48, 144, null)
+    assert rc == 0
+
+
+def test_window_linear_wrapper_validates_and_has_no_cpu_path():
+    w, b = torch.randn(144, 48), torch.randn(144)
+    with pytest.raises(TypeError, match="float16"):
+        crumpet.window_linear(torch.randn(10, 48), w, b)
+    x = torch.randn(10, 48).half()
+    with pytest.raises(ValueError, match="K = 48"):
+        crumpet.window_linear(torch.randn(10, 64).half(), torch.randn(144, 64), b)
+    with pytest.raises(ValueError, match=r"\[N, K\]"):
+        crumpet.window_linear(x, torch.randn(144, 32), b)
+    with pytest.raises(ValueError, match=r"\[N\]"):
+        crumpet.window_linear(x, w, torch.randn(12))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        crumpet.window_linear(x, w, b)
+    out = crumpet.window_linear(torch.empty(3, 343, 48, dtype=torch.float16, device="meta"), w, b)
+    assert out.shape == (3, 343, 144) and out.dtype == torch.float16
+
+
 def test_roi_capi_validation():
     lib = _ops.capi()
     null = ctypes.c_void_p(0)

@@ -89,18 +89,21 @@ def test_head_dim_32_network_argmax_agreement(cuda_device):
 def test_every_fusion_engages_in_the_patched_network(cuda_device):
     """One fp16-autocast forward of the patched feature-size-48 network launches each fused
     op: packed attention, norm1 + partition, crop + residual + norm2, patch merging (all four
-    stages) and the hidden-state norms (all five outputs)."""
+    stages), the hidden-state norms (all five outputs) and the tensor-core qkv / proj
+    Linears where their shapes fit."""
     torch.manual_seed(0)
     model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
     x = torch.rand((1, 1, 96, 96, 96), device=cuda_device)
     names = ["swin_window_attention_qkv", "norm_shift_partition_3d",
-             "unshift_unpartition_crop_norm_3d", "patch_merge_norm_3d", "proj_out_norm_3d"]
+             "unshift_unpartition_crop_norm_3d", "patch_merge_norm_3d", "proj_out_norm_3d",
+             "window_linear"]
     before = {n: profiling.counters[n] for n in names}
     _run(model, x, True)
     got = {n: profiling.counters[n] - before[n] for n in names}
+    # tensor-core Linears: stage 1 qkv + proj (K = 48), stage 2 proj (K = 96, N = 96)
     assert got == {"swin_window_attention_qkv": 8, "norm_shift_partition_3d": 8,
                    "unshift_unpartition_crop_norm_3d": 8, "patch_merge_norm_3d": 4,
-                   "proj_out_norm_3d": 5}, got
+                   "proj_out_norm_3d": 5, "window_linear": 6}, got
 
 
 def test_network_bf16_autocast(cuda_device):
