@@ -11,13 +11,14 @@
 // to ~10^6 window tokens): HBM-bound, with the tensor core nearly idle.  One
 // persistent CTA per SM, warp-specialised:
 //   warp 0      TMA producer: the tile's 128 rows of x as K/16 atoms of
-//               [128 rows x 32 B] (32-byte swizzle) into a 4-stage ring;
+//               [128 rows x 32 B] (32-byte swizzle) into a ring of up to 8 stages;
 //   warp 1      MMA issuer: K/16 tcgen05.mma (M=128, N, K=16) into one of two
 //               TMEM accumulators (columns 0 / 256), commit -> ring slot free +
 //               accumulator full;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lane
-//               quarter w % 4 = rows 32 (w % 4) ..), + bias, round, into a
-//               double-buffered row-major staging tile, one TMA store per tile.
+//   warps 2..9  two epilogue warpgroups, one per accumulator (tiles alternate):
+//               tcgen05.ld of the accumulator (warp w reads TMEM lane quarter
+//               w % 4 = rows 32 (w % 4) ..), + bias, round, into the group's
+//               row-major staging tile, one TMA store per tile.
 // w is loaded once per CTA.  Every mbarrier wait is bounded (2 s); on expiry the
 // CTA stops issuing, drains what it issued, frees TMEM and records the error.
 #include <mutex>
@@ -34,17 +35,19 @@ using namespace sm100;
 
 __device__ int g_linear_error;
 
-constexpr int kLinThreads = 192;              // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kLinThreads = 320;              // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kLinBM = 128;                   // rows per tile: one TMEM lane each
-constexpr int kLinStages = 4;
+constexpr int kLinMaxStages = 8;
 constexpr int kLinAtomBytes = kLinBM * 32;    // one 16-element K atom of a tile
 constexpr uint32_t kLinAccCols = 256;         // columns per TMEM accumulator
-constexpr int kLinEpiBar = 1;                 // named barrier of the epilogue warps
+constexpr int kLinEpiBar = 1;                 // named barriers 1, 2: the two epilogue groups
+constexpr size_t kLinSmemCap = 227 * 1024;
 
 struct LinParams {
   const float* bias;  // [N] (bias values in the element type, widened), or null
   uint32_t N;
   uint32_t tiles;     // ceil(M / 128)
+  uint32_t stages;    // ring depth, 2 .. kLinMaxStages
 };
 
 struct LinLayout {
@@ -53,12 +56,12 @@ struct LinLayout {
   uint32_t a_off, w_off, out_off, bias_off, total;
 };
 
-__host__ __device__ inline LinLayout lin_layout(int KA, uint32_t N) {
+__host__ __device__ inline LinLayout lin_layout(int KA, uint32_t N, uint32_t stages) {
   LinLayout l{};
   l.w_atom = (N * 32 + 1023) & ~1023u;
   l.out_tile = kLinBM * N * 2;
   l.a_off = 0;
-  l.w_off = l.a_off + kLinStages * KA * kLinAtomBytes;
+  l.w_off = l.a_off + stages * KA * kLinAtomBytes;
   l.out_off = l.w_off + KA * l.w_atom;
   l.bias_off = l.out_off + 2 * l.out_tile;
   l.total = l.bias_off + N * 4;
@@ -96,14 +99,14 @@ __global__ void __launch_bounds__(kLinThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  __shared__ uint64_t full[kLinStages], empty[kLinStages], dfull[2], dempty[2];
+  __shared__ uint64_t full[kLinMaxStages], empty[kLinMaxStages], dfull[2], dempty[2];
   __shared__ uint64_t w_ready, mma_drain;
   __shared__ uint32_t tmem_base_s;
-  __shared__ int abort_s, tile_ok_s;
+  __shared__ int abort_s, tile_ok_s[2];
   volatile int* abort_flag = &abort_s;
 
-  const uint32_t N = p.N;
-  const LinLayout L = lin_layout(KA, N);
+  const uint32_t N = p.N, S = p.stages;
+  const LinLayout L = lin_layout(KA, N, S);
   uint8_t* a_ring = smem + L.a_off;
   uint8_t* w_s = smem + L.w_off;
   uint8_t* out_s = smem + L.out_off;
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kLinThreads, 1)
 
   if (threadIdx.x == 0) {
     abort_s = 0;
-    for (int s = 0; s < kLinStages; ++s) {
+    for (uint32_t s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -144,10 +147,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       for (int k = 0; k < KA; ++k) tma_load_2d(w_s + k * L.w_atom, &tw, &w_ready, 16 * k, 0);
       uint32_t i = 0;
       for (uint32_t t = blockIdx.x; t < p.tiles; t += gridDim.x, ++i) {
-        const uint32_t s = i % kLinStages;
-        if (i >= uint32_t(kLinStages) &&
-            !mbar_wait(&empty[s], ((i / kLinStages) - 1) & 1u, abort_flag))
-          break;
+        const uint32_t s = i % S;
+        if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1u, abort_flag)) break;
         mbar_arrive_expect_tx(&full[s], KA * kLinAtomBytes);
 #pragma unroll
         for (int k = 0; k < KA; ++k)
@@ -155,8 +156,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
                       int(t * kLinBM));
       }
       // every load issued lands before the CTA may exit
-      const uint32_t first = i > uint32_t(kLinStages) ? i - kLinStages : 0;
-      for (uint32_t j = first; j < i; ++j) lin_drain_wait(&full[j % kLinStages], (j / kLinStages) & 1u);
+      const uint32_t first = i > S ? i - S : 0;
+      for (uint32_t j = first; j < i; ++j) lin_drain_wait(&full[j % S], (j / S) & 1u);
       lin_drain_wait(&w_ready, 0);
     }
   } else if (warp == 1) {
@@ -166,8 +167,8 @@ __global__ void __launch_bounds__(kLinThreads, 1)
       bool ok = mbar_wait(&w_ready, 0, abort_flag);
       uint32_t i = 0;
       for (uint32_t t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++i) {
-        const uint32_t s = i % kLinStages, b = i & 1u;
-        if (!mbar_wait(&full[s], (i / kLinStages) & 1u, abort_flag)) break;
+        const uint32_t s = i % S, b = i & 1u;
+        if (!mbar_wait(&full[s], (i / S) & 1u, abort_flag)) break;
         if (i >= 2 && !mbar_wait(&dempty[b], ((i >> 1) - 1) & 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + b * kLinAccCols;
@@ -187,41 +188,52 @@ __global__ void __launch_bounds__(kLinThreads, 1)
     }
   } else {
     // --------------------------------------------------------------- epilogue
+    // group e (warps 2..5 / 6..9) takes the tiles of accumulator e: i = e, e + 2, ...
+    const uint32_t e = uint32_t(warp - 2) / 4u;
     const uint32_t quarter = uint32_t(warp) & 3u;
     const uint32_t row = quarter * 32 + lane;
     const uint32_t lane_off = (quarter * 32) << 16;
-    const bool leader = warp == 2 && lane == 0;  // waits, stores; the others follow it
-    uint32_t i = 0;
-    for (uint32_t t = blockIdx.x; t < p.tiles; t += gridDim.x, ++i) {
-      const uint32_t b = i & 1u;
+    const bool leader = (uint32_t(warp) & 3u) == 2u && lane == 0;  // warp 2 or 6: waits, stores
+    const int bar_id = kLinEpiBar + int(e);
+    uint8_t* stage_tile = out_s + e * L.out_tile;
+    const uint32_t acc = tmem + lane_off + e * kLinAccCols;
+    uint32_t i = e;
+    for (uint32_t t = blockIdx.x + e * gridDim.x; t < p.tiles; t += 2 * gridDim.x, i += 2) {
       if (leader) {
-        tile_ok_s = mbar_wait(&dfull[b], (i >> 1) & 1u, abort_flag) ? 1 : 0;
-        bulk_wait_group_read<1>();  // the store that last read staging tile b is done
+        tile_ok_s[e] = mbar_wait(&dfull[e], (i >> 1) & 1u, abort_flag) ? 1 : 0;
+        bulk_wait_group_read<0>();  // this group's previous store has read its staging tile
       }
-      lin_bar_sync(kLinEpiBar, 128);  // one decision for all four warps
-      if (!tile_ok_s) break;
+      lin_bar_sync(bar_id, 128);  // one decision for the group's four warps
+      if (!tile_ok_s[e]) break;
       tc_fence_after();
-      uint8_t* st = out_s + b * L.out_tile + row * N * 2;
-      const uint32_t acc = tmem + lane_off + b * kLinAccCols;
-      for (uint32_t c = 0; c < N; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(acc + c, r);
+      uint8_t* st = stage_tile + row * N * 2;
+      for (uint32_t c = 0; c < N; c += 32) {
+        uint32_t r[32];
+        const bool two = c + 32 <= N;
+        if (two) {
+          tmem_ld32(acc + c, r);
+        } else {
+          tmem_ld16(acc + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        }
         tmem_wait_ld();
-        uint32_t w[8];
+        const uint32_t width = two ? 32u : 16u;
+        for (uint32_t h = 0; h < width; h += 16) {
+          uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          w[e] = lin_pack2<BF16>(__uint_as_float(r[2 * e]) + bias_s[c + 2 * e],
-                                 __uint_as_float(r[2 * e + 1]) + bias_s[c + 2 * e + 1]);
-        *reinterpret_cast<uint4*>(st + 2 * c) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(st + 2 * c + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+          for (int q = 0; q < 8; ++q)
+            w[q] = lin_pack2<BF16>(__uint_as_float(r[h + 2 * q]) + bias_s[c + h + 2 * q],
+                                   __uint_as_float(r[h + 2 * q + 1]) + bias_s[c + h + 2 * q + 1]);
+          *reinterpret_cast<uint4*>(st + 2 * (c + h)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(st + 2 * (c + h) + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dempty[b]);
+      if (lane == 0) mbar_arrive(&dempty[e]);
       fence_proxy_async_shared();  // staging writes -> TMA (async proxy) reads
-      lin_bar_sync(kLinEpiBar, 128);
+      lin_bar_sync(bar_id, 128);
       if (leader) {
-        tma_store_2d(&tout, out_s + b * L.out_tile, 0, int(t * kLinBM));
+        tma_store_2d(&tout, stage_tile, 0, int(t * kLinBM));
         bulk_commit_group();
       }
     }
@@ -287,9 +299,9 @@ int launch_lin(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& 
   auto kern = window_linear_kernel<KA, BF16>;
   // + alignment slack; at least 116 KB so two CTAs never share an SM (each holds
   // all 512 TMEM columns)
-  size_t smem = size_t(lin_layout(KA, p.N).total) + 1024;
+  size_t smem = size_t(lin_layout(KA, p.N, p.stages).total) + 1024;
   if (smem < 116 * 1024) smem = 116 * 1024;
-  if (smem > 227 * 1024) return set_error(kErrUnsupported, "window_linear tile does not fit");
+  if (smem > kLinSmemCap) return set_error(kErrUnsupported, "window_linear tile does not fit");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(smem));
   if (e != cudaSuccess) return set_cuda_error(e, "window_linear smem attribute");
@@ -339,6 +351,11 @@ int launch_window_linear(void* out, const void* x, const void* w, const float* b
   p.bias = bias;
   p.N = uint32_t(N);
   p.tiles = uint32_t((M + kLinBM - 1) / kLinBM);
+  // the deepest ring that fits next to the weights and the two staging tiles
+  const int KA = int(K / 16);
+  p.stages = kLinMaxStages;
+  while (p.stages > 2 && size_t(lin_layout(KA, p.N, p.stages).total) + 1024 > kLinSmemCap)
+    --p.stages;
   const bool bf = dtype == kBF16;
   if (K == 48) return bf ? launch_lin<3, true>(tx, tw, to, p, stream)
                          : launch_lin<3, false>(tx, tw, to, p, stream);
