@@ -90,7 +90,7 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 2D tiled load global -> shared (no multicast), completion counted on `bar`.
+// 2D tiled load global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1) {
   asm volatile(
