@@ -54,11 +54,16 @@ _OP_NAMES = (
 )
 
 
+_fakes_registered = False
+
+
 def _register_fake_impls() -> None:
     # The ops mutate preallocated outputs and return nothing, so their fake
     # (meta) implementations are no-ops (reference: torch-ext/crumpet/__init__.py:50-73).
-    if not _native.available():
+    global _fakes_registered
+    if _fakes_registered or not _native.available():
         return
+    _fakes_registered = True
     register = getattr(torch.library, "register_fake", None)
     if register is None:
         return

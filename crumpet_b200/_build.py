@@ -116,6 +116,11 @@ def build_torch_binding(force: bool = False) -> Path:
 def build(force: bool = False) -> None:
     build_library(force)
     build_torch_binding(force)
+    # a package imported before the libraries existed picks them up now
+    from . import _ops, _register_fake_impls
+
+    _ops.reload()
+    _register_fake_impls()
 
 
 if __name__ == "__main__":

@@ -20,11 +20,27 @@ EXT_PATH = _PKG / "_C.so"
 _load_error: Exception | None = None
 ops = None
 
-try:
-    torch.ops.load_library(str(EXT_PATH))
-    ops = torch.ops.crumpet_ops
-except Exception as exc:  # pragma: no cover - exercised only without a build
-    _load_error = exc
+
+def _try_load() -> bool:
+    global ops, _load_error
+    if ops is not None:
+        return True
+    try:
+        torch.ops.load_library(str(EXT_PATH))
+        ops = torch.ops.crumpet_ops
+        _load_error = None
+    except Exception as exc:  # pragma: no cover - exercised only without a build
+        _load_error = exc
+    return ops is not None
+
+
+_try_load()
+
+
+def reload() -> bool:
+    """Load the libraries if they were missing when the package was imported (a build
+    that runs in the same process as the import); True once they are loaded."""
+    return _try_load()
 
 
 def available() -> bool:
