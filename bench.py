@@ -17,9 +17,12 @@ on the device, CUDA-event timed, max over ranks.  ``e2e``: the same with the
 volume copied from pinned host memory and the segmentation copied back inside
 every step.  The 3.3 GB accumulator and 235 MB volume exceed L2, so no flush is
 needed between steps.  Also reported: live timing of the fused attention
-kernel inside the timed region (roofline), stand-alone per-kernel HBM GB/s at
-the BASELINE stage-0 sizes, clocks sampled during the timed region, and the
-CPU eager baseline (the unpatched network on the host cores).
+kernel inside the timed region (roofline), every crumpet_b200 kernel of the timed
+region against its roofline (crumpet_kernels: event time vs algorithmic bytes at
+the measured HBM rate, or the SFU rate for the attention's exponentials),
+stand-alone per-kernel HBM GB/s at the BASELINE stage-0 sizes, clocks sampled
+during the timed region, and the CPU eager baseline (the unpatched network on
+the host cores).
 
 ``--impl reference``: times the reference path on the CPU -- the eager,
 unpatched network (torch.roll / window partition / eager attention, i.e. the
@@ -316,6 +319,34 @@ def cpu_baseline(roi: int, budget_s: float = 12.0) -> dict:
                       f"{dt:.1f} s"}
 
 
+def kernels_vs_roofline(per_op: dict, peaks: dict, clock, steps: int, dev_ms: float):
+    """This rank's crumpet_b200 kernels inside the timed end-to-end region against their
+    roofline: per op, the CUDA-event time of its launches and its ideal time -- algorithmic
+    bytes at the measured HBM copy rate, or for the attention the larger of that and its
+    exponentials at the SFU rate (16 per clock per SM at the sampled SM clock).  The rest
+    of the step (the UNETR convolution decoder, cuBLAS GEMMs, torch elementwise ops) is
+    not crumpet_b200's and is left out."""
+    if not per_op:
+        return None
+    sm_mhz = (clock or {}).get("sm_mhz") or 1965.0
+    exp_per_ms = 16 * 148 * sm_mhz * 1e6 / 1e3
+    hbm_bytes_per_ms = peaks["hbm_gbs"] * 1e6
+    rows, tot_ms, tot_ideal = {}, 0.0, 0.0
+    for op, d in sorted(per_op.items(), key=lambda kv: -kv[1]["ms"]):
+        ideal, bound = d["bytes"] / hbm_bytes_per_ms, "hbm"
+        if d["exps"] and d["exps"] / exp_per_ms > ideal:
+            ideal, bound = d["exps"] / exp_per_ms, "sfu"
+        rows[op] = {"launches_per_step": d["launches"] / steps, "ms_per_step": d["ms"] / steps,
+                    "ideal_ms_per_step": ideal / steps, "frac": ideal / d["ms"] if d["ms"] else None,
+                    "bound": bound}
+        tot_ms += d["ms"]
+        tot_ideal += ideal
+    return {"ms_per_step": tot_ms / steps, "ideal_ms_per_step": tot_ideal / steps,
+            "frac_of_roofline": tot_ideal / tot_ms if tot_ms else None,
+            "share_of_step": tot_ms / dev_ms if dev_ms else None,
+            "peak_source": peaks["source"], "by_op": rows}
+
+
 def workload_config(args, world: int) -> dict:
     """The workload both arms report."""
     from crumpet_b200.inferer import roi_grid
@@ -437,6 +468,7 @@ def main() -> None:
     launches = profiling.total_launches() - launches0
     clock = clocks.summary() if rank == 0 else None
     attn = ktimer.summary()
+    per_op = ktimer.by_op()
 
     # ---- timed region 2: host buffers in, segmentation out (the public call)
     barrier()
@@ -506,6 +538,7 @@ def main() -> None:
                 # ncu DRAM bytes of one captured launch, scaled by algorithmic bytes
                 roofline["traffic"] = attn["bytes"] * tr["dram_over_algorithmic"]
                 roofline["traffic_source"] = tr["command"]
+        crumpet_kernels = kernels_vs_roofline(per_op, peaks, clock, args.steps, dev_ms)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
@@ -517,6 +550,7 @@ def main() -> None:
             "gpu_launches": total_launches,
             "clocks": clock,
             "roofline": roofline,
+            "crumpet_kernels": crumpet_kernels,
             "kernels": kernels,
             "cpu_baseline": cpu,
         }

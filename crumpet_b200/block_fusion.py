@@ -60,6 +60,10 @@ def padded_geometry(D: int, H: int, W: int, window_size) -> tuple[tuple[int, int
     return dims, num_windows, volume  # type: ignore[return-value]
 
 
+def _nbytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
+
+
 def _aligned(t: torch.Tensor, nbytes: int) -> torch.Tensor:
     t = t.contiguous()
     return t if t.data_ptr() % nbytes == 0 else t.clone()
@@ -108,9 +112,12 @@ def norm_shift_partition_3d(
     out = torch.empty(shape, dtype=out_dtype, device=x.device)
     w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
     b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
+    token = _prof.kernel_begin("norm_shift_partition_3d",
+                               lambda: {"bytes": _nbytes(x) + _nbytes(out)})
     _native.require().norm_shift_partition_3d(out, _aligned(x, 16), w, b, float(eps),
                                               *window_size, *shift_size)
     _prof.count("norm_shift_partition_3d")
+    _prof.kernel_end(token)
     return out
 
 
@@ -163,9 +170,13 @@ def unshift_unpartition_crop_3d(
         raise RuntimeError("unshift_unpartition_crop_3d has no backward; call it under torch.no_grad()")
     out = torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
     res = None if residual is None else _aligned(residual, 16)
+    # algorithmic bytes: the windows of the cropped volume, the residual, the output
+    token = _prof.kernel_begin("unshift_unpartition_crop_3d",
+                               lambda: {"bytes": _nbytes(out) * (3 if res is not None else 2)})
     _native.require().unshift_unpartition_crop_3d(out, _aligned(windows, 16), res, B, D, H, W, C,
                                                   *window_size, *shift_size)
     _prof.count("unshift_unpartition_crop_3d")
+    _prof.kernel_end(token)
     return out
 
 
@@ -233,10 +244,14 @@ def unshift_unpartition_crop_norm_3d(
     w = _aligned(weight.detach().to(device=windows.device, dtype=torch.float32), 16)
     b = _aligned(bias.detach().to(device=windows.device, dtype=torch.float32), 16)
     res = None if residual is None else _aligned(residual, 16)
+    token = _prof.kernel_begin(
+        "unshift_unpartition_crop_norm_3d",
+        lambda: {"bytes": _nbytes(out) * (3 if res is not None else 2) + _nbytes(normed)})
     _native.require().unshift_unpartition_crop_norm_3d(out, normed, _aligned(windows, 16), res, w, b,
                                                        float(eps), B, D, H, W, C, *window_size,
                                                        *shift_size)
     _prof.count("unshift_unpartition_crop_norm_3d")
+    _prof.kernel_end(token)
     return out, normed
 
 
@@ -285,8 +300,10 @@ def patch_merge_norm_3d(
     w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
     b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
     codes = [i | (j << 1) | (k << 2) for i, j, k in order]
+    token = _prof.kernel_begin("patch_merge_norm_3d", lambda: {"bytes": _nbytes(x) + _nbytes(out)})
     _native.require().patch_merge_norm_3d(out, _aligned(x, 16), w, b, float(eps), codes)
     _prof.count("patch_merge_norm_3d")
+    _prof.kernel_end(token)
     return out
 
 
@@ -340,6 +357,8 @@ def proj_out_norm_3d(
     if weight is not None:
         w = _aligned(weight.detach().to(device=x.device, dtype=torch.float32), 16)
         b = _aligned(bias.detach().to(device=x.device, dtype=torch.float32), 16)
+    token = _prof.kernel_begin("proj_out_norm_3d", lambda: {"bytes": _nbytes(x) + _nbytes(out)})
     _native.require().proj_out_norm_3d(out, _aligned(x, 16), w, b, float(eps))
     _prof.count("proj_out_norm_3d")
+    _prof.kernel_end(token)
     return out.permute(0, 4, 1, 2, 3)

@@ -72,7 +72,7 @@ def fused_swin_attention(
     if _prof._active:
         esize = q.element_size()
         masked = 0 if mask_t is None else (B if bnd is None else bnd)
-        token = _prof.attention_begin({
+        token = _prof.kernel_begin("fused_swin_attention", {
             # algorithmic bytes: q, k, v, out, the bias once, plus the mask rows
             # of masked windows (resolved when the timer is summarised)
             "bytes": 4 * B * H * N * D * esize + H * N * N * esize,
@@ -82,7 +82,7 @@ def fused_swin_attention(
         })
     ops.fused_swin_attention(out, q, k, v, bias, mask_t, bnd, float(scale))
     _prof.count("fused_swin_attention")
-    _prof.attention_end(token)
+    _prof.kernel_end(token)
     return out
 
 
@@ -129,7 +129,7 @@ def swin_window_attention_qkv(
     token = None
     if _prof._active:
         esize = qkv.element_size()
-        token = _prof.attention_begin({
+        token = _prof.kernel_begin("swin_window_attention_qkv", {
             # algorithmic bytes: q, k, v, out (the bias is gathered on chip and
             # the mask computed on chip)
             "bytes": 4 * B * H * N * D * esize,
@@ -140,7 +140,7 @@ def swin_window_attention_qkv(
                                   relative_position_index.contiguous(), list(num_windows),
                                   list(window_size), list(shift_size), float(scale))
     _prof.count("swin_window_attention_qkv")
-    _prof.attention_end(token)
+    _prof.kernel_end(token)
     return out
 
 
@@ -181,8 +181,11 @@ def window_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
     if bias is not None:
         b = bias.detach().to(device=x.device, dtype=x.dtype).to(torch.float32).contiguous()
     out = torch.empty((x2.shape[0], N), dtype=x.dtype, device=x.device)
+    token = _prof.kernel_begin("window_linear", lambda: {
+        "bytes": x2.numel() * x2.element_size() + out.numel() * out.element_size()})
     _native.require().window_linear(out, x2, w, b)
     _prof.count("window_linear")
+    _prof.kernel_end(token)
     return out.view(*x.shape[:-1], N)
 
 

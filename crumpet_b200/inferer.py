@@ -118,9 +118,12 @@ class SlidingWindowInferer:
         dtype = self.autocast_dtype if self.autocast_dtype is not None else volume.dtype
         out = torch.empty((len(batch), volume.shape[1], rd, rh, rw), dtype=dtype,
                           device=volume.device)
+        token = _prof.kernel_begin("roi_gather", lambda: {
+            "bytes": out.numel() * (out.element_size() + volume.element_size())})
         _ops.require().roi_gather(out, volume[0].contiguous(), [v for st in batch for v in st],
                                   list(self.roi))
         _prof.count("roi_gather")
+        _prof.kernel_end(token)
         return out
 
     @torch.no_grad()
@@ -138,9 +141,12 @@ class SlidingWindowInferer:
             else:
                 pred = self.model(window)
             if volume.is_cuda:
+                token = _prof.kernel_begin(
+                    "roi_accumulate", lambda: {"bytes": _accumulate_bytes(pred, batch, self.roi)})
                 _ops.require().roi_accumulate(acc[0], pred.contiguous(),
                                               [v for st in batch for v in st], list(self.roi))
                 _prof.count("roi_accumulate")
+                _prof.kernel_end(token)
             else:
                 for i, (z, y, x) in enumerate(batch):
                     acc[0, :, z:z + rd, y:y + rh, x:x + rw] += pred[i].float()
@@ -164,8 +170,11 @@ class SlidingWindowInferer:
         if not acc.is_cuda:
             return acc / self._count_map(tuple(acc.shape[2:]), acc.device)
         out = torch.empty_like(acc)
+        token = _prof.kernel_begin("roi_normalize",
+                                   lambda: {"bytes": 2 * acc.numel() * acc.element_size()})
         _ops.require().roi_normalize(out[0], acc[0], *self._axis_counts(acc.shape[2:], acc.device))
         _prof.count("roi_normalize")
+        _prof.kernel_end(token)
         return out
 
     @torch.no_grad()
@@ -179,9 +188,23 @@ class SlidingWindowInferer:
             logits = acc / self._count_map(tuple(acc.shape[2:]), acc.device)
             return logits[0].argmax(dim=0).to(torch.uint8)
         labels = torch.empty(acc.shape[2:], dtype=torch.uint8, device=acc.device)
+        token = _prof.kernel_begin("roi_argmax", lambda: {
+            "bytes": acc.numel() * acc.element_size() + labels.numel()})
         _ops.require().roi_argmax(labels, acc[0], *self._axis_counts(acc.shape[2:], acc.device))
         _prof.count("roi_argmax")
+        _prof.kernel_end(token)
         return labels
+
+
+def _accumulate_bytes(pred: torch.Tensor, batch, roi) -> int:
+    """Algorithmic bytes of one accumulate launch: the predictions once, and a read and
+    a write of the fp32 accumulator over the batch's bounding box."""
+    box = 1
+    for a in range(3):
+        lo = min(st[a] for st in batch)
+        hi = max(st[a] for st in batch) + roi[a]
+        box *= hi - lo
+    return pred.numel() * pred.element_size() + 8 * int(pred.shape[1]) * box
 
 
 def synthetic_volume(shape=(1, 1, 512, 512, 224), seed: int = 0) -> torch.Tensor:

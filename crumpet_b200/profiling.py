@@ -1,10 +1,10 @@
 """Launch accounting and live per-kernel timing for the benchmark.
 
 ``counters`` counts crumpet_b200 kernel launches per op.  ``KernelTimer``
-(enabled with ``with KernelTimer() as t:``) brackets every fused window
-attention launch with CUDA events on the launching stream and records the
-algorithmic work of that launch, so the benchmark can report the attention
-kernel's achieved bandwidth / FLOP rate inside the timed end-to-end region.
+(enabled with ``with KernelTimer() as t:``) brackets every crumpet_b200 launch
+with CUDA events on the launching stream and records the algorithmic work of
+that launch, so the benchmark can report, inside the timed end-to-end region,
+the attention kernel's achieved rates and every kernel's time against its ideal.
 """
 
 from __future__ import annotations
@@ -25,9 +25,25 @@ def total_launches() -> int:
     return sum(counters.values())
 
 
+# the attention ops (their launches also feed the bench's attention roofline)
+ATTENTION_OPS = ("fused_swin_attention", "swin_window_attention_qkv")
+
+
+def _resolve(work: dict) -> dict:
+    work = dict(work)
+    masked, per_window = work.pop("mask_bytes", (0, 0))
+    if isinstance(masked, torch.Tensor):
+        masked = int(masked.sum())
+    work["bytes"] = work.get("bytes", 0) + masked * per_window
+    return work
+
+
 class KernelTimer:
+    """CUDA events around every crumpet_b200 launch while active, with the launch's
+    algorithmic work ("bytes" moved, plus "flops" / "exps" for the attention)."""
+
     def __init__(self) -> None:
-        self.records: list[tuple[torch.cuda.Event, torch.cuda.Event, dict]] = []
+        self.records: list[tuple[torch.cuda.Event, torch.cuda.Event, str, dict]] = []
 
     def __enter__(self) -> "KernelTimer":
         _active.append(self)
@@ -36,39 +52,50 @@ class KernelTimer:
     def __exit__(self, *exc) -> None:
         _active.remove(self)
 
-    def summary(self) -> dict:
+    def summary(self, ops=ATTENTION_OPS) -> dict:
+        """Launch count, total / average ms and per-launch average work of `ops`."""
         torch.cuda.synchronize()
-        n = len(self.records)
+        recs = [r for r in self.records if r[2] in ops]
+        n = len(recs)
         if n == 0:
             return {"launches": 0}
-        ms = sum(s.elapsed_time(e) for s, e, _ in self.records)
+        ms = sum(s.elapsed_time(e) for s, e, _, _ in recs)
         tot = collections.Counter()
-        for _, _, work in self.records:
-            work = dict(work)
-            masked, per_window = work.pop("mask_bytes", (0, 0))
-            if isinstance(masked, torch.Tensor):
-                masked = int(masked.sum())
-            work["bytes"] = work.get("bytes", 0) + masked * per_window
-            tot.update(work)
+        for _, _, _, work in recs:
+            tot.update(_resolve(work))
         out = {"launches": n, "total_ms": ms, "avg_ms": ms / n}
         out.update({k: v / n for k, v in tot.items()})  # per-launch averages
         return out
 
+    def by_op(self) -> dict:
+        """Per op: launches, total ms and total work."""
+        torch.cuda.synchronize()
+        res: dict = {}
+        for s, e, op, work in self.records:
+            d = res.setdefault(op, {"launches": 0, "ms": 0.0, "bytes": 0, "exps": 0})
+            d["launches"] += 1
+            d["ms"] += s.elapsed_time(e)
+            w = _resolve(work)
+            d["bytes"] += w.get("bytes", 0)
+            d["exps"] += w.get("exps", 0)
+        return res
 
-def attention_begin(work: dict):
-    """Start-of-launch hook for fused attention; returns a token for attention_end."""
+
+def kernel_begin(op: str, work):
+    """Start-of-launch hook; `work` is a dict or a callable returning one (evaluated only
+    while a timer is active).  Returns a token for kernel_end."""
     if not _active:
         return None
     start = torch.cuda.Event(enable_timing=True)
     start.record()
-    return (start, work)
+    return (start, op, work() if callable(work) else work)
 
 
-def attention_end(token) -> None:
+def kernel_end(token) -> None:
     if token is None:
         return
-    start, work = token
+    start, op, work = token
     end = torch.cuda.Event(enable_timing=True)
     end.record()
     for t in _active:
-        t.records.append((start, end, work))
+        t.records.append((start, end, op, work))
