@@ -33,11 +33,21 @@ def _eager_accumulate(model, volume, roi, sw_batch, overlap, classes, autocast):
     return acc, acc / cnt
 
 
+GATHER_LAYOUTS = {
+    # W = 53 and x starts 17 / 21: one element per thread
+    "scalar_x": (53, [(0, 0, 0), (30, 5, 17), (38, 29, 21), (7, 13, 0)]),
+    # W = 64 and every x start a multiple of 8: eight x voxels per thread
+    "vec8_x": (64, [(0, 0, 0), (30, 5, 16), (38, 29, 32), (7, 13, 8)]),
+}
+
+
+@pytest.mark.parametrize("layout", list(GATHER_LAYOUTS))
+@pytest.mark.parametrize("in_dtype", [torch.float32, torch.float16])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
-def test_roi_gather_matches_slicing(out_dtype, cuda_device):
+def test_roi_gather_matches_slicing(out_dtype, in_dtype, layout, cuda_device):
     g = torch.Generator(device=cuda_device).manual_seed(0)
-    vol = torch.rand((2, 70, 61, 53), device=cuda_device, generator=g)
-    starts = [(0, 0, 0), (30, 5, 17), (38, 29, 21), (7, 13, 0)]
+    width, starts = GATHER_LAYOUTS[layout]
+    vol = torch.rand((2, 70, 61, width), device=cuda_device, generator=g).to(in_dtype)
     roi = (32, 32, 32)
     out = torch.empty((4, 2, *roi), dtype=out_dtype, device=cuda_device)
     _ops.require().roi_gather(out, vol, [v for s in starts for v in s], list(roi))
@@ -45,13 +55,15 @@ def test_roi_gather_matches_slicing(out_dtype, cuda_device):
     assert torch.equal(out, want)
 
 
-@pytest.mark.parametrize("width", [61, 64], ids=["scalar_x", "vec4_x"])
+@pytest.mark.parametrize("width,rw", [(61, 24), (64, 24), (80, 32)],
+                         ids=["scalar_x", "vec4_x", "vec8_x"])
 @pytest.mark.parametrize("pred_dtype", [torch.float16, torch.bfloat16, torch.float32])
-def test_roi_accumulate_bit_exact_with_overlaps(pred_dtype, width, cuda_device):
-    # W = 64 puts every ROI x start on a multiple of 4 (4-voxel vector path); W = 61
-    # clamps the last ROI to x = 37 (one voxel per thread)
+def test_roi_accumulate_bit_exact_with_overlaps(pred_dtype, width, rw, cuda_device):
+    # W = 64 puts every ROI x start on a multiple of 4 (4-voxel vector path); W = 80
+    # with 32-wide ROIs on multiples of 8 (8-voxel path); W = 61 clamps the last ROI to
+    # x = 37 (one voxel per thread)
     g = torch.Generator(device=cuda_device).manual_seed(1)
-    classes, spatial, roi = 5, (50, 47, width), (24, 24, 24)
+    classes, spatial, roi = 5, (50, 47, width), (24, 24, rw)
     starts = roi_grid(spatial, roi, 0.5)
     acc = torch.randn((classes, *spatial), device=cuda_device, generator=g)
     want = acc.clone()
@@ -60,15 +72,19 @@ def test_roi_accumulate_bit_exact_with_overlaps(pred_dtype, width, cuda_device):
         pred = torch.randn((len(batch), classes, *roi), device=cuda_device, generator=g).to(pred_dtype)
         _ops.require().roi_accumulate(acc, pred, [v for s in batch for v in s], list(roi))
         for i, (z, y, x) in enumerate(batch):
-            want[:, z:z + 24, y:y + 24, x:x + 24] += pred[i].float()
+            want[:, z:z + 24, y:y + 24, x:x + rw] += pred[i].float()
     assert torch.equal(acc, want)
 
 
-def test_roi_argmax_and_normalize_bit_exact(cuda_device):
+@pytest.mark.parametrize("width", [29, 32], ids=["scalar_x", "vec4_x"])
+@pytest.mark.parametrize("classes", [14, 5])
+def test_roi_argmax_and_normalize_bit_exact(classes, width, cuda_device):
+    # W = 32: four voxels per thread (classes loaded four planes at a time, 5 leaves a
+    # ragged last group); W = 29: one voxel per thread
     g = torch.Generator(device=cuda_device).manual_seed(2)
-    classes, spatial, roi = 14, (40, 33, 29), (16, 16, 16)
+    spatial, roi = (40, 33, width), (16, 16, 16)
     acc = torch.randn((classes, *spatial), device=cuda_device, generator=g)
-    acc[3, :5] = acc[7, :5]              # exact ties: the first index wins
+    acc[3, :5] = acc[classes - 1, :5]    # exact ties: the first index wins
     acc[2, 10:12, :4] = float("nan")     # NaN is the maximum
     counts = [torch.tensor(axis_counts(s, r, 0.5), device=cuda_device)
               for s, r in zip(spatial, roi)]
