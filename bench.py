@@ -331,14 +331,28 @@ def kernels_vs_roofline(per_op: dict, peaks: dict, clock, steps: int, dev_ms: fl
     sm_mhz = (clock or {}).get("sm_mhz") or 1965.0
     exp_per_ms = 16 * 148 * sm_mhz * 1e6 / 1e3
     hbm_bytes_per_ms = peaks["hbm_gbs"] * 1e6
-    rows, tot_ms, tot_ideal = {}, 0.0, 0.0
-    for op, d in sorted(per_op.items(), key=lambda kv: -kv[1]["ms"]):
+    def ideal_ms(d):
         ideal, bound = d["bytes"] / hbm_bytes_per_ms, "hbm"
         if d["exps"] and d["exps"] / exp_per_ms > ideal:
             ideal, bound = d["exps"] / exp_per_ms, "sfu"
+        return ideal, bound
+
+    rows, tot_ms, tot_ideal = {}, 0.0, 0.0
+    for op, d in sorted(per_op.items(), key=lambda kv: -kv[1]["ms"]):
+        ideal, bound = ideal_ms(d)
         rows[op] = {"launches_per_step": d["launches"] / steps, "ms_per_step": d["ms"] / steps,
                     "ideal_ms_per_step": ideal / steps, "frac": ideal / d["ms"] if d["ms"] else None,
                     "bound": bound}
+        # the same split by launch shape (largest first): where the time goes per stage
+        sizes = []
+        for nbytes, sd in sorted(d.get("sizes", {}).items(), key=lambda kv: -kv[0])[:6]:
+            s_ideal, _ = ideal_ms(sd)
+            sizes.append({"mb_per_launch": round(nbytes / 1e6, 3),
+                          "launches_per_step": sd["launches"] / steps,
+                          "us_per_launch": 1e3 * sd["ms"] / sd["launches"],
+                          "frac": s_ideal / sd["ms"] if sd["ms"] else None})
+        if len(sizes) > 1:
+            rows[op]["by_launch_size"] = sizes
         tot_ms += d["ms"]
         tot_ideal += ideal
     return {"ms_per_step": tot_ms / steps, "ideal_ms_per_step": tot_ideal / steps,

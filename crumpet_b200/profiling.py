@@ -68,16 +68,23 @@ class KernelTimer:
         return out
 
     def by_op(self) -> dict:
-        """Per op: launches, total ms and total work."""
+        """Per op: launches, total ms and total work; "sizes" splits the same totals by
+        the launch's algorithmic bytes (one entry per distinct launch shape, e.g. per
+        Swin stage)."""
         torch.cuda.synchronize()
         res: dict = {}
         for s, e, op, work in self.records:
-            d = res.setdefault(op, {"launches": 0, "ms": 0.0, "bytes": 0, "exps": 0})
-            d["launches"] += 1
-            d["ms"] += s.elapsed_time(e)
+            d = res.setdefault(op, {"launches": 0, "ms": 0.0, "bytes": 0, "exps": 0,
+                                    "sizes": {}})
+            ms = s.elapsed_time(e)
             w = _resolve(work)
-            d["bytes"] += w.get("bytes", 0)
-            d["exps"] += w.get("exps", 0)
+            for tgt in (d, d["sizes"].setdefault(int(w.get("bytes", 0)),
+                                                 {"launches": 0, "ms": 0.0, "bytes": 0,
+                                                  "exps": 0})):
+                tgt["launches"] += 1
+                tgt["ms"] += ms
+                tgt["bytes"] += w.get("bytes", 0)
+                tgt["exps"] += w.get("exps", 0)
         return res
 
 

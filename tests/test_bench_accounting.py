@@ -1,0 +1,50 @@
+"""bench.py's in-step roofline accounting, on synthetic launch records (no GPU):
+per-op ideal times at the HBM copy rate or the SFU exponential rate, and the split
+of an op's launches by launch shape."""
+
+from __future__ import annotations
+
+import pytest
+
+import bench
+
+PEAKS = {"hbm_gbs": 6449.7, "source": "measured"}
+CLOCK = {"sm_mhz": 1965.0}
+
+
+def _rec(launches, ms, nbytes, exps=0):
+    return {"launches": launches, "ms": ms, "bytes": nbytes, "exps": exps}
+
+
+def test_hbm_and_sfu_bounds():
+    per_op = {
+        "copy": dict(_rec(2, 0.2, 1_289_940_000), sizes={}),
+        # 2 * 4.65e9 exponentials per ms of SFU time at 1965 MHz: 1 ms ideal
+        "attn": dict(_rec(1, 2.0, 1_000, exps=16 * 148 * 1965e3), sizes={}),
+    }
+    out = bench.kernels_vs_roofline(per_op, PEAKS, CLOCK, steps=1, dev_ms=10.0)
+    assert out["by_op"]["copy"]["bound"] == "hbm"
+    assert out["by_op"]["copy"]["frac"] == pytest.approx(1.0, rel=1e-3)
+    assert out["by_op"]["attn"]["bound"] == "sfu"
+    assert out["by_op"]["attn"]["frac"] == pytest.approx(0.5, rel=1e-6)
+    assert out["share_of_step"] == pytest.approx(0.22)
+    assert "by_launch_size" not in out["by_op"]["copy"]
+
+
+def test_split_by_launch_size_largest_first():
+    big, small = 175_000_000, 50_000_000
+    per_op = {"norm": dict(_rec(6, 6.0, 2 * big + 4 * small), sizes={
+        small: _rec(4, 5.92, 4 * small),
+        big: _rec(2, 0.08, 2 * big),
+    })}
+    out = bench.kernels_vs_roofline(per_op, PEAKS, CLOCK, steps=2, dev_ms=100.0)
+    sizes = out["by_op"]["norm"]["by_launch_size"]
+    assert [s["mb_per_launch"] for s in sizes] == [175.0, 50.0]
+    assert sizes[0]["launches_per_step"] == 1.0
+    assert sizes[0]["us_per_launch"] == pytest.approx(40.0)
+    assert sizes[0]["frac"] == pytest.approx(2 * big / (PEAKS["hbm_gbs"] * 1e6) / 0.08)
+    assert out["by_op"]["norm"]["ms_per_step"] == pytest.approx(3.0)
+
+
+def test_no_records():
+    assert bench.kernels_vs_roofline({}, PEAKS, CLOCK, steps=1, dev_ms=1.0) is None
