@@ -15,11 +15,14 @@ NCCL reduce merges the accumulators on rank 0 (total work fixed: strong scaling)
 ``value``: ROIs/s with the volume resident in HBM and the segmentation left
 on the device, CUDA-event timed, max over ranks.  ``e2e``: the same with the
 volume copied from pinned host memory and the segmentation copied back inside
-every step.  The 3.3 GB accumulator and 235 MB volume exceed L2, so no flush is
-needed between steps.  Also reported: live timing of the fused attention
-kernel inside the timed region (roofline), every crumpet_b200 kernel of the timed
-region against its roofline (crumpet_kernels: event time vs algorithmic bytes at
-the measured HBM rate, or the SFU rate for the attention's exponentials),
+every step.  Both run each ROI batch's network forward as a CUDA graph replay
+(``--eager``: without graphs).  The 3.3 GB accumulator and 235 MB volume exceed
+L2, so no flush is needed between steps.  Also reported: the same steps on the
+eager forward with CUDA events around every crumpet_b200 launch (``eager``), and
+from that pass the fused attention kernel's rates (roofline) and every
+crumpet_b200 kernel against its roofline (crumpet_kernels: event time vs
+algorithmic bytes at the measured HBM rate, or the SFU rate for the attention's
+exponentials),
 stand-alone per-kernel HBM GB/s at the BASELINE stage-0 sizes, clocks sampled
 during the timed region, and the CPU eager baseline (the unpatched network on
 the host cores).
@@ -47,6 +50,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "Swin UNETR 96³ ROIs/s (fp16, 1/2/4/8 B200); per-kernel HBM GB/s vs peak"
 UNIT = "ROIs/s"
+PER_KERNEL_PASS = ("per-kernel pass: the timed steps repeated on the eager forward with CUDA "
+                   "events around every crumpet_b200 launch on its stream (the timed steps "
+                   "replay CUDA graphs of the same kernels, which cannot be bracketed per kernel)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
                   "source": "fallback"}
 
@@ -63,6 +69,8 @@ def parse_args():
     ap.add_argument("--overlap", type=float, default=0.5)
     ap.add_argument("--skip-kernels", action="store_true", help="omit stand-alone kernel timings")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline")
+    ap.add_argument("--eager", action="store_true",
+                    help="run the timed steps without CUDA graphs (the eager forward)")
     ap.add_argument("--only-kernels", action="store_true",
                     help="print only the stand-alone kernel timings (profiling target)")
     return ap.parse_args()
@@ -442,7 +450,10 @@ def main() -> None:
     model = build_model(device)
     crumpet.patch_monai_swin_unetr(swin_unetr)
     inferer = SlidingWindowInferer(model, (args.roi,) * 3, args.sw_batch, args.overlap, 14,
-                                   torch.float16, rank, world)
+                                   torch.float16, rank, world, cuda_graphs=not args.eager)
+    # the same inference without graphs: its launches can be bracketed one by one
+    eager_inferer = SlidingWindowInferer(model, (args.roi,) * 3, args.sw_batch, args.overlap,
+                                         14, torch.float16, rank, world)
     spatial = tuple(args.volume)
     n_rois = len(roi_grid(spatial, (args.roi,) * 3, args.overlap))
     host = synthetic_volume((1, 1, *spatial)).pin_memory()
@@ -468,8 +479,7 @@ def main() -> None:
     launches0 = profiling.total_launches()
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(visible_gpu_ids(world) if rank == 0 else []) as clocks, \
-            profiling.KernelTimer() as ktimer:
+    with ClockSampler(visible_gpu_ids(world) if rank == 0 else []) as clocks:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
@@ -481,6 +491,25 @@ def main() -> None:
     dev_ms = max_over_ranks(start.elapsed_time(end))
     launches = profiling.total_launches() - launches0
     clock = clocks.summary() if rank == 0 else None
+
+    # ---- per-kernel pass: the same steps on the eager forward, with CUDA events around
+    # every crumpet_b200 launch (a graph replay cannot be bracketed kernel by kernel)
+    if args.eager:
+        eager_inferer = inferer
+    else:
+        eager_inferer.segment(vol)  # warm
+    barrier()
+    torch.cuda.synchronize()
+    with profiling.KernelTimer() as ktimer:
+        s1 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        s1.record()
+        for _ in range(args.steps):
+            eager_inferer.segment(vol)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+    eager_ms = max_over_ranks(s1.elapsed_time(e1))
     attn = ktimer.summary()
     per_op = ktimer.by_op()
 
@@ -552,12 +581,22 @@ def main() -> None:
                 # ncu DRAM bytes of one captured launch, scaled by algorithmic bytes
                 roofline["traffic"] = attn["bytes"] * tr["dram_over_algorithmic"]
                 roofline["traffic_source"] = tr["command"]
-        crumpet_kernels = kernels_vs_roofline(per_op, peaks, clock, args.steps, dev_ms)
+            roofline["timed_in"] = PER_KERNEL_PASS
+        crumpet_kernels = kernels_vs_roofline(per_op, peaks, clock, args.steps, eager_ms)
+        if crumpet_kernels is not None:
+            crumpet_kernels["timed_in"] = PER_KERNEL_PASS
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": workload_config(args, world),
+            "config": dict(workload_config(args, world),
+                           execution="eager forward" if args.eager else
+                           "CUDA graph replay of each ROI batch's forward (one graph per "
+                           "batch size); crop and accumulate launches outside the graphs"),
+            "eager": {"value": n_rois * args.steps / (eager_ms / 1000.0), "unit": UNIT,
+                      "ms_per_step": eager_ms / args.steps,
+                      "note": "same steps without CUDA graphs, every crumpet_b200 launch "
+                              "bracketed by CUDA events (the per-kernel pass)"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": host.numel() * host.element_size() * world,
                     "d2h_bytes_per_step": seg_host.numel()},

@@ -13,6 +13,16 @@ one launch per ROI batch instead of a copy, a cast and an add per ROI, with the
 same fp32 additions in the same order, so the results are bit-identical to the
 eager loop; CPU tensors take the eager torch path.
 
+With ``cuda_graphs=True`` each ROI batch's network forward is a CUDA graph
+replay: one graph per batch size, captured on first use (after two warm-up
+forwards on a side stream) with the crop kernel writing straight into the
+graph's input buffer and the accumulate kernel reading its output buffer.  The
+crop and accumulate launches stay outside the graph (their ROI starts change
+from batch to batch).  Replays run the same kernels on the same data as the eager
+forward, so the results are identical; what goes away is the host's per-launch
+work between the GPU's kernels.  The model must be fixed (weights are read
+in place by the replays) and its forward free of host synchronisation.
+
 Multi-GPU: one process per GPU.  Rank r runs the r-th contiguous 1/world of the ROI
 grid (balanced to one ROI), cut into batches; each rank accumulates its own
 predictions, and the only collective is one NCCL sum-reduce of the
@@ -61,13 +71,14 @@ class SlidingWindowInferer:
     ``rank``/``world`` select this process's share of the ROI batches (a
     single-process run is rank 0 of 1).  ``autocast_dtype`` wraps every
     forward in ``torch.autocast`` (fp16 in the benchmark, as in the
-    reference's runs).
+    reference's runs).  ``cuda_graphs`` replays each batch's forward from a
+    captured CUDA graph (CUDA volumes only; see the module docstring).
     """
 
     def __init__(self, model: torch.nn.Module, roi_size=(96, 96, 96), sw_batch_size: int = 4,
                  overlap: float = 0.5, num_classes: int = 14,
                  autocast_dtype: torch.dtype | None = torch.float16, rank: int = 0, world: int = 1,
-                 group=None):
+                 group=None, cuda_graphs: bool = False):
         self.model = model
         self.roi = tuple(int(r) for r in roi_size)
         self.sw_batch = int(sw_batch_size)
@@ -77,7 +88,9 @@ class SlidingWindowInferer:
         self.rank = rank
         self.world = world
         self.group = group
+        self.cuda_graphs = bool(cuda_graphs)
         self._count_cache: dict = {}
+        self._graphs: dict = {}
 
     def rois(self, spatial) -> list[tuple[int, int, int]]:
         return roi_grid(spatial, self.roi, self.overlap)
@@ -109,15 +122,18 @@ class SlidingWindowInferer:
                 for s, r in zip(spatial, self.roi)]
         return self._count_cache[key]
 
-    def _gather(self, volume: torch.Tensor, batch) -> torch.Tensor:
+    def _window_dtype(self, volume: torch.Tensor) -> torch.dtype:
+        # under autocast the first convolutions cast their input to the autocast
+        # dtype; the crop writes that dtype directly (same rounding)
+        return self.autocast_dtype if self.autocast_dtype is not None else volume.dtype
+
+    def _gather(self, volume: torch.Tensor, batch, out: torch.Tensor | None = None) -> torch.Tensor:
         rd, rh, rw = self.roi
         if not volume.is_cuda:
             return torch.cat([volume[..., z:z + rd, y:y + rh, x:x + rw] for z, y, x in batch])
-        # under autocast the first convolutions cast their input to the autocast
-        # dtype; the crop writes that dtype directly (same rounding)
-        dtype = self.autocast_dtype if self.autocast_dtype is not None else volume.dtype
-        out = torch.empty((len(batch), volume.shape[1], rd, rh, rw), dtype=dtype,
-                          device=volume.device)
+        if out is None:
+            out = torch.empty((len(batch), volume.shape[1], rd, rh, rw),
+                              dtype=self._window_dtype(volume), device=volume.device)
         token = _prof.kernel_begin("roi_gather", lambda: {
             "bytes": out.numel() * (out.element_size() + volume.element_size())})
         _ops.require().roi_gather(out, volume[0].contiguous(), [v for st in batch for v in st],
@@ -125,6 +141,33 @@ class SlidingWindowInferer:
         _prof.count("roi_gather")
         _prof.kernel_end(token)
         return out
+
+    def _forward(self, window: torch.Tensor, cache: bool = True) -> torch.Tensor:
+        if self.autocast_dtype is None:
+            return self.model(window)
+        with torch.autocast("cuda", dtype=self.autocast_dtype, cache_enabled=cache):
+            return self.model(window)
+
+    def _graph(self, n: int, volume: torch.Tensor):
+        """(graph, input buffer, output buffer, launch counts of one replay) for batches
+        of n ROIs, captured on first use."""
+        dtype = self._window_dtype(volume)
+        key = (n, int(volume.shape[1]), dtype, volume.device)
+        if key not in self._graphs:
+            static_in = torch.zeros((n, volume.shape[1], *self.roi), dtype=dtype,
+                                    device=volume.device)
+            # warm-up on a side stream (library handles, workspaces, the mask cache)
+            side = torch.cuda.Stream(volume.device)
+            side.wait_stream(torch.cuda.current_stream(volume.device))
+            with torch.cuda.stream(side), _prof.suspended():
+                for _ in range(2):
+                    self._forward(static_in, cache=False)
+            torch.cuda.current_stream(volume.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with _prof.suspended() as launches, torch.cuda.graph(graph):
+                static_out = self._forward(static_in, cache=False)
+            self._graphs[key] = (graph, static_in, static_out, launches.delta)
+        return self._graphs[key]
 
     @torch.no_grad()
     def accumulate(self, volume: torch.Tensor) -> tuple[torch.Tensor, int]:
@@ -134,12 +177,13 @@ class SlidingWindowInferer:
         acc = torch.zeros((1, self.num_classes, *spatial), dtype=torch.float32, device=volume.device)
         done = 0
         for batch in self.my_batches(spatial):
-            window = self._gather(volume, batch)
-            if self.autocast_dtype is not None:
-                with torch.autocast("cuda", dtype=self.autocast_dtype):
-                    pred = self.model(window)
+            if self.cuda_graphs and volume.is_cuda:
+                graph, static_in, pred, launches = self._graph(len(batch), volume)
+                self._gather(volume, batch, out=static_in)
+                graph.replay()
+                _prof.count_replay(launches)
             else:
-                pred = self.model(window)
+                pred = self._forward(self._gather(volume, batch))
             if volume.is_cuda:
                 token = _prof.kernel_begin(
                     "roi_accumulate", lambda: {"bytes": _accumulate_bytes(pred, batch, self.roi)})

@@ -88,6 +88,29 @@ class KernelTimer:
         return res
 
 
+class suspended:
+    """Within this context no timer records launches, and the launch counts it adds are
+    handed back as ``delta`` and removed from ``counters``: used while a CUDA graph is
+    captured, where nothing runs yet (each replay adds ``delta`` with ``count_replay``)."""
+
+    def __enter__(self) -> "suspended":
+        self._timers = list(_active)
+        _active.clear()
+        self._before = collections.Counter(counters)
+        self.delta: "collections.Counter[str]" = collections.Counter()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.delta = counters - self._before
+        counters.clear()
+        counters.update(self._before)
+        _active.extend(self._timers)
+
+
+def count_replay(delta: "collections.Counter[str]") -> None:
+    counters.update(delta)
+
+
 def kernel_begin(op: str, work):
     """Start-of-launch hook; `work` is a dict or a callable returning one (evaluated only
     while a timer is active).  Returns a token for kernel_end."""

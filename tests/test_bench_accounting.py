@@ -48,3 +48,25 @@ def test_split_by_launch_size_largest_first():
 
 def test_no_records():
     assert bench.kernels_vs_roofline({}, PEAKS, CLOCK, steps=1, dev_ms=1.0) is None
+
+
+def test_capture_suspends_timers_and_hands_back_the_launch_counts():
+    """While a CUDA graph is captured nothing runs: the launches counted then are taken
+    out of the counters and handed back, to be added once per replay."""
+    from crumpet_b200 import profiling
+
+    timer = profiling.KernelTimer()
+    with timer:
+        profiling.count("roi_gather")
+        before = dict(profiling.counters)
+        with profiling.suspended() as cap:
+            assert profiling._active == []
+            assert profiling.kernel_begin("x", {}) is None  # no timer records during capture
+            profiling.count("swin_window_attention_qkv", 8)
+            profiling.count("window_linear", 6)
+        assert profiling._active == [timer]
+        assert dict(profiling.counters) == before
+        assert dict(cap.delta) == {"swin_window_attention_qkv": 8, "window_linear": 6}
+        profiling.count_replay(cap.delta)
+        profiling.count_replay(cap.delta)
+        assert profiling.counters["window_linear"] == before.get("window_linear", 0) + 12

@@ -72,6 +72,35 @@ def test_sliding_window_patched_vs_eager(cuda_device):
     assert (logit_p - logit_e).abs().max().item() < 5e-2
 
 
+def test_sliding_window_cuda_graphs_match_eager_bit_for_bit(cuda_device):
+    """CUDA-graph mode replays the same kernels on the same data: logits and labels equal
+    the eager patched run's exactly, over two volumes in a row (the second replays the
+    graphs captured for the first) and a ragged last batch (6 ROIs in batches of 4: a
+    second graph for batches of 2), and each replay counts its crumpet_b200 launches."""
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
+    vols = [torch.rand((1, 1, 96, 144, 160), device=cuda_device) for _ in range(2)]
+    eager = SlidingWindowInferer(model, (96, 96, 96), 4, 0.5, 14, torch.float16)
+    graphed = SlidingWindowInferer(model, (96, 96, 96), 4, 0.5, 14, torch.float16,
+                                   cuda_graphs=True)
+    assert len(graphed.rois((96, 144, 160))) == 6
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        for vol in vols:
+            want_logits, want_seg = eager.logits(vol), eager.segment(vol)
+            n0 = profiling.counters["swin_window_attention_qkv"]
+            got_logits = graphed.logits(vol)
+            n1 = profiling.counters["swin_window_attention_qkv"]
+            got_seg = graphed.segment(vol)
+            assert torch.equal(got_logits, want_logits)
+            assert torch.equal(got_seg, want_seg)
+            # 8 attention launches per forward, one forward per batch of 4 and of 2
+            assert n1 - n0 == 2 * 8
+        assert sorted(k[0] for k in graphed._graphs) == [2, 4]
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+
+
 def test_head_dim_32_network_argmax_agreement(cuda_device):
     # feature size 96: heads (3, 6, 12, 24) of head_dim 32 at every stage
     torch.manual_seed(0)
