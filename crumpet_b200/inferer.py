@@ -21,7 +21,10 @@ crop and accumulate launches stay outside the graph (their ROI starts change
 from batch to batch).  Replays run the same kernels on the same data as the eager
 forward, so the results are identical; what goes away is the host's per-launch
 work between the GPU's kernels.  The model must be fixed (weights are read
-in place by the replays) and its forward free of host synchronisation.
+in place by the replays) and its forward free of host synchronisation.  A graph
+holds the forward as it was captured -- including whether crumpet_b200's patch
+was applied -- so after changing the model (patching or unpatching it, replacing
+modules or parameter tensors) call ``reset_graphs()``.
 
 Multi-GPU: one process per GPU.  Rank r runs the r-th contiguous 1/world of the ROI
 grid (balanced to one ROI), cut into batches; each rank accumulates its own
@@ -147,6 +150,10 @@ class SlidingWindowInferer:
             return self.model(window)
         with torch.autocast("cuda", dtype=self.autocast_dtype, cache_enabled=cache):
             return self.model(window)
+
+    def reset_graphs(self) -> None:
+        """Drop the captured graphs (and their memory pool); the next batches capture anew."""
+        self._graphs.clear()
 
     def _graph(self, n: int, volume: torch.Tensor):
         """(graph, input buffer, output buffer, launch counts of one replay) for batches

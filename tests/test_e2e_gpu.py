@@ -99,6 +99,11 @@ def test_sliding_window_cuda_graphs_match_eager_bit_for_bit(cuda_device):
         assert sorted(k[0] for k in graphed._graphs) == [2, 4]
     finally:
         crumpet.unpatch_monai_swin_unetr()
+    # unpatched: the captured graphs still hold the patched forward until reset
+    graphed.reset_graphs()
+    n0 = profiling.counters["swin_window_attention_qkv"]
+    assert torch.equal(graphed.logits(vols[1]), eager.logits(vols[1]))
+    assert profiling.counters["swin_window_attention_qkv"] == n0
 
 
 def test_head_dim_32_network_argmax_agreement(cuda_device):
