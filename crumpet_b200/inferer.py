@@ -185,9 +185,11 @@ class SlidingWindowInferer:
         done = 0
         for batch in self.my_batches(spatial):
             if self.cuda_graphs and volume.is_cuda:
-                graph, static_in, pred, launches = self._graph(len(batch), volume)
-                self._gather(volume, batch, out=static_in)
-                graph.replay()
+                # capture and replay on the volume's device and its current stream
+                with torch.cuda.device(volume.device):
+                    graph, static_in, pred, launches = self._graph(len(batch), volume)
+                    self._gather(volume, batch, out=static_in)
+                    graph.replay()
                 _prof.count_replay(launches)
             else:
                 pred = self._forward(self._gather(volume, batch))
