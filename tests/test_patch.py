@@ -133,3 +133,18 @@ def test_sliding_window_eager_cpu_matches_single_forward():
         got = inf.logits(x)
         want = model(x)
     assert torch.allclose(got, want)
+
+
+def test_cuda_graphs_option_leaves_cpu_volumes_on_the_eager_path():
+    # graphs apply to CUDA volumes only: a CPU volume runs the eager loop and captures nothing
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(1, 3, 12, depths=(1, 1, 1, 1)).eval()
+    x = torch.rand((1, 1, 64, 64, 80))
+    plain = SlidingWindowInferer(model, (64, 64, 64), 1, 0.5, num_classes=3, autocast_dtype=None)
+    graphed = SlidingWindowInferer(model, (64, 64, 64), 1, 0.5, num_classes=3,
+                                   autocast_dtype=None, cuda_graphs=True)
+    assert torch.equal(graphed.logits(x), plain.logits(x))
+    assert torch.equal(graphed.segment(x), plain.segment(x))
+    assert graphed._graphs == {}
+    graphed.reset_graphs()
+    assert graphed._graphs == {}
