@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import contextlib
 import os
-from typing import Sequence
+from typing import NamedTuple, Sequence
 
 import torch
 
@@ -58,60 +58,85 @@ _fakes_registered = False
 
 
 def _register_fake_impls() -> None:
-    # The ops mutate preallocated outputs and return nothing, so their fake
-    # (meta) implementations are no-ops (reference: torch-ext/crumpet/__init__.py:50-73).
+    """Shape-only (fake / meta) implementations for the ops.  They mutate preallocated
+    outputs and return nothing, so each fake is a no-op (reference:
+    torch-ext/crumpet/__init__.py:50-73).  Runs once, when the native library loads."""
     global _fakes_registered
-    if _fakes_registered or not _native.available():
+    register = getattr(torch.library, "register_fake", None)
+    if _fakes_registered or register is None or not _native.loaded():
         return
     _fakes_registered = True
-    register = getattr(torch.library, "register_fake", None)
-    if register is None:
-        return
+    noop = lambda *args, **kwargs: None  # noqa: E731
     for name in _OP_NAMES:
         try:
-            register(f"crumpet_ops::{name}")(lambda *args, **kwargs: None)
+            register(f"crumpet_ops::{name}")(noop)
         except (RuntimeError, AttributeError, ValueError):
-            pass
+            pass  # already registered (a second package import in the same process)
 
 
-_register_fake_impls()
+_native.on_load(_register_fake_impls)
 
 
-@contextlib.contextmanager
-def _nvtx_range(name: str):
+def _nvtx(name: str):
+    """An NVTX range around a launch when CRUMPET_ENABLE_NVTX=1 and CUDA is up."""
     if os.environ.get("CRUMPET_ENABLE_NVTX", "0") == "1" and torch.cuda.is_available():
-        torch.cuda.nvtx.range_push(name)
-        try:
-            yield
-        finally:
-            torch.cuda.nvtx.range_pop()
-    else:
-        yield
+        return torch.cuda.nvtx.range(name)
+    return contextlib.nullcontext()
 
 
-def _triple(name: str, value: Sequence[int]) -> tuple[int, int, int]:
-    if len(value) != 3:
+def _as_triple(name: str, value: Sequence[int]) -> tuple[int, int, int]:
+    items = tuple(int(v) for v in value)
+    if len(items) != 3:
         raise ValueError(f"{name} must contain exactly three values")
-    out = tuple(int(v) for v in value)
-    if any(v < 0 for v in out):
+    if min(items) < 0:
         raise ValueError(f"{name} values must be non-negative")
-    return out  # type: ignore[return-value]
+    return items  # type: ignore[return-value]
 
 
-def _validate_shape(
-    D: int, H: int, W: int, window_size: tuple[int, int, int], shift_size: tuple[int, int, int]
-) -> None:
-    if D <= 0 or H <= 0 or W <= 0:
-        raise ValueError("D, H and W must be positive")
-    if any(v <= 0 for v in window_size):
-        raise ValueError("window_size values must be positive")
-    if D % window_size[0] or H % window_size[1] or W % window_size[2]:
-        raise ValueError(
-            "standalone CRUMPET kernels require D, H and W to be divisible by window_size"
-        )
-    for axis, (shift, window) in enumerate(zip(shift_size, window_size)):
-        if shift < 0 or shift >= window:
-            raise ValueError(f"shift_size[{axis}] must satisfy 0 <= shift < window_size[{axis}]")
+class _Grid(NamedTuple):
+    """A volume [D, H, W] cut into windows, with the cyclic shift of a Swin block."""
+
+    dims: tuple[int, int, int]
+    window: tuple[int, int, int]
+    shift: tuple[int, int, int]
+
+    @property
+    def tokens(self) -> int:  # tokens per window
+        return self.window[0] * self.window[1] * self.window[2]
+
+    @property
+    def windows(self) -> int:  # windows per batch entry
+        return ((self.dims[0] // self.window[0]) * (self.dims[1] // self.window[1])
+                * (self.dims[2] // self.window[2]))
+
+    def windows_shape(self, B: int, C: int) -> tuple[int, int, int]:
+        return (B * self.windows, self.tokens, C)
+
+
+# The rules a grid must meet, checked in this order; each is (violated?, message).  The
+# messages and the order are the reference's (torch-ext/crumpet/__init__.py:89-117): its
+# tests match on "divisible" and "shift_size".
+_GRID_RULES = (
+    (lambda g: min(g.dims) <= 0, lambda g: "D, H and W must be positive"),
+    (lambda g: min(g.window) <= 0, lambda g: "window_size values must be positive"),
+    (lambda g: any(d % w for d, w in zip(g.dims, g.window)),
+     lambda g: "standalone CRUMPET kernels require D, H and W to be divisible by window_size"),
+    (lambda g: _first_bad_shift(g) is not None,
+     lambda g: "shift_size[{0}] must satisfy 0 <= shift < window_size[{0}]".format(_first_bad_shift(g))),
+)
+
+
+def _first_bad_shift(g: _Grid) -> int | None:
+    return next((a for a in range(3) if not 0 <= g.shift[a] < g.window[a]), None)
+
+
+def _grid(D, H, W, window_size, shift_size) -> _Grid:
+    g = _Grid((int(D), int(H), int(W)), _as_triple("window_size", window_size),
+              _as_triple("shift_size", shift_size))
+    for violated, message in _GRID_RULES:
+        if violated(g):
+            raise ValueError(message(g))
+    return g
 
 
 def _check_dtype(dtype: torch.dtype) -> None:
@@ -128,12 +153,6 @@ def _require_cuda(t_or_dev, what: str) -> None:
         )
 
 
-def _geometry(D, H, W, window_size):
-    volume = window_size[0] * window_size[1] * window_size[2]
-    num_windows = (D // window_size[0]) * (H // window_size[1]) * (W // window_size[2])
-    return volume, num_windows
-
-
 def compute_attn_mask_3d(
     D: int,
     H: int,
@@ -144,75 +163,76 @@ def compute_attn_mask_3d(
     device: torch.device | str,
 ) -> torch.Tensor:
     """Shifted 3D Swin attention mask ``[num_windows, volume, volume]`` (0 / -100), cached."""
-    window_size = _triple("window_size", window_size)
-    shift_size = _triple("shift_size", shift_size)
+    ws = _as_triple("window_size", window_size)
+    ss = _as_triple("shift_size", shift_size)
     _check_dtype(dtype)
-    D, H, W = int(D), int(H), int(W)
-    _validate_shape(D, H, W, window_size, shift_size)
+    g = _grid(D, H, W, ws, ss)
     dev = torch.device(device)
-    volume, num_windows = _geometry(D, H, W, window_size)
+    shape = (g.windows, g.tokens, g.tokens)
     if dev.type == "meta":
-        return torch.empty((num_windows, volume, volume), dtype=dtype, device=dev)
+        return torch.empty(shape, dtype=dtype, device=dev)
     _require_cuda(dev, "compute_attn_mask_3d")
-    if volume > 1024:
+    if g.tokens > 1024:
         raise ValueError("compute_attn_mask_3d supports window volumes up to 1024")
 
     def compute() -> torch.Tensor:
-        out = torch.empty((num_windows, volume, volume), dtype=dtype, device=dev)
-        with _nvtx_range("crumpet.compute_attn_mask_3d"):
-            _native.require().compute_attn_mask_3d(out, D, H, W, *window_size, *shift_size)
+        out = torch.empty(shape, dtype=dtype, device=dev)
+        with _nvtx("crumpet.compute_attn_mask_3d"):
+            _native.require().compute_attn_mask_3d(out, *g.dims, *g.window, *g.shift)
             _prof.count("compute_attn_mask_3d")
         return out
 
-    return get_or_compute_mask(make_mask_key(D, H, W, window_size, shift_size, dtype, dev), compute)
+    return get_or_compute_mask(make_mask_key(*g.dims, g.window, g.shift, dtype, dev), compute)
 
 
-class _ShiftPartitionFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, window_size, shift_size):
-        x = x.contiguous()
-        B, D, H, W, C = (int(v) for v in x.shape)
-        volume, num_windows = _geometry(D, H, W, window_size)
-        out = torch.empty((B * num_windows, volume, C), dtype=x.dtype, device=x.device)
-        _native.require().fused_shift_partition_3d(out, x, *window_size, *shift_size)
-        ctx.shape = (B, D, H, W, C)
-        ctx.window_size = window_size
-        ctx.shift_size = shift_size
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_output):
-        B, D, H, W, C = ctx.shape
-        grad_x = torch.empty((B, D, H, W, C), dtype=grad_output.dtype, device=grad_output.device)
-        _native.require().fused_shift_partition_3d_backward(
-            grad_x, grad_output.contiguous(), B, D, H, W, C, *ctx.window_size, *ctx.shift_size
-        )
-        return grad_x, None, None
+# The two window permutations and their gradients.  Each is one op; the gradient of
+# one permutation is the other permutation, registered under the reference's
+# *_backward op names (torch-ext/torch_binding.cpp:23-25,29-31).
+#   (to_windows, gradient) -> op name
+_PERMUTE_OPS = {
+    (True, False): "fused_shift_partition_3d",
+    (False, False): "fused_unshift_unpartition_3d",
+    (False, True): "fused_shift_partition_3d_backward",
+    (True, True): "fused_unshift_unpartition_3d_backward",
+}
 
 
-class _UnshiftUnpartitionFn(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, windows, B, D, H, W, C, window_size, shift_size):
-        windows = windows.contiguous()
-        out = torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
-        _native.require().fused_unshift_unpartition_3d(
-            out, windows, B, D, H, W, C, *window_size, *shift_size
-        )
-        ctx.window_size = window_size
-        ctx.shift_size = shift_size
-        return out
+def _permute(t: torch.Tensor, to_windows: bool, g: _Grid, B: int, C: int,
+             gradient: bool = False) -> torch.Tensor:
+    """Launch one window permutation of ``t`` into a new tensor: volume [B, D, H, W, C]
+    -> windows (``to_windows``) or windows -> volume."""
+    name = _PERMUTE_OPS[(to_windows, gradient)]
+    op = getattr(_native.require(), name)
+    src = t.contiguous()
+    if to_windows:
+        out = torch.empty(g.windows_shape(B, C), dtype=t.dtype, device=t.device)
+        op(out, src, *g.window, *g.shift)
+    else:
+        out = torch.empty((B, *g.dims, C), dtype=t.dtype, device=t.device)
+        op(out, src, B, *g.dims, C, *g.window, *g.shift)
+    _prof.count(name)
+    return out
+
+
+class _WindowPermute(torch.autograd.Function):
+    """Autograd for both permutations: the backward runs the inverse permutation."""
 
     @staticmethod
-    def backward(ctx, grad_output):
-        B, D, H, W, C = (int(v) for v in grad_output.shape)
-        volume, num_windows = _geometry(D, H, W, ctx.window_size)
-        grad_windows = torch.empty(
-            (B * num_windows, volume, C), dtype=grad_output.dtype, device=grad_output.device
-        )
-        _native.require().fused_unshift_unpartition_3d_backward(
-            grad_windows, grad_output.contiguous(), *ctx.window_size, *ctx.shift_size
-        )
-        return grad_windows, None, None, None, None, None, None, None
+    def forward(ctx, t, to_windows, g, B, C):
+        ctx.args = (to_windows, g, B, C)
+        return _permute(t, to_windows, g, B, C)
+
+    @staticmethod
+    def backward(ctx, grad):
+        to_windows, g, B, C = ctx.args
+        return _permute(grad, not to_windows, g, B, C, gradient=True), None, None, None, None
+
+
+def _run_permute(t: torch.Tensor, to_windows: bool, g: _Grid, B: int, C: int) -> torch.Tensor:
+    with _nvtx("crumpet." + _PERMUTE_OPS[(to_windows, False)]):
+        if torch.is_grad_enabled() and t.requires_grad:
+            return _WindowPermute.apply(t, to_windows, g, B, C)
+        return _permute(t, to_windows, g, B, C)
 
 
 def fused_shift_partition_3d(
@@ -221,22 +241,15 @@ def fused_shift_partition_3d(
     """Cyclic shift by ``-shift_size`` and 3D window partition of ``[B, D, H, W, C]``."""
     if x.ndim != 5:
         raise ValueError("x must have shape [B, D, H, W, C]")
-    window_size = _triple("window_size", window_size)
-    shift_size = _triple("shift_size", shift_size)
+    ws = _as_triple("window_size", window_size)
+    ss = _as_triple("shift_size", shift_size)
     _check_dtype(x.dtype)
     B, D, H, W, C = (int(v) for v in x.shape)
-    _validate_shape(D, H, W, window_size, shift_size)
-    volume, num_windows = _geometry(D, H, W, window_size)
+    g = _grid(D, H, W, ws, ss)
     if x.device.type == "meta":
-        return torch.empty((B * num_windows, volume, C), dtype=x.dtype, device=x.device)
+        return torch.empty(g.windows_shape(B, C), dtype=x.dtype, device=x.device)
     _require_cuda(x, "fused_shift_partition_3d")
-    with _nvtx_range("crumpet.fused_shift_partition_3d"):
-        if torch.is_grad_enabled() and x.requires_grad:
-            return _ShiftPartitionFn.apply(x, window_size, shift_size)
-        out = torch.empty((B * num_windows, volume, C), dtype=x.dtype, device=x.device)
-        _native.require().fused_shift_partition_3d(out, x.contiguous(), *window_size, *shift_size)
-        _prof.count("fused_shift_partition_3d")
-        return out
+    return _run_permute(x, True, g, B, C)
 
 
 def fused_unshift_unpartition_3d(
@@ -252,27 +265,18 @@ def fused_unshift_unpartition_3d(
     """3D window reverse and cyclic shift by ``+shift_size``: back to ``[B, D, H, W, C]``."""
     if windows.ndim != 3:
         raise ValueError("windows must have shape [B * num_windows, window_volume, C]")
-    window_size = _triple("window_size", window_size)
-    shift_size = _triple("shift_size", shift_size)
+    ws = _as_triple("window_size", window_size)
+    ss = _as_triple("shift_size", shift_size)
     _check_dtype(windows.dtype)
-    B, D, H, W, C = int(B), int(D), int(H), int(W), int(C)
-    _validate_shape(D, H, W, window_size, shift_size)
-    volume, num_windows = _geometry(D, H, W, window_size)
-    expected = (B * num_windows, volume, C)
+    B, C = int(B), int(C)
+    g = _grid(D, H, W, ws, ss)
+    expected = g.windows_shape(B, C)
     if tuple(int(v) for v in windows.shape) != expected:
         raise ValueError(f"windows must have shape {expected}")
     if windows.device.type == "meta":
-        return torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
+        return torch.empty((B, *g.dims, C), dtype=windows.dtype, device=windows.device)
     _require_cuda(windows, "fused_unshift_unpartition_3d")
-    with _nvtx_range("crumpet.fused_unshift_unpartition_3d"):
-        if torch.is_grad_enabled() and windows.requires_grad:
-            return _UnshiftUnpartitionFn.apply(windows, B, D, H, W, C, window_size, shift_size)
-        out = torch.empty((B, D, H, W, C), dtype=windows.dtype, device=windows.device)
-        _native.require().fused_unshift_unpartition_3d(
-            out, windows.contiguous(), B, D, H, W, C, *window_size, *shift_size
-        )
-        _prof.count("fused_unshift_unpartition_3d")
-        return out
+    return _run_permute(windows, False, g, B, C)
 
 
 from .fused_attention import (  # noqa: E402
@@ -287,6 +291,27 @@ from .block_fusion import (  # noqa: E402
     patch_merge_norm_3d,
     proj_out_norm_3d,
 )
+
+
+def device_status(clear: bool = False, device: torch.device | int | None = None) -> int:
+    """The device error word of crumpet_b200's kernels on ``device`` (default: the current
+    CUDA device): 0 while healthy; non-zero once a kernel gave up on one of its bounded
+    waits (it then stopped early, so its output is incomplete) or met an out-of-range
+    relative-position index.  ``clear`` resets it.  Reading it waits for the device."""
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        value = int(_native.capi().crumpet_device_status(1 if clear else 0))
+    if value < 0:
+        raise RuntimeError(f"crumpet_b200: cannot read the device error word ({value})")
+    return value
+
+
+def check_device_status(device: torch.device | int | None = None) -> None:
+    """Raise RuntimeError (and clear the word) if :func:`device_status` is non-zero."""
+    value = device_status(clear=True, device=device)
+    if value:
+        raise RuntimeError(
+            f"crumpet_b200 kernel reported device error {value}: a bounded wait expired or "
+            "an input was out of range, so an output is incomplete")
 
 
 def patch_monai_swin_unetr(swin_module=None) -> bool:
@@ -324,6 +349,8 @@ __all__ = [
     "unpatch_monai_swin_unetr",
     "clear_mask_cache",
     "mask_cache_info",
+    "device_status",
+    "check_device_status",
     "window_partition_reference",
     "window_reverse_reference",
     "unfused_shift_partition_3d_reference",

@@ -19,6 +19,7 @@ EXT_PATH = _PKG / "_C.so"
 
 _load_error: Exception | None = None
 ops = None
+_on_load: list = []
 
 
 def _try_load() -> bool:
@@ -31,25 +32,39 @@ def _try_load() -> bool:
         _load_error = None
     except Exception as exc:  # pragma: no cover - exercised only without a build
         _load_error = exc
-    return ops is not None
+        return False
+    for hook in _on_load:
+        hook()
+    return True
 
 
-_try_load()
+def on_load(hook) -> None:
+    """Run ``hook()`` once the libraries are loaded (now, if they already are)."""
+    _on_load.append(hook)
+    if ops is not None:
+        hook()
 
 
 def reload() -> bool:
-    """Load the libraries if they were missing when the package was imported (a build
-    that runs in the same process as the import); True once they are loaded."""
+    """Load the libraries now (for example after a build in the same process); True once
+    they are loaded.  Importing the package maps no native library: the first op call,
+    ``require()``, ``available()`` or ``capi()`` does."""
     return _try_load()
 
 
-def available() -> bool:
+def loaded() -> bool:
+    """Whether the libraries are mapped into this process, without trying to load them."""
     return ops is not None
 
 
+def available() -> bool:
+    return _try_load()
+
+
 def require():
-    """Return ``torch.ops.crumpet_ops`` or raise the reason it is unavailable."""
-    if ops is None:
+    """Return ``torch.ops.crumpet_ops`` (loading it on first use) or raise the reason it
+    is unavailable."""
+    if ops is None and not _try_load():
         raise RuntimeError(
             "crumpet_b200 native kernels are not built or failed to load "
             f"({EXT_PATH}): {_load_error!r}. Run `python -m crumpet_b200._build`."
@@ -82,7 +97,7 @@ def capi() -> ctypes.CDLL:
         ]
         lib.crumpet_fused_swin_attention.restype = i32
         lib.crumpet_swin_window_attention_qkv.argtypes = (
-            [vp, vp, vp, i32, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
+            [vp, vp, vp, i32, i64, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
         lib.crumpet_swin_window_attention_qkv.restype = i32
         lib.crumpet_norm_shift_partition_3d.argtypes = (
             [vp, i32, vp, i32, vp, vp, ctypes.c_float] + [i64] * 11 + [vp])

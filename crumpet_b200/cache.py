@@ -1,11 +1,14 @@
-"""Device-aware LRU cache for shifted-window attention masks.
+"""Per-device LRU of shifted-window attention masks.
 
-Same contract as the reference mask cache (torch-ext/crumpet/cache.py:1-97):
-keys are (D, H, W, window_size, shift_size, dtype, device), at most
-``CRUMPET_MASK_CACHE_SIZE`` entries (default 64) and
-``CRUMPET_MASK_CACHE_MAX_BYTES`` bytes (default 1 GiB) are kept, a value
-larger than the byte cap is returned uncached, and
-``CRUMPET_DISABLE_MASK_CACHE=1`` bypasses the cache.  Not thread-safe.
+The user-visible contract is the reference's mask cache
+(torch-ext/crumpet/cache.py:1-97): an entry is keyed by
+(D, H, W, window_size, shift_size, dtype, device); ``CRUMPET_MASK_CACHE_SIZE``
+(default 64) bounds the number of entries and ``CRUMPET_MASK_CACHE_MAX_BYTES``
+(default 1 GiB) their total size; a mask bigger than the byte bound is handed
+back without being stored; the least recently used entries go first; and
+``CRUMPET_DISABLE_MASK_CACHE=1`` turns caching off.  The limits are read from
+the environment on every insertion, so they can change at run time.  Not
+thread-safe (callers hold the GIL, as every op wrapper does).
 """
 
 from __future__ import annotations
@@ -18,38 +21,67 @@ import torch
 
 MaskKey = tuple[int, int, int, tuple[int, int, int], tuple[int, int, int], torch.dtype, str]
 
-_DEFAULT_ENTRIES = 64
-_DEFAULT_BYTES = 1 << 30
-
-_entries: "OrderedDict[MaskKey, torch.Tensor]" = OrderedDict()
-_total_bytes = 0
+_ENTRIES_VAR, _ENTRIES_DEFAULT = "CRUMPET_MASK_CACHE_SIZE", 64
+_BYTES_VAR, _BYTES_DEFAULT = "CRUMPET_MASK_CACHE_MAX_BYTES", 1 << 30
 
 
-def _env_int(name: str, default: int) -> int:
-    raw = os.environ.get(name)
-    if raw is None:
-        return default
+def _setting(var: str, default: int) -> int:
     try:
-        return int(raw)
-    except ValueError:
+        return int(os.environ[var])
+    except (KeyError, ValueError):
         return default
 
 
-def _limits() -> tuple[int, int]:
-    return (
-        _env_int("CRUMPET_MASK_CACHE_SIZE", _DEFAULT_ENTRIES),
-        _env_int("CRUMPET_MASK_CACHE_MAX_BYTES", _DEFAULT_BYTES),
-    )
+class _MaskLRU:
+    """Masks in least- to most-recently-used order, with their running byte total."""
+
+    def __init__(self) -> None:
+        self.items: "OrderedDict[MaskKey, torch.Tensor]" = OrderedDict()
+        self.nbytes = 0
+
+    @staticmethod
+    def size_of(t: torch.Tensor) -> int:
+        return t.numel() * t.element_size()
+
+    def limits(self) -> tuple[int, int]:
+        return _setting(_ENTRIES_VAR, _ENTRIES_DEFAULT), _setting(_BYTES_VAR, _BYTES_DEFAULT)
+
+    def lookup(self, key: MaskKey) -> torch.Tensor | None:
+        hit = self.items.get(key)
+        if hit is not None:
+            self.items.move_to_end(key)
+        return hit
+
+    def insert(self, key: MaskKey, value: torch.Tensor) -> None:
+        max_entries, max_bytes = self.limits()
+        size = self.size_of(value)
+        if max_entries <= 0 or size > max_bytes:
+            return  # too big to keep: the caller still gets the tensor
+        self.items[key] = value
+        self.nbytes += size
+        while self.items and (len(self.items) > max_entries or self.nbytes > max_bytes):
+            _, evicted = self.items.popitem(last=False)
+            self.nbytes -= self.size_of(evicted)
+
+    def clear(self) -> None:
+        self.items.clear()
+        self.nbytes = 0
+
+    def live(self) -> list[torch.Tensor]:
+        """The tensors held right now (a CUDA graph captured over them keeps these alive)."""
+        return list(self.items.values())
+
+
+_LRU = _MaskLRU()
 
 
 def _device_key(device: torch.device | str) -> str:
     dev = torch.device(device)
-    if dev.type != "cuda":
-        return str(dev)
-    index = dev.index
-    if index is None and torch.cuda.is_available():
-        index = torch.cuda.current_device()
-    return f"cuda:{0 if index is None else index}"
+    if dev.type == "cuda" and dev.index is None:
+        # an index-less CUDA device means the current one
+        index = torch.cuda.current_device() if torch.cuda.is_available() else 0
+        return f"cuda:{index}"
+    return str(dev)
 
 
 def make_mask_key(
@@ -65,46 +97,32 @@ def make_mask_key(
 
 
 def clear_mask_cache() -> None:
-    global _total_bytes
-    _entries.clear()
-    _total_bytes = 0
+    _LRU.clear()
 
 
 def mask_cache_info() -> dict[str, int]:
-    max_entries, max_bytes = _limits()
-    return {
-        "entries": len(_entries),
-        "bytes": _total_bytes,
-        "max_entries": max_entries,
-        "max_bytes": max_bytes,
-    }
+    max_entries, max_bytes = _LRU.limits()
+    return {"entries": len(_LRU.items), "bytes": _LRU.nbytes, "max_entries": max_entries,
+            "max_bytes": max_bytes}
 
 
-def _nbytes(t: torch.Tensor) -> int:
-    return t.numel() * t.element_size()
+def cached_masks() -> list[torch.Tensor]:
+    """Every mask the cache holds at this moment."""
+    return _LRU.live()
 
 
 def get_or_compute_mask(key: MaskKey, compute: Callable[[], torch.Tensor]) -> torch.Tensor:
-    """Return the cached mask for ``key`` or compute, insert and return it.
+    """The mask stored under ``key``; on a miss, ``compute()`` builds it and it is stored
+    (unless it exceeds the byte bound).
 
-    The cache is a convenience LRU, not a lifetime guarantee: callers in hot
-    loops keep their own reference to the returned tensor.
+    An entry can be evicted at any later insertion, so code that reuses a mask across
+    many calls should hold on to the tensor it got back rather than look it up again.
     """
-    global _total_bytes
     if os.environ.get("CRUMPET_DISABLE_MASK_CACHE", "0") == "1":
         return compute()
-    cached = _entries.get(key)
-    if cached is not None:
-        _entries.move_to_end(key)
-        return cached
+    hit = _LRU.lookup(key)
+    if hit is not None:
+        return hit
     value = compute()
-    max_entries, max_bytes = _limits()
-    size = _nbytes(value)
-    if max_entries <= 0 or size > max_bytes:
-        return value
-    _entries[key] = value
-    _total_bytes += size
-    while _entries and (len(_entries) > max_entries or _total_bytes > max_bytes):
-        _, old = _entries.popitem(last=False)
-        _total_bytes -= _nbytes(old)
+    _LRU.insert(key, value)
     return value

@@ -118,6 +118,7 @@ struct KParams {
   const uint16_t* bias;
   const void* table;
   const long long* index;
+  long long table_rows;  // index values outside [0, table_rows) are flagged, not read
   int index_stride;
   int bias_from_table;
   int table_f32;
@@ -558,7 +559,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               vals[u][e] = 0.f;
               if (in) {
                 if (p.bias_from_table) {
-                  idx[u][e] = p.index[(long long)grow * p.index_stride + col];
+                  // -1 marks "not gathered" below, so a stored -1 is mapped to another
+                  // out-of-range value to be flagged like any other
+                  const long long v = p.index[(long long)grow * p.index_stride + col];
+                  idx[u][e] = v == -1 ? -2 : v;
                 } else {
                   vals[u][e] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
                 }
@@ -566,6 +570,20 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             }
           }
           if (p.bias_from_table) {
+            // An index value outside the table would read past it: flag it in the
+            // device error word (bit 2) and take the bias as 0 instead.
+            bool bad = false;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (idx[u][e] != -1 && (idx[u][e] < 0 || idx[u][e] >= p.table_rows)) {
+                  bad = true;
+                  idx[u][e] = -1;
+                }
+              }
+            }
+            if (bad) atomicOr(&g_device_error, 2);
 #pragma unroll
             for (int u = 0; u < kBatch; ++u) {
 #pragma unroll
@@ -832,7 +850,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   // ---- teardown
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_device_error, 1);
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(&g_device_error, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -952,6 +970,8 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
     return set_error(kErrInvalid, "null bias pointer");
   if (a.bias_from_table && a.index_stride < a.N)
     return set_error(kErrInvalid, "relative position index is smaller than N x N");
+  if (a.bias_from_table && a.table_rows < 1)
+    return set_error(kErrInvalid, "relative position bias table has no rows");
   if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(a.out))
     return set_error(kErrInvalid, "q, k, v and out must be 16-byte aligned");
   if ((a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 != 0 ||
@@ -977,6 +997,7 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.table = a.table;
   kp.index = reinterpret_cast<const long long*>(a.index);
   kp.index_stride = int(a.index_stride);
+  kp.table_rows = a.table_rows;
   kp.bias_from_table = a.bias_from_table ? 1 : 0;
   kp.table_f32 = a.table_f32 ? 1 : 0;
   kp.mask = static_cast<const uint16_t*>(a.mask);

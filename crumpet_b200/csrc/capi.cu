@@ -156,7 +156,7 @@ int crumpet_fused_swin_attention(void* out, const void* q, const void* k, const 
 }
 
 int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bias_table,
-                                      int table_f32, const int64_t* rel_index,
+                                      int table_f32, int64_t table_rows, const int64_t* rel_index,
                                       int64_t index_stride, int64_t nw_d, int64_t nw_h,
                                       int64_t nw_w, int64_t ws_d, int64_t ws_h, int64_t ws_w,
                                       int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype,
@@ -177,6 +177,7 @@ int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bi
   a.bias_from_table = true;
   a.table = bias_table;
   a.table_f32 = table_f32 != 0;
+  a.table_rows = table_rows;
   a.index = rel_index;
   a.index_stride = index_stride;
   a.analytic = (ss_d | ss_h | ss_w) != 0;

@@ -102,6 +102,7 @@ struct AttnArgs {
   bool bias_from_table;    // gather bias[h,i,j] = table[index[i*index_stride + j], h]
   const void* table;       // [T, H] fp32 (table_f32) or the element type
   bool table_f32;
+  int64_t table_rows;      // T: index values outside [0, T) are flagged, not read
   const int64_t* index;    // [>=N, index_stride] relative position index, sliced [:N, :N]
   int64_t index_stride;
   const void* mask;        // [mask_windows, N, N] contiguous or nullptr

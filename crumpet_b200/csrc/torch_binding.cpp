@@ -43,6 +43,13 @@ void check_cuda_contig(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
 
+// Every operand of a launch must live on the device the launch is guarded to: a
+// pointer into another GPU's memory would be dereferenced by the kernel as if local.
+void same_device(const at::Tensor& ref, const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.device() == ref.device(), name, " must be on ", ref.device(), " (got ",
+              t.device(), ")");
+}
+
 int64_t num_windows(int64_t D, int64_t H, int64_t W, int64_t wd, int64_t wh, int64_t ww) {
   TORCH_CHECK(wd > 0 && wh > 0 && ww > 0, "window_size values must be positive");
   return (D / wd) * (H / wh) * (W / ww);
@@ -68,6 +75,7 @@ void fused_shift_partition_3d(at::Tensor& output, const at::Tensor& x, int64_t w
   check_cuda_contig(output, "output");
   TORCH_CHECK(x.dim() == 5, "x must have shape [B, D, H, W, C]");
   TORCH_CHECK(output.scalar_type() == x.scalar_type(), "output and x dtypes differ");
+  same_device(x, output, "output");
   const c10::cuda::CUDAGuard guard(x.device());
   if (output.numel() == 0) return;
   const int64_t B = x.size(0), D = x.size(1), H = x.size(2), W = x.size(3), C = x.size(4);
@@ -87,6 +95,7 @@ void fused_unshift_unpartition_3d(at::Tensor& output, const at::Tensor& windows,
   check_cuda_contig(windows, "windows");
   check_cuda_contig(output, "output");
   TORCH_CHECK(output.scalar_type() == windows.scalar_type(), "output and windows dtypes differ");
+  same_device(windows, output, "output");
   const c10::cuda::CUDAGuard guard(windows.device());
   if (output.numel() == 0) return;
   const int64_t nw = num_windows(D, H, W, ws_d, ws_h, ws_w);
@@ -137,11 +146,16 @@ void fused_swin_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor
   TORCH_CHECK(k.scalar_type() == st && v.scalar_type() == st && out.scalar_type() == st &&
                   rel_bias.scalar_type() == st,
               "q, k, v, out and relative_position_bias must share one dtype");
+  same_device(q, k, "k");
+  same_device(q, v, "v");
+  same_device(q, out, "out");
+  same_device(q, rel_bias, "relative_position_bias");
   const c10::cuda::CUDAGuard guard(q.device());
   const void* mask_ptr = nullptr;
   int64_t mask_windows = 0;
   if (mask.has_value() && mask->defined()) {
     check_cuda_contig(*mask, "mask");
+    same_device(q, *mask, "mask");
     TORCH_CHECK(mask->dim() == 3 && mask->size(1) == N && mask->size(2) == N,
                 "mask must have shape [num_windows, N, N]");
     TORCH_CHECK(mask->scalar_type() == st, "mask must have the dtype of q");
@@ -153,6 +167,7 @@ void fused_swin_attention(at::Tensor& out, const at::Tensor& q, const at::Tensor
   const uint8_t* bnd = nullptr;
   if (boundary.has_value() && boundary->defined()) {
     check_cuda_contig(*boundary, "boundary");
+    same_device(q, *boundary, "boundary");
     TORCH_CHECK(boundary->scalar_type() == at::kByte && boundary->numel() == B,
                 "boundary must be a uint8 tensor of B elements");
     bnd = boundary->data_ptr<uint8_t>();
@@ -184,10 +199,13 @@ void swin_window_attention_qkv(at::Tensor& out, const at::Tensor& qkv, const at:
               "relative_position_index must be int64 [>=N, >=N]");
   TORCH_CHECK(num_windows.size() == 3 && window_size.size() == 3 && shift_size.size() == 3,
               "num_windows, window_size and shift_size take three values");
+  same_device(qkv, out, "out");
+  same_device(qkv, table, "relative_position_bias_table");
+  same_device(qkv, index, "relative_position_index");
   const c10::cuda::CUDAGuard guard(qkv.device());
   check_rc(crumpet_swin_window_attention_qkv(
       out.data_ptr(), qkv.data_ptr(), table.data_ptr(), table.scalar_type() == at::kFloat ? 1 : 0,
-      index.data_ptr<int64_t>(), index.size(1), num_windows[0], num_windows[1], num_windows[2],
+      table.size(0), index.data_ptr<int64_t>(), index.size(1), num_windows[0], num_windows[1], num_windows[2],
       window_size[0], window_size[1], window_size[2], shift_size[0], shift_size[1],
       shift_size[2], dtype_code(qkv), B, H, N, Dh, static_cast<float>(scale), cur_stream(qkv)));
 }
@@ -206,6 +224,9 @@ void norm_shift_partition_3d(at::Tensor& output, const at::Tensor& x, const at::
   TORCH_CHECK(weight.scalar_type() == at::kFloat && bias.scalar_type() == at::kFloat &&
                   weight.numel() == C && bias.numel() == C,
               "weight and bias must be float32 tensors of C elements");
+  same_device(x, output, "output");
+  same_device(x, weight, "weight");
+  same_device(x, bias, "bias");
   const c10::cuda::CUDAGuard guard(x.device());
   const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
                                  ws_w);
@@ -226,6 +247,7 @@ void unshift_unpartition_crop_3d(at::Tensor& output, const at::Tensor& windows,
   check_cuda_contig(windows, "windows");
   check_cuda_contig(output, "output");
   TORCH_CHECK(output.scalar_type() == windows.scalar_type(), "output and windows dtypes differ");
+  same_device(windows, output, "output");
   const c10::cuda::CUDAGuard guard(windows.device());
   const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
                                  ws_w);
@@ -236,6 +258,7 @@ void unshift_unpartition_crop_3d(at::Tensor& output, const at::Tensor& windows,
   const void* res = nullptr;
   if (residual.has_value() && residual->defined()) {
     check_cuda_contig(*residual, "residual");
+    same_device(windows, *residual, "residual");
     TORCH_CHECK(residual->scalar_type() == windows.scalar_type(),
                 "residual must have the dtype of windows");
     TORCH_CHECK(residual->numel() == B * D * H * W * C, "residual must have B*D*H*W*C elements");
@@ -263,6 +286,10 @@ void unshift_unpartition_crop_norm_3d(at::Tensor& output, at::Tensor& normed,
   TORCH_CHECK(weight.scalar_type() == at::kFloat && bias.scalar_type() == at::kFloat &&
                   weight.numel() == C && bias.numel() == C,
               "weight and bias must be float32 tensors of C elements");
+  same_device(windows, output, "output");
+  same_device(windows, normed, "normed");
+  same_device(windows, weight, "weight");
+  same_device(windows, bias, "bias");
   const c10::cuda::CUDAGuard guard(windows.device());
   const int64_t nw = num_windows(ceil_to(D, ws_d), ceil_to(H, ws_h), ceil_to(W, ws_w), ws_d, ws_h,
                                  ws_w);
@@ -274,6 +301,7 @@ void unshift_unpartition_crop_norm_3d(at::Tensor& output, at::Tensor& normed,
   const void* res = nullptr;
   if (residual.has_value() && residual->defined()) {
     check_cuda_contig(*residual, "residual");
+    same_device(windows, *residual, "residual");
     TORCH_CHECK(residual->scalar_type() == windows.scalar_type(),
                 "residual must have the dtype of windows");
     TORCH_CHECK(residual->numel() == B * D * H * W * C, "residual must have B*D*H*W*C elements");
@@ -302,6 +330,9 @@ void patch_merge_norm_3d(at::Tensor& output, const at::Tensor& x, const at::Tens
                   output.size(2) == (H + 1) / 2 && output.size(3) == (W + 1) / 2 &&
                   output.size(4) == 8 * C,
               "output must have shape [B, ceil(D/2), ceil(H/2), ceil(W/2), 8C]");
+  same_device(x, output, "output");
+  same_device(x, weight, "weight");
+  same_device(x, bias, "bias");
   const c10::cuda::CUDAGuard guard(x.device());
   if (output.numel() == 0) return;
   int codes[8];
@@ -326,6 +357,8 @@ void proj_out_norm_3d(at::Tensor& output, const at::Tensor& x,
   if (weight.has_value()) {
     check_cuda_contig(*weight, "weight");
     check_cuda_contig(*bias, "bias");
+    same_device(x, *weight, "weight");
+    same_device(x, *bias, "bias");
     TORCH_CHECK(weight->scalar_type() == at::kFloat && bias->scalar_type() == at::kFloat &&
                     weight->numel() == C && bias->numel() == C,
                 "weight and bias must be float32 tensors of C elements");
@@ -335,6 +368,7 @@ void proj_out_norm_3d(at::Tensor& output, const at::Tensor& x,
   TORCH_CHECK(output.dim() == 5 && output.size(0) == B && output.size(1) == D &&
                   output.size(2) == H && output.size(3) == W && output.size(4) == C,
               "output must have shape [B, D, H, W, C]");
+  same_device(x, output, "output");
   const c10::cuda::CUDAGuard guard(x.device());
   if (output.numel() == 0) return;
   check_rc(crumpet_proj_out_norm_3d(output.data_ptr(), dtype_code(output), x.data_ptr(),
@@ -353,9 +387,12 @@ void window_linear(at::Tensor& out, const at::Tensor& x, const at::Tensor& weigh
   TORCH_CHECK(weight.scalar_type() == x.scalar_type() && out.scalar_type() == x.scalar_type(),
               "x, weight and out must share one dtype");
   TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N, "out must be [M, N]");
+  same_device(x, out, "out");
+  same_device(x, weight, "weight");
   const float* b = nullptr;
   if (bias.has_value()) {
     check_cuda_contig(*bias, "bias");
+    same_device(x, *bias, "bias");
     TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N,
                 "bias must be a float32 tensor of N elements");
     b = bias->data_ptr<float>();
@@ -382,6 +419,7 @@ void roi_gather(at::Tensor& out, const at::Tensor& volume, at::IntArrayRef start
   TORCH_CHECK(out.dim() == 5 && out.size(0) == n && out.size(1) == volume.size(0) &&
                   out.size(2) == roi[0] && out.size(3) == roi[1] && out.size(4) == roi[2],
               "out must have shape [n, C, rd, rh, rw]");
+  same_device(volume, out, "out");
   const c10::cuda::CUDAGuard guard(volume.device());
   check_rc(crumpet_roi_gather(out.data_ptr(), dtype_code(out), volume.data_ptr(),
                               dtype_code(volume), volume.size(0), volume.size(1), volume.size(2),
@@ -400,6 +438,7 @@ void roi_accumulate(at::Tensor& acc, const at::Tensor& pred, at::IntArrayRef sta
   TORCH_CHECK(pred.dim() == 5 && pred.size(0) == n && pred.size(1) == acc.size(0) &&
                   pred.size(2) == roi[0] && pred.size(3) == roi[1] && pred.size(4) == roi[2],
               "pred must have shape [n, classes, rd, rh, rw]");
+  same_device(acc, pred, "pred");
   const c10::cuda::CUDAGuard guard(acc.device());
   check_rc(crumpet_roi_accumulate(acc.data_ptr<float>(), pred.data_ptr(), dtype_code(pred),
                                   acc.size(0), acc.size(1), acc.size(2), acc.size(3), s.data(), n,
@@ -415,6 +454,7 @@ void roi_argmax_impl(uint8_t* labels, float* logits, const at::Tensor& acc,
   const at::Tensor* counts[3] = {&count_d, &count_h, &count_w};
   for (int a = 0; a < 3; ++a) {
     check_cuda_contig(*counts[a], "count");
+    same_device(acc, *counts[a], "count");
     TORCH_CHECK(counts[a]->scalar_type() == at::kFloat && counts[a]->numel() == acc.size(1 + a),
                 "counts must be float32 vectors of D, H and W elements");
   }
@@ -427,6 +467,8 @@ void roi_argmax_impl(uint8_t* labels, float* logits, const at::Tensor& acc,
 void roi_argmax(at::Tensor& labels, const at::Tensor& acc, const at::Tensor& count_d,
                 const at::Tensor& count_h, const at::Tensor& count_w) {
   check_cuda_contig(labels, "labels");
+  check_cuda_contig(acc, "acc");
+  same_device(acc, labels, "labels");
   TORCH_CHECK(labels.scalar_type() == at::kByte && labels.numel() == acc.numel() / acc.size(0),
               "labels must be a uint8 [D, H, W] tensor");
   roi_argmax_impl(labels.data_ptr<uint8_t>(), nullptr, acc, count_d, count_h, count_w);
@@ -435,6 +477,8 @@ void roi_argmax(at::Tensor& labels, const at::Tensor& acc, const at::Tensor& cou
 void roi_normalize(at::Tensor& logits, const at::Tensor& acc, const at::Tensor& count_d,
                    const at::Tensor& count_h, const at::Tensor& count_w) {
   check_cuda_contig(logits, "logits");
+  check_cuda_contig(acc, "acc");
+  same_device(acc, logits, "logits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.sizes() == acc.sizes(),
               "logits must be a float32 tensor shaped like acc");
   roi_argmax_impl(nullptr, logits.data_ptr<float>(), acc, count_d, count_h, count_w);

@@ -42,6 +42,7 @@ import torch
 import torch.distributed as dist
 
 from . import _ops
+from . import cache as _mask_cache
 from . import profiling as _prof
 
 
@@ -173,8 +174,12 @@ class SlidingWindowInferer:
             graph = torch.cuda.CUDAGraph()
             with _prof.suspended() as launches, torch.cuda.graph(graph):
                 static_out = self._forward(static_in, cache=False)
-            self._graphs[key] = (graph, static_in, static_out, launches.delta)
-        return self._graphs[key]
+            # The replays read every tensor the capture read, by address.  Masks taken
+            # from the mask cache (the dense-mask and unpatched paths) could be evicted
+            # or cleared later and their memory reused, so the graph entry holds them.
+            held = _mask_cache.cached_masks()
+            self._graphs[key] = (graph, static_in, static_out, launches.delta, held)
+        return self._graphs[key][:4]
 
     @torch.no_grad()
     def accumulate(self, volume: torch.Tensor) -> tuple[torch.Tensor, int]:
@@ -206,8 +211,25 @@ class SlidingWindowInferer:
             done += len(batch)
         return acc, done
 
+    def _check_kernels(self, device: torch.device) -> None:
+        """Raise when a crumpet_b200 kernel gave up on a bounded wait while this volume ran
+        (its output is then incomplete).  With several ranks every rank learns of a
+        failure on any of them through one small all-reduce, so all of them raise
+        together instead of leaving the others waiting in the next collective."""
+        bad = device_error(device)
+        if self.world > 1:
+            flag = torch.tensor([bad], dtype=torch.int32, device=device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.group)
+            bad = int(flag.item())
+        if bad:
+            raise RuntimeError(
+                f"crumpet_b200 kernel reported device error {bad} during sliding-window "
+                "inference (a bounded wait expired or an input was out of range); the "
+                "accumulated predictions are incomplete")
+
     def _reduced(self, volume: torch.Tensor) -> torch.Tensor | None:
         acc, _ = self.accumulate(volume)
+        self._check_kernels(volume.device)
         if self.world > 1:
             dist.reduce(acc, dst=0, op=dist.ReduceOp.SUM, group=self.group)
             if self.rank != 0:
@@ -247,6 +269,16 @@ class SlidingWindowInferer:
         _prof.count("roi_argmax")
         _prof.kernel_end(token)
         return labels
+
+
+def device_error(device: torch.device) -> int:
+    """The crumpet_b200 device error word for CUDA work (0 = healthy), cleared after the
+    read; 0 for CPU devices.  Reading it waits for the device."""
+    if device.type != "cuda":
+        return 0
+    from . import device_status
+
+    return device_status(clear=True)
 
 
 def _accumulate_bytes(pred: torch.Tensor, batch, roi) -> int:

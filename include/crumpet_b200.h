@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define CRUMPET_ABI_VERSION 1
+#define CRUMPET_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define CRUMPET_API __attribute__((visibility("default")))
@@ -133,9 +133,12 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
  * between its qkv and proj Linears.
  *   qkv   [B, N, 3, H, head_dim]   (q | k | v along dim 2; B = batch * nW)
  *   out   [B, N, H * head_dim]     (heads interleaved per token: ready for proj)
- *   bias_table [T, H]              fp32 when table_f32 != 0, else dtype
+ *   bias_table [T, H]              fp32 when table_f32 != 0, else dtype; T = table_rows
  *   rel_index  [>=N, index_stride] int64; bias[h,i,j] = table[rel_index[i,j], h]
- *              for i, j < N (MONAI slices the configured window's index [:N, :N])
+ *              for i, j < N (MONAI slices the configured window's index [:N, :N]).
+ *              An index value outside [0, T) is not read: its bias is taken as 0 and
+ *              the device error word (crumpet_device_status) gets bit 2 (value 2),
+ *              where the eager table[index] would raise an indexing error.
  *   nw_*  windows per axis of one batch entry (window b is b % (nw_d*nw_h*nw_w))
  *   ws_*  window size (ws_d*ws_h*ws_w == N); ss_* cyclic shift (all 0: no mask)
  * The mask equals crumpet_compute_attn_mask_3d's on the padded grid; masked
@@ -147,7 +150,8 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
  * fused_swin_attention.
  */
 CRUMPET_API int crumpet_swin_window_attention_qkv(
-    void* out, const void* qkv, const void* bias_table, int table_f32, const int64_t* rel_index,
+    void* out, const void* qkv, const void* bias_table, int table_f32, int64_t table_rows,
+    const int64_t* rel_index,
     int64_t index_stride, int64_t nw_d, int64_t nw_h, int64_t nw_w, int64_t ws_d, int64_t ws_h,
     int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype, int64_t B, int64_t H,
     int64_t N, int64_t head_dim, float scale, void* stream);
@@ -303,8 +307,9 @@ CRUMPET_API int crumpet_roi_argmax(uint8_t* labels, float* logits, const float* 
 
 /*
  * Device error word: non-zero once a kernel of this library gave up on a
- * bounded wait (it then drained its work, freed its tensor memory and
- * returned without completing its output).  Reading it synchronises with the
+ * bounded wait (bit 1: it then drained its work, freed its tensor memory and
+ * returned without completing its output) or met a relative-position index
+ * outside its table (bit 2).  Reading it synchronises with the
  * device; `clear` != 0 resets it.  Returns the word (0 = healthy) or a negative
  * value / CRUMPET_ERR_CUDA when it cannot be read.  No reference counterpart:
  * the reference kernels contain no waits.

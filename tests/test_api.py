@@ -29,7 +29,7 @@ def test_capi_library_exports_every_declared_symbol():
     assert len(names) >= 9
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.crumpet_abi_version() == 1
+    assert lib.crumpet_abi_version() == 2
 
 
 def test_capi_rejects_bad_arguments_without_touching_the_device():
@@ -166,11 +166,11 @@ def test_packed_attention_capi_validation():
     lib = _ops.capi()
     null = ctypes.c_void_p(0)
     # analytic geometry that does not multiply out to N
-    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, null, 343, 2, 2, 2, 7, 7, 6, 3, 3,
+    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, 2197, null, 343, 2, 2, 2, 7, 7, 6, 3, 3,
                                                3, 1, 8, 3, 343, 16, 0.25, null)
     assert rc == 1 and _ops.last_error()
     # null pointers
-    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, null, 343, 2, 2, 2, 7, 7, 7, 3, 3,
+    rc = lib.crumpet_swin_window_attention_qkv(null, null, null, 1, 2197, null, 343, 2, 2, 2, 7, 7, 7, 3, 3,
                                                3, 1, 8, 3, 343, 16, 0.25, null)
     assert rc == 1
 

@@ -81,7 +81,7 @@ def test_packed_attention_capi_fp16_table(cuda_device):
     B, N, _, H, D = qkv.shape
     out = torch.empty((B, N, H * D), dtype=qkv.dtype, device=cuda_device)
     rc = _ops.capi().crumpet_swin_window_attention_qkv(
-        ptr(out), ptr(qkv), ptr(table), 0, ptr(index), index.shape[1], *nw, *ws, *ss,
+        ptr(out), ptr(qkv), ptr(table), 0, table.shape[0], ptr(index), index.shape[1], *nw, *ws, *ss,
         DTYPE_CODE[qkv.dtype], B, H, N, D, 0.25, stream_ptr())
     assert rc == 0, _ops.last_error()
     torch.cuda.synchronize()
@@ -138,3 +138,26 @@ def test_cfg3_full_size_sampled_windows(cuda_device):
     assert np.abs(dense[sel].float().cpu().numpy() - want).max() <= 2e-3
     got = packed[sel].reshape(len(sel), N, H, D).permute(0, 2, 1, 3)
     assert np.abs(got.float().cpu().numpy() - want).max() <= 2e-3
+
+
+def test_out_of_range_index_is_flagged_not_read(cuda_device):
+    """A relative-position index value outside the bias table is not read: its bias is
+    taken as 0, the device error word gets bit 2, and check_device_status raises."""
+    import crumpet_b200 as crumpet
+
+    (qkv, table, index, nw, ws, ss), _ = make_case(CASES[0], cuda_device)
+    bad = index.clone()
+    bad[5, 7] = table.shape[0]
+    bad[100, 3] = -1
+    bad[200, 300] = -12345
+    assert crumpet.device_status(clear=True) == 0
+    out = swin_window_attention_qkv(qkv, table, bad, nw, ws, ss, 0.25)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert crumpet.device_status() == 2
+    with pytest.raises(RuntimeError, match="device error 2"):
+        crumpet.check_device_status()
+    assert crumpet.device_status() == 0
+    # the same call with the valid index leaves the word clear
+    swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
+    crumpet.check_device_status()

@@ -70,3 +70,36 @@ def test_capture_suspends_timers_and_hands_back_the_launch_counts():
         profiling.count_replay(cap.delta)
         profiling.count_replay(cap.delta)
         assert profiling.counters["window_linear"] == before.get("window_linear", 0) + 12
+
+
+def test_importing_the_package_maps_no_native_library():
+    # the CPU reference arm imports crumpet_b200's pure-torch modules; loading the
+    # kernels' libraries there would put this repository's native code in that arm
+    import subprocess
+    import sys
+
+    code = ("import crumpet_b200, crumpet_b200.swin_unetr, crumpet_b200.inferer, "
+            "crumpet_b200.monai_patch\n"
+            "from crumpet_b200 import _ops\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "assert _ops.ops is None and not _ops.loaded()\n"
+            "assert 'libcrumpet_b200' not in maps and '_C.so' not in maps\n")
+    subprocess.run([sys.executable, "-c", code], check=True, cwd=str(bench.ROOT))
+
+
+def test_reference_arm_reports_its_sample_and_loads_nothing_native():
+    import json
+    import subprocess
+    import sys
+
+    proc = subprocess.run(
+        [sys.executable, str(bench.ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+         "--warmup", "0", "--roi", "64", "--volume", "128", "128", "64"],
+        check=True, capture_output=True, text=True, timeout=600)
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["native_libraries_loaded"] is False
+    assert line["sample"]["rois_per_step"] == 1
+    assert line["config"]["rois_per_step"] == 9
+    assert "execution" not in line["config"]
+    assert line["e2e"]["value"] == line["value"]

@@ -191,3 +191,37 @@ def test_network_fp32_without_autocast(cuda_device):
     print(f"fp32 agreement {agree:.5f} max logit diff {diff:.2e}")
     assert agree >= 0.999, agree
     assert diff < 5e-3, diff
+
+
+def test_cfg5_full_volume_patched_vs_eager(cuda_device):
+    """BASELINE config 5 itself, as bench.py times it: the 1x1x512x512x224 synthetic
+    volume, 96^3 ROIs at 0.5 overlap (400 ROIs), batches of 8, fp16 autocast, the
+    patched network replayed from CUDA graphs -- against the unpatched eager network
+    on the same GPU.  North-star criterion: segmentation arg-max agreement >= 99.9 %."""
+    from crumpet_b200.inferer import roi_grid, synthetic_volume
+
+    torch.manual_seed(0)
+    model = swin_unetr.SwinUNETR(in_channels=1, out_channels=14, feature_size=48,
+                                 depths=(2, 2, 2, 2), num_heads=(3, 6, 12, 24))
+    model = model.to(cuda_device).eval()
+    vol = synthetic_volume((1, 1, 512, 512, 224)).to(cuda_device)
+    assert len(roi_grid((512, 512, 224), (96, 96, 96), 0.5)) == 400
+    patched_inf = SlidingWindowInferer(model, (96, 96, 96), 8, 0.5, 14, torch.float16,
+                                       cuda_graphs=True)
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        seg_p = patched_inf.segment(vol)
+        logit_p = patched_inf.logits(vol)
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+        patched_inf.reset_graphs()
+    eager_inf = SlidingWindowInferer(model, (96, 96, 96), 8, 0.5, 14, torch.float16)
+    logit_e = eager_inf.logits(vol)
+    lab_p = logit_p[0].argmax(0).to(torch.uint8)
+    lab_e = logit_e[0].argmax(0).to(torch.uint8)
+    assert torch.equal(seg_p, lab_p)  # the arg-max kernel agrees with torch.argmax
+    agree = (lab_p == lab_e).float().mean().item()
+    max_diff = (logit_p - logit_e).abs().max().item()
+    print(f"cfg5 full volume: arg-max agreement {agree:.6f}, max |logit diff| {max_diff:.4e}")
+    assert agree >= 0.999, (agree, max_diff)
+    assert max_diff < 5e-2, (agree, max_diff)
