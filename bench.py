@@ -156,6 +156,148 @@ def visible_gpu_ids(world: int) -> list[int]:
     return list(range(world))
 
 
+class ReferenceGPUKernels:
+    """The reference's own GPU kernels, built from its sources by
+    ``baseline/build_reference.py`` into ``baseline/_ref`` (absent -> not timed):
+    its CUDA extension under the op namespace ``crumpet_ref_ops`` and its Triton
+    attention kernel as an sm_100 cubin, launched through the CUDA driver API with
+    the parameter layout Triton's own launcher uses (every non-constexpr argument in
+    order, then two null scratch pointers).  Used only for side-by-side timing."""
+
+    DIR = ROOT / "baseline" / "_ref"
+
+    def __init__(self):
+        import ctypes
+
+        import torch
+
+        torch.ops.load_library(str(self.DIR / "crumpet_ref_ops.so"))
+        self.ops = torch.ops.crumpet_ref_ops
+        self.cuda = ctypes.CDLL("libcuda.so.1")
+        vp, ui = ctypes.c_void_p, ctypes.c_uint
+        self.cuda.cuModuleLoadData.argtypes = [ctypes.POINTER(vp), vp]
+        self.cuda.cuModuleGetFunction.argtypes = [ctypes.POINTER(vp), vp, ctypes.c_char_p]
+        self.cuda.cuLaunchKernel.argtypes = [vp, ui, ui, ui, ui, ui, ui, ui, vp, vp, vp]
+        for fn in ("cuModuleLoadData", "cuModuleGetFunction", "cuLaunchKernel"):
+            getattr(self.cuda, fn).restype = ctypes.c_int
+        self.kernels = {}
+        for meta_path in sorted(self.DIR.glob("ref_swin_attention_n*.json")):
+            meta = json.loads(meta_path.read_text())
+            image = meta_path.with_suffix(".cubin").read_bytes()
+            module, func = ctypes.c_void_p(), ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(image, len(image))
+            self._check(self.cuda.cuModuleLoadData(ctypes.byref(module), buf), "cuModuleLoadData")
+            self._check(self.cuda.cuModuleGetFunction(ctypes.byref(func), module,
+                                                      meta["kernel"].encode()), "cuModuleGetFunction")
+            self.kernels[meta["constants"]["N"]] = (func, meta, module, buf)
+
+    @classmethod
+    def load(cls):
+        if not (cls.DIR / "crumpet_ref_ops.so").exists():
+            return None
+        return cls()
+
+    @staticmethod
+    def _check(rc, what):
+        if rc != 0:
+            raise RuntimeError(f"{what} failed with CUresult {rc}")
+
+    def attention(self, out, q, k, v, bias, mask, boundary, scale):
+        """The reference launcher's call (fused_attention.py:149-226) for float16
+        [B, H, N, 16] contiguous q/k/v/out, bias [H, N, N], mask [B or 1, N, N] and
+        uint8 boundary [B], each checked against the cubin's specialisation first."""
+        import ctypes
+
+        import torch
+
+        B, H, N, D = q.shape
+        func, meta, _, _ = self.kernels[N]
+        c = meta["constants"]
+        tensors = (q, k, v, out, bias, mask, boundary)
+        if (D != c["D"] or any(t.dtype != torch.float16 for t in (q, k, v, out, bias, mask))
+                or boundary.dtype != torch.uint8 or not all(t.is_contiguous() for t in tensors)
+                or tuple(bias.shape) != (H, N, N) or mask.shape[1:] != (N, N)
+                or mask.shape[0] not in (1, B) or boundary.numel() != B
+                or any(t.data_ptr() % 16 for t in tensors) or any(t.shape != q.shape for t in (k, v, out))
+                or any(st % 16 for st in q.stride()[:3])):
+            raise ValueError("arguments outside the compiled reference kernel's specialisation")
+        mstride = (0 if mask.shape[0] == 1 else mask.stride(0), mask.stride(1))
+        vals = {"Q": q, "K": k, "V": v, "BIAS": bias, "MASK": mask, "BOUNDARY": boundary,
+                "OUT": out, "SCALE": float(scale),
+                "stride_qb": q.stride(0), "stride_qh": q.stride(1), "stride_qn": q.stride(2),
+                "stride_kb": k.stride(0), "stride_kh": k.stride(1), "stride_kn": k.stride(2),
+                "stride_vb": v.stride(0), "stride_vh": v.stride(1), "stride_vn": v.stride(2),
+                "stride_bh": bias.stride(0), "stride_bm": bias.stride(1),
+                "stride_mb": mstride[0], "stride_mm": mstride[1],
+                "stride_ob": out.stride(0), "stride_oh": out.stride(1), "stride_on": out.stride(2)}
+        store = []
+        for arg in meta["runtime_args"]:
+            val = vals[arg["name"]]
+            if arg["type"].startswith("*"):
+                store.append(ctypes.c_uint64(val.data_ptr()))
+            elif arg["type"] == "fp32":
+                store.append(ctypes.c_float(val))
+            else:
+                store.append(ctypes.c_int32(int(val)))
+        store += [ctypes.c_uint64(0)] * meta["trailing_null_pointers"]
+        params = (ctypes.c_void_p * len(store))(*[ctypes.addressof(x) for x in store])
+        grid = (-(-N // c["BLOCK_M"]), H, B)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
+        self._check(self.cuda.cuLaunchKernel(func, *grid, meta["threads"], 1, 1,
+                                             meta["shared_bytes"], stream, params, None),
+                    "cuLaunchKernel")
+
+
+def attention_stages(device, ref, timed) -> list:
+    """The window attention of each Swin stage of one 8-ROI sliding-window batch (the
+    bench's workload), this repository's packed entry (what the patched network runs)
+    against the reference's Triton kernel on the same windows: exps, times, ratio."""
+    import torch
+
+    from crumpet_b200.fused_attention import swin_window_attention_qkv
+
+    rows = []
+    # (padded edge, heads, window, shift): 48^3 -> 49, 24^3 -> 28, 12^3 -> 14, 6^3
+    for edge, H, w, sh in ((49, 3, 7, 3), (28, 6, 7, 3), (14, 12, 7, 3), (6, 24, 6, 0)):
+        g = torch.Generator(device=device).manual_seed(edge)
+        nw = (edge // w,) * 3
+        B = 8 * nw[0] ** 3
+        N = w ** 3
+        qkv = (torch.randn((B, N, 3, H, 16), device=device, generator=g) * 0.5).half()
+        table = torch.randn((13 ** 3, H), device=device, generator=g) * 0.02
+        coords = torch.stack(torch.meshgrid(*(torch.arange(7),) * 3, indexing="ij")).flatten(1)
+        rel = (coords[:, :, None] - coords[:, None, :]) + 6
+        index = (rel[0] * 169 + rel[1] * 13 + rel[2]).to(device)
+        ws, ss = (w,) * 3, (sh,) * 3
+        ms = timed(lambda: swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25),
+                   iters=10)
+        row = {"stage_windows": f"{edge}^3 padded, {B} windows x {H} heads, N={N}",
+               "exps": B * H * N * N, "ms": ms,
+               "sfu_frac": B * H * N * N / ms / 1e6 / (16 * 148 * 1965e-3)}
+        if ref is not None and N in ref.kernels:
+            q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).contiguous() for i in range(3))
+            bias = table[index[:N, :N].reshape(-1)].reshape(N, N, H).permute(2, 0, 1)
+            bias = bias.contiguous().half()
+            if sh:
+                import crumpet_b200 as crumpet
+
+                mask = crumpet.compute_attn_mask_3d(edge, edge, edge, ws, ss, torch.float16, device)
+                flags = (mask.reshape(mask.shape[0], -1).abs().amax(1) > 0).to(torch.uint8)
+                mask = mask.repeat(8, 1, 1)  # the reference launcher wants B masks (or one)
+                bnd = flags.repeat(8)
+            else:  # the launcher's no-mask case: one zero mask, every window interior
+                mask = torch.zeros((1, N, N), dtype=torch.float16, device=device)
+                bnd = torch.zeros((B,), dtype=torch.uint8, device=device)
+            out_r = torch.empty_like(q)
+            ms_r = timed(lambda: ref.attention(out_r, q, k, v, bias, mask, bnd, 0.25), iters=10)
+            ours = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
+            ours = ours.reshape(B, N, H, 16).permute(0, 2, 1, 3)
+            row.update({"reference_triton_ms": ms_r, "speedup_vs_reference": ms_r / ms,
+                        "max_abs_diff": float((out_r.float() - ours.float()).abs().max())})
+        rows.append(row)
+    return rows
+
+
 def time_kernels(device, peaks) -> dict:
     """Stand-alone kernel timings at the BASELINE stage-0 sizes (configs 2 and 3)."""
     import torch
@@ -189,6 +331,23 @@ def time_kernels(device, peaks) -> dict:
 
     hbm = peaks["hbm_gbs"]
     res = {}
+    ref = ref_error = None
+    try:
+        ref = ReferenceGPUKernels.load()
+    except Exception as exc:  # reported in the line, never fatal
+        ref_error = repr(exc)
+
+    def beside(name, ref_fn, agreement):
+        """Time the reference's own kernel on the same call as res[name] and record how
+        its output compares with this repository's."""
+        if ref is None:
+            return
+        ms_r = timed(ref_fn, iters=10)
+        d = res[name]
+        d["reference"] = {"ms": ms_r, "gbs": d["bytes"] / ms_r / 1e6,
+                          "frac_hbm": d["bytes"] / ms_r / 1e6 / hbm,
+                          "speedup_vs_reference": ms_r / d["ms"], "outputs": agreement()}
+
     g = torch.Generator(device=device).manual_seed(2)
     x = torch.randn((1, 98, 98, 98, 48), device=device, generator=g).half()
     ws, ss = (7, 7, 7), (3, 3, 3)
@@ -198,10 +357,22 @@ def time_kernels(device, peaks) -> dict:
     res["fused_shift_partition_3d"] = {"config": "[1,98,98,98,48] fp16 ws7 ss3", "ms": ms,
                                        "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                                        "frac_hbm": nbytes / ms / 1e6 / hbm}
+    if ref is not None:
+        win_r = torch.empty_like(win)
+        beside("fused_shift_partition_3d",
+               lambda: ref.ops.fused_shift_partition_3d(win_r, x, *ws, *ss),
+               lambda: "bit-exact" if torch.equal(win_r, win) else "DIFFERENT")
+        del win_r
     ms = timed(lambda: crumpet.fused_unshift_unpartition_3d(win, 1, 98, 98, 98, 48, ws, ss))
     res["fused_unshift_unpartition_3d"] = {"config": "[2744,343,48] fp16 ws7 ss3", "ms": ms,
                                            "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                                            "frac_hbm": nbytes / ms / 1e6 / hbm}
+    if ref is not None:
+        x_r = torch.empty_like(x)
+        beside("fused_unshift_unpartition_3d",
+               lambda: ref.ops.fused_unshift_unpartition_3d(x_r, win, 1, 98, 98, 98, 48, *ws, *ss),
+               lambda: "bit-exact" if torch.equal(x_r, x) else "DIFFERENT")
+        del x_r
     mask = torch.empty((2744, 343, 343), dtype=torch.float16, device=device)
     ops = crumpet._ops.require()
     ms = timed(lambda: ops.compute_attn_mask_3d(mask, 98, 98, 98, *ws, *ss))
@@ -209,6 +380,12 @@ def time_kernels(device, peaks) -> dict:
     res["compute_attn_mask_3d"] = {"config": "[2744,343,343] fp16 (write-only)", "ms": ms,
                                    "bytes": mbytes, "gbs": mbytes / ms / 1e6,
                                    "frac_hbm": mbytes / ms / 1e6 / hbm}
+    if ref is not None:
+        mask_r = torch.empty_like(mask)
+        beside("compute_attn_mask_3d",
+               lambda: ref.ops.compute_attn_mask_3d(mask_r, 98, 98, 98, *ws, *ss),
+               lambda: "bit-exact" if torch.equal(mask_r, mask) else "DIFFERENT")
+        del mask_r
     B, H, N = 2744, 3, 343
     w_qkv = torch.randn((3 * 48, 48), device=device, generator=g) * 0.02
     qkv = torch.nn.functional.linear(win.float(), w_qkv).half()
@@ -229,6 +406,16 @@ def time_kernels(device, peaks) -> dict:
                                    "tflops": flops / ms / 1e9,
                                    "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
                                    "gexp_s": B * H * N * N / ms / 1e6}
+    attn_ours = crumpet.fused_swin_attention(q, k, v, bias, mask, bnd)
+    if ref is not None:
+        out_r = torch.empty_like(q)
+        beside("fused_swin_attention",
+               lambda: ref.attention(out_r, q, k, v, bias, mask, bnd, 0.25),
+               lambda: {"max_abs_diff": float((out_r.float() - attn_ours.float()).abs().max())})
+        res["fused_swin_attention"]["reference"]["kernel"] = (
+            "reference Triton _fused_swin_attention_kernel, AOT-compiled for sm_100 "
+            "(BLOCK_M 64, BLOCK_N 32, 4 warps, 3 stages)")
+        del out_r
     # the patched-network path: packed qkv, in-kernel bias gather, on-chip mask
     from crumpet_b200.fused_attention import swin_window_attention_qkv
 
@@ -241,7 +428,17 @@ def time_kernels(device, peaks) -> dict:
                                         "frac_hbm": pbytes / ms / 1e6 / hbm,
                                         "tflops": flops / ms / 1e9,
                                         "frac_tensor": flops / ms / 1e9 / peaks["bf16_tflops"],
-                                        "gexp_s": B * H * N * N / ms / 1e6}
+                                        "gexp_s": B * H * N * N / ms / 1e6,
+                                        "sfu_frac": B * H * N * N / ms / 1e6 / (16 * 148 * 1965e-3)}
+    if ref is not None:
+        res["swin_window_attention_qkv"]["speedup_vs_reference_triton"] = (
+            res["fused_swin_attention"]["reference"]["ms"] / ms)
+        del attn_ours
+        res["attention_by_stage"] = attention_stages(device, ref, timed)
+    elif ref_error is not None:
+        res["reference_unavailable"] = ref_error
+    else:
+        res["reference_unavailable"] = "baseline/_ref not built (python baseline/build_reference.py)"
     # the fused block glue at the first stage of an 8-ROI sliding-window batch:
     # [8,48,48,48,48] fp16 -> LayerNorm + pad to 49^3 + roll + partition -> fp16 windows,
     # and windows -> unpartition + roll back + crop + residual add

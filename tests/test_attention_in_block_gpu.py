@@ -91,7 +91,7 @@ def test_packed_attention_inside_stage(cuda_device, monkeypatch):
         shifts.append(tuple(ss))
         B, N, _, H, hd = qkv.shape
         assert qkv.dtype == torch.float16 and (B, N, H, hd) == (64, 343, 3, 16)
-        bias = OA.gather_bias(table.float().cpu().numpy(), index.cpu().numpy(), N)
+        bias = OA.gather_bias(table.detach().float().cpu().numpy(), index.cpu().numpy(), N)
         bias = torch.from_numpy(bias).half().float().numpy()  # rounded as the reference does
         q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).float().cpu().numpy() for i in range(3))
         mask = None
