@@ -26,8 +26,8 @@ INCLUDE = REPO / "include"
 LIB = PKG / "libcrumpet_b200.so"
 EXT = PKG / "_C.so"
 
-CUDA_SOURCES = ["capi.cu", "partition.cu", "mask.cu", "attention.cu", "norm_partition.cu", "sliding_window.cu",
-                "proj_norm.cu", "linear.cu"]
+CUDA_SOURCES = ["capi.cu", "partition.cu", "mask.cu", "attention.cu", "attention_simt.cu",
+                "norm_partition.cu", "sliding_window.cu", "proj_norm.cu", "linear.cu"]
 CUDA_HEADERS = ["common.cuh", "sm100.cuh", "kernels.h"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

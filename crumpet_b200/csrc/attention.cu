@@ -955,16 +955,19 @@ std::atomic<int> g_test_stall{0};
 int set_attention_test_stall(int enable) { return g_test_stall.exchange(enable ? 1 : 0); }
 
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
-  if (a.dtype != kF16 && a.dtype != kBF16)
-    return set_error(kErrUnsupported, "fused_swin_attention supports float16 and bfloat16");
-  if (a.head_dim != 16 && a.head_dim != 32)
-    return set_error(kErrUnsupported, "fused_swin_attention requires head_dim 16 or 32");
-  if (a.N < 1 || a.N > 384) return set_error(kErrUnsupported, "fused_swin_attention supports 1 <= N <= 384");
+  if (a.dtype != kF16 && a.dtype != kBF16 && a.dtype != kF32)
+    return set_error(kErrUnsupported,
+                     "fused_swin_attention supports float32, float16 and bfloat16");
+  if (!simt_attention_head_dim(a.head_dim))
+    return set_error(kErrUnsupported,
+                     "fused_swin_attention requires a power-of-two head_dim between 16 and 256");
+  if (a.N < 1) return set_error(kErrUnsupported, "fused_swin_attention requires N >= 1");
   if (a.B < 0 || a.H < 1) return set_error(kErrInvalid, "B must be >= 0 and H >= 1");
   if (!(a.scale > 0.f) || !(a.scale < 1e30f))
     return set_error(kErrUnsupported, "fused_swin_attention requires a finite scale > 0");
   if (a.B == 0) return kOk;
-  if (a.B > 0x7fffffff || a.H > 0xffff) return set_error(kErrInvalid, "B or H too large");
+  if (a.B > 0x7fffffff || a.H > 0xffff || a.N > 0xffffff)
+    return set_error(kErrInvalid, "B, H or N too large");
   if (!a.q || !a.k || !a.v || !a.out) return set_error(kErrInvalid, "null tensor pointer");
   if (a.bias_from_table ? (!a.table || !a.index) : !a.bias)
     return set_error(kErrInvalid, "null bias pointer");
@@ -972,11 +975,6 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
     return set_error(kErrInvalid, "relative position index is smaller than N x N");
   if (a.bias_from_table && a.table_rows < 1)
     return set_error(kErrInvalid, "relative position bias table has no rows");
-  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(a.out))
-    return set_error(kErrInvalid, "q, k, v and out must be 16-byte aligned");
-  if ((a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 != 0 ||
-      (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 != 0)
-    return set_error(kErrInvalid, "q/k/v/out strides must be multiples of 8 elements");
   if (a.mask && a.mask_windows < 1) return set_error(kErrInvalid, "mask_windows must be >= 1");
   if (a.analytic) {
     if (a.mask) return set_error(kErrInvalid, "analytic and dense masks are exclusive");
@@ -986,6 +984,15 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
       if (a.shift[i] < 0 || a.shift[i] >= a.win[i])
         return set_error(kErrInvalid, "analytic mask shift must satisfy 0 <= shift < window");
   }
+  // The tensor-core kernel: fp16 / bf16, head_dim 16 or 32, N <= 384, q/k/v/out on
+  // 16-byte boundaries with 16-byte row strides (TMA); everything else runs the
+  // fp32 SIMT kernel (attention_simt.cu).
+  const bool tensor_path =
+      a.dtype != kF32 && (a.head_dim == 16 || a.head_dim == 32) && a.N <= 384 &&
+      aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
+      (a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 == 0 &&
+      (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 == 0;
+  if (!tensor_path) return launch_window_attention_simt(a, stream);
 
   CUtensorMap tq, tk, tv;
   if (int e = make_qkv_map(&tq, a.q, a)) return e;

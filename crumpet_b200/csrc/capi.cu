@@ -164,9 +164,10 @@ int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bi
                                       float scale, void* stream) {
   AttnArgs a{};
   const int64_t hd = H * head_dim;
+  const int64_t esize = dtype == kF32 ? 4 : 2;
   a.q = qkv;
-  a.k = static_cast<const uint16_t*>(qkv) + hd;
-  a.v = static_cast<const uint16_t*>(qkv) + 2 * hd;
+  a.k = static_cast<const char*>(qkv) + hd * esize;
+  a.v = static_cast<const char*>(qkv) + 2 * hd * esize;
   a.qkv_stride_n = 3 * hd;
   a.qkv_stride_h = head_dim;
   a.qkv_stride_b = N * 3 * hd;

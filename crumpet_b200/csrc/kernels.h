@@ -114,10 +114,16 @@ struct AttnArgs {
   int64_t shift[3];        // cyclic shift; all zero means no mask
   int64_t B, H, N, head_dim;
   float scale;
-  int dtype;               // kF16 or kBF16
+  int dtype;               // kF32, kF16 or kBF16
 };
 
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream);
+
+// The fp32 SIMT attention kernel (attention_simt.cu) for what the tensor-core kernel does
+// not take: float32 q/k/v, head_dim 64..256, N > 384, unaligned operands.  Arguments are
+// validated by launch_window_attention, which dispatches here.
+bool simt_attention_head_dim(int64_t head_dim);
+int launch_window_attention_simt(const AttnArgs& a, cudaStream_t stream);
 
 // Test hook: while enabled, attention launches issue no TMA loads (every wait in
 // the kernel expires after its time limit).  Returns the previous setting.

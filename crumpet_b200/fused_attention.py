@@ -12,8 +12,12 @@ Python entry point with the signature of the reference Triton launcher
 ``mask.shape[0] in (1, B)`` cases and MONAI's sliding-window tiling without a
 ``repeat``) or ``None``; ``boundary``: per-window flag, mask rows are read only
 where it is non-zero.  ``block_m`` / ``block_n`` are accepted for API
-compatibility and ignored: the tile shape is fixed by the tcgen05 design
-(128 query rows x 64-key chunks).  fp16 and bf16, head_dim 16 or 32, N <= 384.
+compatibility and ignored: the tile shapes are fixed by the kernels' designs.
+
+Inputs: float16, bfloat16 or float32; head_dim a power of two from 16 to 256 (the
+reference's Triton kernel takes power-of-two head dims >= 16); any N >= 1.  float16
+/ bfloat16 with head_dim 16 or 32 and N <= 384 run the tcgen05 tensor-core kernel;
+the rest runs an fp32 SIMT kernel (float32 arithmetic throughout).
 """
 
 from __future__ import annotations
@@ -22,6 +26,13 @@ import torch
 
 from . import _ops as _native
 from . import profiling as _prof
+
+_ATTN_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def head_dim_supported(head_dim: int) -> bool:
+    """Head dims the attention kernels take: powers of two from 16 to 256."""
+    return head_dim in (16, 32, 64, 128, 256)
 
 
 def fused_swin_attention(
@@ -45,10 +56,11 @@ def fused_swin_attention(
     B, H, N, D = (int(s) for s in q.shape)
     if tuple(relative_position_bias.shape) != (H, N, N):
         raise ValueError(f"relative_position_bias must have shape {(H, N, N)}")
-    if q.dtype not in (torch.float16, torch.bfloat16):
-        raise TypeError("fused_swin_attention supports torch.float16 and torch.bfloat16")
-    if D not in (16, 32):
-        raise ValueError("fused_swin_attention requires head_dim 16 or 32")
+    if q.dtype not in _ATTN_DTYPES:
+        raise TypeError("fused_swin_attention supports torch.float32, torch.float16 and "
+                        "torch.bfloat16")
+    if not head_dim_supported(D):
+        raise ValueError("fused_swin_attention requires a power-of-two head_dim between 16 and 256")
     if scale is None:
         scale = 1.0 / (D ** 0.5)
     if not 0.0 < float(scale) < float("inf"):
@@ -111,10 +123,12 @@ def swin_window_attention_qkv(
     if qkv.ndim != 5 or qkv.shape[2] != 3:
         raise ValueError("qkv must have shape [B, N, 3, H, head_dim]")
     B, N, _, H, D = (int(s) for s in qkv.shape)
-    if D not in (16, 32):
-        raise ValueError("swin_window_attention_qkv requires head_dim 16 or 32")
-    if qkv.dtype not in (torch.float16, torch.bfloat16):
-        raise TypeError("swin_window_attention_qkv supports torch.float16 and torch.bfloat16")
+    if not head_dim_supported(D):
+        raise ValueError("swin_window_attention_qkv requires a power-of-two head_dim between 16 "
+                         "and 256")
+    if qkv.dtype not in _ATTN_DTYPES:
+        raise TypeError("swin_window_attention_qkv supports torch.float32, torch.float16 and "
+                        "torch.bfloat16")
     if window_size is None:
         window_size = (N, 1, 1)
     if scale is None:
@@ -144,7 +158,7 @@ def swin_window_attention_qkv(
     return out
 
 
-__all__ = ["fused_swin_attention", "swin_window_attention_qkv"]
+__all__ = ["fused_swin_attention", "swin_window_attention_qkv", "head_dim_supported"]
 
 
 def window_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:

@@ -19,10 +19,12 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   itertools.product order: MONAI's PatchMergingV2 or the bundled module) runs as
   one gather + LayerNorm kernel and a channels-first reduction GEMM, which also
   removes the final permute copy;
-* ``WindowAttention.forward``: qkv Linear -> fused tcgen05 window attention ->
-  proj Linear (reference :117-198), falling back to the module's own eager
-  forward in training, with attention dropout, for head dims other than 16
-  and 32, or for fp32 activations;
+* ``WindowAttention.forward``: qkv Linear -> fused window attention -> proj
+  Linear (reference :117-198), falling back to the module's own eager forward
+  where the reference does (training, attention dropout, head_dim < 16) and for
+  head dims that are not a power of two up to 256 (the reference's Triton kernel
+  cannot compile those); fp16 / bf16 head_dim 16 / 32 windows of up to 384 tokens
+  run the tcgen05 kernel, the rest (fp32 activations included) the fp32 SIMT one;
 * ``SwinTransformer.proj_out`` (not patched by the reference; only when the
   module has it): the hidden-state LayerNorm of every stage output runs as one
   kernel that reads the channels-first volume and writes the channels-last
@@ -70,6 +72,7 @@ from .block_fusion import (
 )
 from .fused_attention import (
     fused_swin_attention,
+    head_dim_supported,
     swin_window_attention_qkv,
     window_linear,
     window_linear_supported,
@@ -265,8 +268,13 @@ def _patched_window_attention_forward(original):
         b, n, c = x.shape
         heads = self.num_heads
         head_dim = c // heads
+        # The reference's own fallbacks (training, attention dropout, head_dim < 16;
+        # torch-ext/crumpet/monai_patch.py:137-151), plus head dims no kernel here takes
+        # (not a power of two, or above 256), where the reference's Triton compile fails.
+        if head_dim < 16 or not head_dim_supported(head_dim) or not x.is_cuda:
+            return original(self, x, mask)
         qkv = _linear(self.qkv, x)
-        if head_dim not in (16, 32) or qkv.dtype not in (torch.float16, torch.bfloat16) or n > 384:
+        if qkv.dtype not in (torch.float32, torch.float16, torch.bfloat16):
             return original(self, x, mask)
         geometry = None if mask is None else getattr(mask, _GEOMETRY_ATTR, None)
         if mask is None or geometry is not None:

@@ -115,8 +115,10 @@ CRUMPET_API int crumpet_compute_attn_mask_3d(void* output, int dtype, int64_t D,
  * rel_bias: [H, N, N]; mask: [mask_windows, N, N] or NULL; boundary: uint8 [B]
  * or NULL.  When boundary is given, mask rows are read only for windows with
  * boundary[b] != 0 (the others are treated as unmasked); when it is NULL and a
- * mask is given, every window reads its mask.  dtype: F16 or BF16 (all tensors
- * share it); head_dim 16 or 32; 1 <= N <= 384.
+ * mask is given, every window reads its mask.  dtype: F32, F16 or BF16 (all
+ * tensors share it); head_dim 16, 32, 64, 128 or 256; any N >= 1.  F16 / BF16
+ * with head_dim 16 or 32, N <= 384 and 16-byte aligned tensors run the tcgen05
+ * tensor-core kernel; every other call runs an fp32 SIMT kernel.
  * Replaces crumpet.fused_attention.fused_swin_attention
  *   (torch-ext/crumpet/fused_attention.py:149-226; kernel :48-146), which the
  *   reference exposes only as a Python/Triton function.
@@ -143,7 +145,8 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
  *   ws_*  window size (ws_d*ws_h*ws_w == N); ss_* cyclic shift (all 0: no mask)
  * The mask equals crumpet_compute_attn_mask_3d's on the padded grid; masked
  * scores are dropped exactly (e^-100 and e^-inf are both 0 in fp32).
- * dtype F16 or BF16, head_dim 16 or 32, N <= 384.
+ * dtype F32, F16 or BF16, head_dim 16 to 256 (powers of two), any N >= 1, with
+ * the same split between the tensor-core and SIMT kernels as above.
  * Replaces the eager glue of torch-ext/crumpet/monai_patch.py:152-196 (q/k/v
  * split and .contiguous() copies, bias gather and permute, mask repeat, the
  * per-call mask abs().amax() scan, the output transpose) plus

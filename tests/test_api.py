@@ -47,13 +47,17 @@ def test_capi_rejects_bad_arguments_without_touching_the_device():
     # empty batch is a no-op
     rc = lib.crumpet_fused_shift_partition_3d(null, null, 1, 0, 14, 14, 14, 4, 7, 7, 7, 3, 3, 3, null)
     assert rc == 0
-    # attention: unsupported head_dim / N, and an empty batch
-    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 343, 64, 0.25, null)
+    # attention: unsupported head_dim / N / dtype, null pointers, and an empty batch
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 343, 48, 0.25, null)
     assert rc == 3 and "head_dim" in _ops.last_error()
-    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 1000, 16, 0.25, null)
-    assert rc == 3
-    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 0, 4, 3, 343, 16, 0.25, null)
-    assert rc == 3 and "float16" in _ops.last_error()
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 4, 3, 0, 16, 0.25, null)
+    assert rc == 3 and "N >= 1" in _ops.last_error()
+    rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 5, 4, 3, 343, 16, 0.25, null)
+    assert rc == 3 and "float32" in _ops.last_error()
+    for dtype, n, hd in ((0, 343, 16), (1, 343, 64), (1, 1000, 16), (2, 216, 256)):
+        rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, dtype, 4, 3,
+                                              n, hd, 0.25, null)
+        assert rc == 1 and "null" in _ops.last_error()
     rc = lib.crumpet_fused_swin_attention(null, null, null, null, null, null, 0, null, 1, 0, 3, 343, 16, 0.25, null)
     assert rc == 0
 
