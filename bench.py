@@ -9,13 +9,15 @@ feature 48, depths 2,2,2,2, heads 3,6,12,24, window 7, patch 2), random init
 overlap over a synthetic 1x1x512x512x224 volume of uniform[-1000, 1000]
 intensities scaled to [0, 1]: 400 ROIs per step, batches of 8, arg-max
 segmentation.  A step is one full volume.  With N GPUs (torchrun, one process
-per GPU) each rank takes a contiguous, balanced 1/N of the ROI grid and one
-NCCL reduce merges the accumulators on rank 0 (total work fixed: strong scaling).
+per GPU) each rank takes a contiguous, balanced 1/N of the ROI grid, accumulates
+over the z-slab its ROIs cover, exchanges only the overlapping halo planes with
+its neighbours (NCCL point-to-point), takes the arg-max of the z-range it owns, and
+rank 0 gathers the uint8 labels (total work fixed: strong scaling).
 
 ``value``: ROIs/s with the volume resident in HBM and the segmentation left
-on the device, CUDA-event timed, max over ranks.  ``e2e``: the same with the
-volume copied from pinned host memory and the segmentation copied back inside
-every step.  Both run each ROI batch's network forward as a CUDA graph replay
+on the device, CUDA-event timed, max over ranks.  ``e2e``: the same through
+``segment(host_volume)`` -- each rank copies its slab from pinned host memory --
+with the segmentation copied back inside every step.  Both run each ROI batch's network forward as a CUDA graph replay
 (``--eager``: without graphs).  The 3.3 GB accumulator and 235 MB volume exceed
 L2, so no flush is needed between steps.  Also reported: the same steps on the
 eager forward with CUDA events around every crumpet_b200 launch (``eager``), and
@@ -657,7 +659,8 @@ def main() -> None:
     model = build_model(device)
     crumpet.patch_monai_swin_unetr(swin_unetr)
     inferer = SlidingWindowInferer(model, (args.roi,) * 3, args.sw_batch, args.overlap, 14,
-                                   torch.float16, rank, world, cuda_graphs=not args.eager)
+                                   torch.float16, rank, world, cuda_graphs=not args.eager,
+                                   device=device)
     # the same inference without graphs: its launches can be bracketed one by one
     eager_inferer = SlidingWindowInferer(model, (args.roi,) * 3, args.sw_batch, args.overlap,
                                          14, torch.float16, rank, world)
@@ -727,8 +730,8 @@ def main() -> None:
     e2 = torch.cuda.Event(enable_timing=True)
     s2.record()
     for _ in range(args.steps):
-        vol.copy_(host, non_blocking=True)
-        seg = inferer.segment(vol)
+        # the public call with the host volume: each rank copies its z-slab to its GPU
+        seg = inferer.segment(host)
         if seg is not None:
             seg_host.copy_(seg, non_blocking=True)
     e2.record()
@@ -736,11 +739,16 @@ def main() -> None:
     barrier()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2))
 
-    total_launches = launches
+    # per step, summed over ranks: launches, host->device bytes of the e2e call, and bytes
+    # moved between GPUs (halo planes of the accumulators, owned label ranges to rank 0)
+    plan = inferer.plan(spatial)
+    label_bytes = 0 if rank == 0 else (plan[rank].own[1] - plan[rank].own[0]) * spatial[1] * spatial[2]
+    counts = [launches, inferer.staged_bytes(spatial), inferer.exchanged_bytes + label_bytes]
     if world > 1:
-        t = torch.tensor([launches], dtype=torch.int64, device=device)
+        t = torch.tensor(counts, dtype=torch.int64, device=device)
         dist.all_reduce(t)
-        total_launches = int(t.item())
+        counts = [int(v) for v in t.tolist()]
+    total_launches, h2d_bytes, p2p_bytes = counts
 
     crumpet.unpatch_monai_swin_unetr()
     kernels = None
@@ -808,8 +816,10 @@ def main() -> None:
                       "note": "same steps without CUDA graphs, every crumpet_b200 launch "
                               "bracketed by CUDA events (the per-kernel pass)"},
             "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": host.numel() * host.element_size() * world,
-                    "d2h_bytes_per_step": seg_host.numel()},
+                    "h2d_bytes_per_step": h2d_bytes,
+                    "d2h_bytes_per_step": seg_host.numel(),
+                    "note": "each rank copies only the z-slab of the host volume its ROIs read"},
+            "interconnect_bytes_per_step": p2p_bytes,
             "gpu_launches": total_launches,
             "clocks": clock,
             "roofline": roofline,

@@ -26,16 +26,23 @@ holds the forward as it was captured -- including whether crumpet_b200's patch
 was applied -- so after changing the model (patching or unpatching it, replacing
 modules or parameter tensors) call ``reset_graphs()``.
 
-Multi-GPU: one process per GPU.  Rank r runs the r-th contiguous 1/world of the ROI
-grid (balanced to one ROI), cut into batches; each rank accumulates its own
-predictions, and the only collective is one NCCL sum-reduce of the
-accumulator onto rank 0 at the end, which then normalises and takes the
-arg-max.  There is no inter-GPU traffic inside the model.
+Multi-GPU: one process per GPU, nothing exchanged inside the model.  Rank r runs the
+r-th contiguous 1/world of the ROI grid (balanced to one ROI), cut into batches.  The
+grid is ordered with z outermost, so a rank's ROIs cover a z-slab of the volume: the
+rank accumulates into a slab-sized buffer only.  The output z-axis is cut into
+disjoint ranges, one owned by each rank (from the z of its first ROI to that of the
+next rank's first ROI), each inside its owner's slab.  After accumulation every rank
+sends the parts of its slab that lie in other ranks' ranges to their owners (NCCL
+point-to-point: only the halo planes where neighbouring slabs overlap), each owner
+adds them into its range in rank order, normalises it and takes its arg-max, and
+rank 0 gathers the uint8 labels.  With a host (CPU) volume and a CUDA ``device``,
+each rank copies only its slab of the volume to its GPU.
 """
 
 from __future__ import annotations
 
 import itertools
+from dataclasses import dataclass
 from typing import Sequence
 
 import torch
@@ -69,6 +76,42 @@ def axis_counts(size: int, roi: int, overlap: float) -> list[float]:
     return counts
 
 
+@dataclass(frozen=True)
+class RankShard:
+    """One rank's share of a sliding-window pass along z (the grid's outer axis)."""
+
+    rois: tuple  # its ROI starts (absolute (z, y, x))
+    slab: tuple  # [z0, z1): the planes its ROIs read and write
+    own: tuple   # [a, b): the planes whose normalised logits / labels it produces
+
+
+def shard_plan(starts, world: int, depth: int, roi_d: int) -> list[RankShard]:
+    """Contiguous balanced ROI ranges per rank, their z-slabs, and a partition of
+    [0, depth) into owned ranges with each range inside its owner's slab."""
+    n = len(starts)
+    bounds = [r * n // world for r in range(world + 1)]
+    first_z = [starts[bounds[r]][0] if bounds[r] < n else depth for r in range(world)]
+    plan = []
+    for r in range(world):
+        mine = tuple(starts[bounds[r]:bounds[r + 1]])
+        a = 0 if r == 0 else first_z[r]
+        b = depth if r == world - 1 else first_z[r + 1]
+        if mine:
+            z0 = min(st[0] for st in mine)
+            z1 = min(depth, max(st[0] for st in mine) + roi_d)
+        else:
+            z0 = z1 = a
+        # the buffer must also cover the owned range (it does whenever consecutive ROI
+        # z-starts are at most a ROI apart, which every overlap >= 0 grid satisfies)
+        plan.append(RankShard(mine, (min(z0, a), max(z1, b)) if b > a else (z0, z1), (a, b)))
+    return plan
+
+
+def _intersect(p, q):
+    lo, hi = max(p[0], q[0]), min(p[1], q[1])
+    return (lo, hi) if hi > lo else None
+
+
 class SlidingWindowInferer:
     """Runs ``model`` over a ``[1, C_in, D, H, W]`` volume in ROI batches.
 
@@ -82,8 +125,9 @@ class SlidingWindowInferer:
     def __init__(self, model: torch.nn.Module, roi_size=(96, 96, 96), sw_batch_size: int = 4,
                  overlap: float = 0.5, num_classes: int = 14,
                  autocast_dtype: torch.dtype | None = torch.float16, rank: int = 0, world: int = 1,
-                 group=None, cuda_graphs: bool = False):
+                 group=None, cuda_graphs: bool = False, device: torch.device | str | None = None):
         self.model = model
+        self.device = None if device is None else torch.device(device)
         self.roi = tuple(int(r) for r in roi_size)
         self.sw_batch = int(sw_batch_size)
         self.overlap = float(overlap)
@@ -95,17 +139,23 @@ class SlidingWindowInferer:
         self.cuda_graphs = bool(cuda_graphs)
         self._count_cache: dict = {}
         self._graphs: dict = {}
+        self._staging: dict = {}
 
     def rois(self, spatial) -> list[tuple[int, int, int]]:
         return roi_grid(spatial, self.roi, self.overlap)
 
+    def plan(self, spatial) -> list[RankShard]:
+        """Every rank's ROIs, z-slab and owned z-range (see :func:`shard_plan`)."""
+        key = ("plan", tuple(spatial))
+        if key not in self._count_cache:
+            self._count_cache[key] = shard_plan(self.rois(spatial), self.world,
+                                                int(spatial[0]), self.roi[0])
+        return self._count_cache[key]
+
     def my_batches(self, spatial) -> list[list[tuple[int, int, int]]]:
         """This rank's ROI batches: a contiguous range of the ROI grid (ranks differ by at
         most one ROI, and a batch's ROIs stay spatially adjacent), cut into sw_batch."""
-        starts = self.rois(spatial)
-        lo = self.rank * len(starts) // self.world
-        hi = (self.rank + 1) * len(starts) // self.world
-        mine = starts[lo:hi]
+        mine = list(self.plan(spatial)[self.rank].rois)
         return [mine[i:i + self.sw_batch] for i in range(0, len(mine), self.sw_batch)]
 
     def _count_map(self, spatial, device) -> torch.Tensor:
@@ -181,32 +231,61 @@ class SlidingWindowInferer:
             self._graphs[key] = (graph, static_in, static_out, launches.delta, held)
         return self._graphs[key][:4]
 
+    def _stage(self, volume: torch.Tensor, shard: RankShard) -> tuple[torch.Tensor, int]:
+        """The tensor the ROI crops read and the z of its first plane: the volume itself
+        when it is already on the compute device; a host volume with a CUDA ``device``
+        has this rank's slab copied (asynchronously from pinned memory) into a device
+        buffer that later calls reuse."""
+        dev = self.device if self.device is not None else volume.device
+        if dev.type != "cuda" or volume.device == dev:
+            return volume, 0
+        z0, z1 = shard.slab
+        shape = (*volume.shape[:2], z1 - z0, *volume.shape[3:])
+        key = (shape, volume.dtype, dev)
+        buf = self._staging.get(key)
+        if buf is None:
+            buf = self._staging[key] = torch.empty(shape, dtype=volume.dtype, device=dev)
+        buf.copy_(volume[:, :, z0:z1], non_blocking=True)
+        return buf, z0
+
+    def staged_bytes(self, spatial, channels: int = 1, itemsize: int = 4) -> int:
+        """Host-to-device bytes one call copies on this rank for a host volume."""
+        z0, z1 = self.plan(spatial)[self.rank].slab
+        return channels * (z1 - z0) * int(spatial[1]) * int(spatial[2]) * itemsize
+
     @torch.no_grad()
     def accumulate(self, volume: torch.Tensor) -> tuple[torch.Tensor, int]:
-        """This rank's summed predictions [1, classes, D, H, W] (fp32) and its ROI count."""
+        """This rank's summed predictions over its z-slab, fp32 [1, classes, z1 - z0, H, W]
+        (the whole volume when one process covers every ROI), and its ROI count."""
         spatial = tuple(int(s) for s in volume.shape[2:])
+        shard = self.plan(spatial)[self.rank]
+        src, src_z = self._stage(volume, shard)
+        base = shard.slab[0]
         rd, rh, rw = self.roi
-        acc = torch.zeros((1, self.num_classes, *spatial), dtype=torch.float32, device=volume.device)
+        acc = torch.zeros((1, self.num_classes, shard.slab[1] - base, *spatial[1:]),
+                          dtype=torch.float32, device=src.device)
         done = 0
         for batch in self.my_batches(spatial):
-            if self.cuda_graphs and volume.is_cuda:
+            crops = [(z - src_z, y, x) for z, y, x in batch]
+            if self.cuda_graphs and src.is_cuda:
                 # capture and replay on the volume's device and its current stream
-                with torch.cuda.device(volume.device):
-                    graph, static_in, pred, launches = self._graph(len(batch), volume)
-                    self._gather(volume, batch, out=static_in)
+                with torch.cuda.device(src.device):
+                    graph, static_in, pred, launches = self._graph(len(batch), src)
+                    self._gather(src, crops, out=static_in)
                     graph.replay()
                 _prof.count_replay(launches)
             else:
-                pred = self._forward(self._gather(volume, batch))
-            if volume.is_cuda:
+                pred = self._forward(self._gather(src, crops))
+            into = [(z - base, y, x) for z, y, x in batch]
+            if src.is_cuda:
                 token = _prof.kernel_begin(
-                    "roi_accumulate", lambda: {"bytes": _accumulate_bytes(pred, batch, self.roi)})
+                    "roi_accumulate", lambda: {"bytes": _accumulate_bytes(pred, into, self.roi)})
                 _ops.require().roi_accumulate(acc[0], pred.contiguous(),
-                                              [v for st in batch for v in st], list(self.roi))
+                                              [v for st in into for v in st], list(self.roi))
                 _prof.count("roi_accumulate")
                 _prof.kernel_end(token)
             else:
-                for i, (z, y, x) in enumerate(batch):
+                for i, (z, y, x) in enumerate(into):
                     acc[0, :, z:z + rd, y:y + rh, x:x + rw] += pred[i].float()
             done += len(batch)
         return acc, done
@@ -227,48 +306,124 @@ class SlidingWindowInferer:
                 "inference (a bounded wait expired or an input was out of range); the "
                 "accumulated predictions are incomplete")
 
-    def _reduced(self, volume: torch.Tensor) -> torch.Tensor | None:
+    def _peer(self, r: int) -> int:
+        return r if self.group is None else dist.get_global_rank(self.group, r)
+
+    def _exchange(self, acc: torch.Tensor, plan: list[RankShard]) -> None:
+        """Send this rank's slab planes that other ranks own to them, and add the planes of
+        its own range that other ranks' slabs produced (in rank order)."""
+        me = plan[self.rank]
+        base = me.slab[0]
+        ops, incoming = [], []
+        for r, sh in enumerate(plan):
+            ov = _intersect(sh.own, me.slab) if r != self.rank else None
+            if ov is not None:
+                part = acc[0, :, ov[0] - base:ov[1] - base].contiguous()
+                ops.append(dist.P2POp(dist.isend, part, self._peer(r), self.group))
+        for q, sh in enumerate(plan):
+            ov = _intersect(me.own, sh.slab) if q != self.rank else None
+            if ov is not None:
+                buf = torch.empty((acc.shape[1], ov[1] - ov[0], *acc.shape[3:]),
+                                  dtype=acc.dtype, device=acc.device)
+                ops.append(dist.P2POp(dist.irecv, buf, self._peer(q), self.group))
+                incoming.append((ov, buf))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for ov, buf in incoming:
+            acc[0, :, ov[0] - base:ov[1] - base] += buf
+        # bytes this rank moved over the interconnect for this volume (sent + received)
+        self.exchanged_bytes = sum(op.tensor.numel() * op.tensor.element_size() for op in ops)
+
+    def _merged(self, volume: torch.Tensor):
+        """(this rank's owned z-range, the summed predictions over it [1, classes, b - a,
+        H, W]) with every rank's contributions added."""
+        spatial = tuple(int(s) for s in volume.shape[2:])
         acc, _ = self.accumulate(volume)
-        self._check_kernels(volume.device)
+        self._check_kernels(acc.device)
+        plan = self.plan(spatial)
+        self.exchanged_bytes = 0
         if self.world > 1:
-            dist.reduce(acc, dst=0, op=dist.ReduceOp.SUM, group=self.group)
-            if self.rank != 0:
-                return None
-        return acc
+            self._exchange(acc, plan)
+        me = plan[self.rank]
+        a, b = me.own
+        base = me.slab[0]
+        if (a, b) == (base, base + acc.shape[2]):
+            return (a, b), acc
+        return (a, b), acc[:, :, a - base:b - base].contiguous()
+
+    def _to_rank0(self, part: torch.Tensor, spatial, zdim: int):
+        """Assemble the owned ranges of every rank along ``zdim`` on rank 0 (None elsewhere)."""
+        if self.world == 1:
+            return part
+        plan = self.plan(spatial)
+        if self.rank != 0:
+            if plan[self.rank].own[1] > plan[self.rank].own[0]:
+                # batched, so NCCL does not serialise it with the other ranks' sends
+                op = dist.P2POp(dist.isend, part.contiguous(), self._peer(0), self.group)
+                for req in dist.batch_isend_irecv([op]):
+                    req.wait()
+            return None
+        shape = list(part.shape)
+        shape[zdim] = int(spatial[0])
+        full = torch.empty(shape, dtype=part.dtype, device=part.device)
+        a, b = plan[0].own
+        full.narrow(zdim, a, b - a).copy_(part)
+        ops, bufs = [], []
+        for q in range(1, self.world):
+            aq, bq = plan[q].own
+            if bq > aq:
+                shp = list(part.shape)
+                shp[zdim] = bq - aq
+                buf = torch.empty(shp, dtype=part.dtype, device=part.device)
+                ops.append(dist.P2POp(dist.irecv, buf, self._peer(q), self.group))
+                bufs.append((aq, bq, buf))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for aq, bq, buf in bufs:
+            full.narrow(zdim, aq, bq - aq).copy_(buf)
+        return full
 
     @torch.no_grad()
     def logits(self, volume: torch.Tensor) -> torch.Tensor | None:
-        """Averaged logits on rank 0 (None on other ranks)."""
-        acc = self._reduced(volume)
-        if acc is None:
-            return None
-        if not acc.is_cuda:
-            return acc / self._count_map(tuple(acc.shape[2:]), acc.device)
-        out = torch.empty_like(acc)
-        token = _prof.kernel_begin("roi_normalize",
-                                   lambda: {"bytes": 2 * acc.numel() * acc.element_size()})
-        _ops.require().roi_normalize(out[0], acc[0], *self._axis_counts(acc.shape[2:], acc.device))
-        _prof.count("roi_normalize")
-        _prof.kernel_end(token)
-        return out
+        """Averaged logits [1, classes, D, H, W] on rank 0 (None on other ranks)."""
+        spatial = tuple(int(s) for s in volume.shape[2:])
+        (a, b), acc = self._merged(volume)
+        if b == a:  # this rank owns no planes (more ranks than ROI rows)
+            out = acc[:, :, :0]
+        elif not acc.is_cuda:
+            out = acc / self._count_map(spatial, acc.device)[:, :, a:b]
+        else:
+            out = torch.empty_like(acc)
+            count_d, count_h, count_w = self._axis_counts(spatial, acc.device)
+            token = _prof.kernel_begin("roi_normalize",
+                                       lambda: {"bytes": 2 * acc.numel() * acc.element_size()})
+            _ops.require().roi_normalize(out[0], acc[0], count_d[a:b], count_h, count_w)
+            _prof.count("roi_normalize")
+            _prof.kernel_end(token)
+        return self._to_rank0(out, spatial, 2)
 
     @torch.no_grad()
     def segment(self, volume: torch.Tensor) -> torch.Tensor | None:
         """uint8 label map [D, H, W] on rank 0 (None on other ranks): the arg-max of
         the averaged logits."""
-        acc = self._reduced(volume)
-        if acc is None:
-            return None
-        if not acc.is_cuda:
-            logits = acc / self._count_map(tuple(acc.shape[2:]), acc.device)
-            return logits[0].argmax(dim=0).to(torch.uint8)
-        labels = torch.empty(acc.shape[2:], dtype=torch.uint8, device=acc.device)
-        token = _prof.kernel_begin("roi_argmax", lambda: {
-            "bytes": acc.numel() * acc.element_size() + labels.numel()})
-        _ops.require().roi_argmax(labels, acc[0], *self._axis_counts(acc.shape[2:], acc.device))
-        _prof.count("roi_argmax")
-        _prof.kernel_end(token)
-        return labels
+        spatial = tuple(int(s) for s in volume.shape[2:])
+        (a, b), acc = self._merged(volume)
+        if b == a:  # this rank owns no planes (more ranks than ROI rows)
+            labels = torch.empty((0, *spatial[1:]), dtype=torch.uint8, device=acc.device)
+        elif not acc.is_cuda:
+            logits = acc / self._count_map(spatial, acc.device)[:, :, a:b]
+            labels = logits[0].argmax(dim=0).to(torch.uint8)
+        else:
+            labels = torch.empty((b - a, *spatial[1:]), dtype=torch.uint8, device=acc.device)
+            count_d, count_h, count_w = self._axis_counts(spatial, acc.device)
+            token = _prof.kernel_begin("roi_argmax", lambda: {
+                "bytes": acc.numel() * acc.element_size() + labels.numel()})
+            _ops.require().roi_argmax(labels, acc[0], count_d[a:b], count_h, count_w)
+            _prof.count("roi_argmax")
+            _prof.kernel_end(token)
+        return self._to_rank0(labels, spatial, 0)
 
 
 def device_error(device: torch.device) -> int:
