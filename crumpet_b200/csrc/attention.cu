@@ -1,6 +1,6 @@
 // crumpet_b200: fused 3D Swin window attention for sm_100a (B200).
 //
-// Computes, per window b and head h (head_dim 16 or 32, N <= 384 tokens),
+// Computes, per window b and head h (head_dim 16 or 32, N <= 352 tokens),
 //   out[b,h] = softmax(q k^T * scale + bias[h] + mask) v
 // with fp32 scores and softmax -- the function of the reference Triton kernel
 // torch-ext/crumpet/fused_attention.py:48-146 (eager form: MONAI WindowAttention,
@@ -68,7 +68,7 @@ constexpr int kThreads = kCtrlWarps * 32 + kSmThreads;  // 512
 constexpr int kRowBytes = kAtom * 2;  // one atom row: 16 channels of fp16/bf16
 constexpr int kBarsPerWG = 9;
 constexpr uint32_t kTmemCols = 512;
-constexpr float kRescaleLog2 = 8.f;  // P = 2^(x - m_ref) stays <= 2^8
+constexpr float kRescaleLog2 = 15.f;  // P = 2^(x - m_ref) stays <= 2^15 (fp16 max 65504)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Per (padded key count, head dim) layout.  A head dim of 32 is two 16-channel
@@ -76,16 +76,20 @@ constexpr float kLog2e = 1.4426950408889634f;
 // takes one MMA per atom, and PV one MMA per atom ([V_0 | 1] then V_1).
 template <int NPAD, int HD>
 struct Cfg {
-  static_assert(NPAD % 32 == 0 && NPAD <= 384, "NPAD must be a multiple of 32, at most 384");
+  static_assert(NPAD % 32 == 0 && NPAD <= 352, "NPAD must be a multiple of 32, at most 352");
   static_assert(HD == 16 || HD == 32, "head_dim 16 or 32");
   static constexpr int NKH = HD / kAtom;              // channel atoms
-  static constexpr int NKB = (NPAD + 127) / 128;      // 128-row TMA boxes for K and V
+  // K / V rows per TMA box: NPAD split into equal boxes of at most 128 rows (multiples of
+  // 8 rows, so every box starts on the 32-byte swizzle's 256-byte period)
+  static constexpr int KVB = NPAD == 352 ? 88 : NPAD == 224 ? 112 : (NPAD < 128 ? NPAD : 128);
+  static constexpr int NKB = NPAD / KVB;
+  static_assert(NPAD % KVB == 0 && KVB % 8 == 0 && KVB <= 128, "K/V box rows");
   static constexpr int NCH = (NPAD + kCH - 1) / kCH;  // key chunks
   static constexpr int LAST_W = NPAD - (NCH - 1) * kCH;
   static constexpr int STAGES = HD == 16 ? 4 : 2;     // Q/K/V ring stages (shared memory budget)
   static constexpr int NPB = HD == 16 ? 2 : 1;        // P chunk buffers (TMEM budget)
   static constexpr int Q_ATOM = kBM * kRowBytes;
-  static constexpr int KV_ATOM = NKB * 128 * kRowBytes;
+  static constexpr int KV_ATOM = NPAD * kRowBytes;
   static constexpr int Q_BYTES = NKH * Q_ATOM;
   static constexpr int KV_BYTES = NKH * KV_ATOM;
   static constexpr int STAGE_BYTES = Q_BYTES + 2 * KV_BYTES;
@@ -93,8 +97,14 @@ struct Cfg {
   // 128 bytes; core matrix (row group rg, column group cg) at cg * 2048 + rg * 128.
   static constexpr int BIAS_CG_BYTES = (kBM / 8) * 128;  // 2048
   static constexpr int BIAS_BYTES = (NPAD / 8) * BIAS_CG_BYTES;
-  static constexpr int ONES_BYTES = NKB * 128 * kRowBytes;  // [keys][16] of 1.0
-  static constexpr int PLANE_BYTES = 3 * NCH * 8;     // analytic-mask code planes
+  // [16 keys][16] of 1.0: every PV MMA (K = 16 keys) reads its ones columns from this one
+  // block (the content is the same for every key, so the swizzle does not matter)
+  static constexpr int ONES_BYTES = 16 * kRowBytes;
+  // Shifted-window mask on the tensor cores: three query-feature tiles (one per axis,
+  // [128 rows x 16], UMMA A operand like the bias tile) and one key-feature tile
+  // ([NPAD keys x 16], UMMA B operand, K-major without swizzle).
+  static constexpr int MASKA_BYTES = 3 * (kBM / 8) * 128 * 2;
+  static constexpr int MASKB_BYTES = (NPAD / 8) * 128 * 2;
   // TMEM columns of one WG: S chunk (64), NPB P chunk buffers (32 packed each),
   // O_0 (16) + row sum (16) [+ O_1 (16) for head dim 32].
   static constexpr int TM_S = 0;
@@ -106,7 +116,7 @@ struct Cfg {
   static_assert(TMEM_PER_WG * kNumWG <= kTmemCols, "TMEM budget");
   static constexpr int IDENT_BYTES = 512;             // 16x16 identity, UMMA B operand
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
-                                    IDENT_BYTES + PLANE_BYTES +
+                                    IDENT_BYTES + MASKA_BYTES + MASKB_BYTES +
                                     (2 * STAGES + kNumWG * kBarsPerWG + 1) * 8 + 64 + 4 * STAGES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -259,6 +269,16 @@ __device__ __forceinline__ uint32_t token_code(const KParams& p, int t) {
          (uint32_t(lw >= p.wsw - p.ssw) << 2);
 }
 
+// Axes (bit a) on which window b is the last window of a shifted grid: there the roll
+// seam splits the window into regions whose tokens must not attend to each other.
+__device__ __forceinline__ uint32_t window_last_axes(const KParams& p, int b) {
+  const int wi = b % (p.nwd * p.nwh * p.nww);
+  const int iw = wi % p.nww, t = wi / p.nww;
+  const int ih = t % p.nwh, id = t / p.nwh;
+  return uint32_t(p.ssd != 0 && id == p.nwd - 1) | (uint32_t(p.ssh != 0 && ih == p.nwh - 1) << 1) |
+         (uint32_t(p.ssw != 0 && iw == p.nww - 1) << 2);
+}
+
 template <int NPAD, int HD, bool BF16, int MASK>
 __global__ void __launch_bounds__(kThreads, 1)
 window_attention_kernel(const __grid_constant__ CUtensorMap tq,
@@ -273,9 +293,9 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   uint16_t* ones_s = reinterpret_cast<uint16_t*>(smem + kStages * C::STAGE_BYTES);
   uint8_t* bias_s = reinterpret_cast<uint8_t*>(ones_s) + C::ONES_BYTES;
   uint16_t* ident_s = reinterpret_cast<uint16_t*>(bias_s + C::BIAS_BYTES);
-  uint64_t* planes = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(ident_s) +
-                                                 C::IDENT_BYTES);
-  uint64_t* bars = planes + 3 * C::NCH;
+  uint8_t* maska_s = reinterpret_cast<uint8_t*>(ident_s) + C::IDENT_BYTES;
+  uint8_t* maskb_s = maska_s + C::MASKA_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(maskb_s + C::MASKB_BYTES);
   uint64_t* bias_ready = bars + 2 * kStages + kNumWG * kBarsPerWG;  // one phase per pair
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bias_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -322,15 +342,22 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     fence_mbar_init();
   }
   if constexpr (MASK == kMaskAnalytic) {
-    // Code planes: bit j of plane[a][c] = bit a of the code of token c*64 + j.
-    if (threadIdx.x < 3 * C::NCH) {
-      const int a = threadIdx.x / C::NCH, c = threadIdx.x % C::NCH;
-      uint64_t bits = 0;
-      for (int j = 0; j < kCH; ++j) {
-        const int t = c * kCH + j;
-        if (t < p.N && ((token_code(p, t) >> a) & 1u)) bits |= uint64_t(1) << j;
+    // Key features of the mask MMA, B[j][2a] = (1 - code_j,a) * pen, B[j][2a+1] = code_j,a * pen
+    // with pen = elem(-100 / scale); with the query features A_a[i][2a] = code_i,a,
+    // A_a[i][2a+1] = 1 - code_i,a of one axis a, sum_k A_a[i][k] B[j][k] is pen exactly when
+    // the two tokens sit on different sides of that axis' roll seam, else 0.  Padded keys
+    // get no features (the bias tile already drops them).  K-major without swizzle: element
+    // (j, k) at (k / 8) * (NPAD / 8) * 128 + (j / 8) * 128 + (j % 8) * 16 + (k % 8) * 2.
+    const uint16_t pen = f32_to_elem<BF16>(-100.f / p.scale);
+    uint16_t* mb = reinterpret_cast<uint16_t*>(maskb_s);
+    for (int e = threadIdx.x; e < NPAD * 16; e += kThreads) {
+      const int j = e >> 4, k = e & 15;
+      uint16_t val = 0;
+      if (j < p.N && k < 6) {
+        const uint32_t bit = (token_code(p, j) >> (k >> 1)) & 1u;
+        val = ((k & 1) ? bit : 1u - bit) ? pen : uint16_t(0);
       }
-      planes[a * C::NCH + c] = bits;
+      mb[((k >> 3) * (NPAD / 8) * 128 + (j >> 3) * 128 + (j & 7) * 16 + (k & 7) * 2) / 2] = val;
     }
   }
   {
@@ -387,10 +414,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               tma_load_4d(sb + hk * C::Q_ATOM, &tq, full, kAtom * hk, mt * kBM, h, b);
 #pragma unroll
               for (int kb = 0; kb < C::NKB; ++kb) {
-                tma_load_4d(sb + C::Q_BYTES + hk * C::KV_ATOM + kb * 128 * kRowBytes, &tk, full,
-                            kAtom * hk, kb * 128, h, b);
-                tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + hk * C::KV_ATOM + kb * 128 * kRowBytes,
-                            &tv, full, kAtom * hk, kb * 128, h, b);
+                tma_load_4d(sb + C::Q_BYTES + hk * C::KV_ATOM + kb * C::KVB * kRowBytes, &tk, full,
+                            kAtom * hk, kb * C::KVB, h, b);
+                tma_load_4d(sb + C::Q_BYTES + C::KV_BYTES + hk * C::KV_ATOM + kb * C::KVB * kRowBytes,
+                            &tv, full, kAtom * hk, kb * C::KVB, h, b);
               }
             }
           }
@@ -426,15 +453,17 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             tc_fence_after();
           }
           const int width = (c < C::NCH - 1) ? kCH : C::LAST_W;
-          // B = [V_0 | ones]: MN-major, the ones atom sits LBO bytes after V_0; further
-          // channel atoms V_1.. accumulate into their own 16 columns after the row sums
+          // B = [V_0 | ones]: MN-major, the ones atom sits LBO bytes after this MMA's 16 V
+          // rows -- every MMA points at the same 16-row ones block, which lies above the
+          // ring -- and further channel atoms V_1.. accumulate into their own 16 columns
+          // after the row sums
           constexpr uint32_t idesc_pv = idesc_f16(kBM, 2 * kAtom, BF16, true);
           constexpr uint32_t idesc_pv1 = idesc_f16(kBM, kAtom, BF16, true);
-          const uint32_t lbo = ones_addr - v_addr;
           for (int k = 0; k < width / 16; ++k) {
             const uint32_t pa = tP + buf * uint32_t(kCH / 2) + uint32_t(k * 8);
             const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
             const uint32_t row_off = uint32_t(c * kCH + k * 16) * kRowBytes;
+            const uint32_t lbo = ones_addr - (v_addr + row_off);
             umma_ts(tO, pa, smem_desc(v_addr + row_off, lbo, 256, kLayoutSW32), idesc_pv, acc);
 #pragma unroll
             for (int hk = 1; hk < C::NKH; ++hk) {
@@ -450,6 +479,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         // Bias MMA: S[:, 16i..16i+16) += bias_tile[:, 16i..16i+16) * I16, which adds
         // the (bias / scale) tile to the scores exactly (one non-zero product per sum).
         const uint32_t bias_addr = smem_u32(bias_s);
+        const uint32_t maska_addr = smem_u32(maska_s);
+        const uint32_t maskb_addr = smem_u32(maskb_s);
+        (void)maska_addr;
+        (void)maskb_addr;
         const uint64_t ident_desc = smem_desc(smem_u32(ident_s), 256, 128, kLayoutNone);
         constexpr uint32_t idesc_bias = idesc_f16(kBM, 16, BF16, false);
         uint32_t k = 0;
@@ -469,6 +502,9 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             }
             tc_fence_after();
             const uint32_t sb = smem_u32(smem + st * C::STAGE_BYTES);
+            // axes on which this window is the last one of a shifted grid
+            uint32_t am = 0;
+            if constexpr (MASK == kMaskAnalytic) am = window_last_axes(p, b);
             const uint32_t q_addr = sb;
             const uint32_t k_addr = sb + C::Q_BYTES;
             const uint32_t v_addr = sb + C::Q_BYTES + C::KV_BYTES;
@@ -493,6 +529,20 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
                     bias_addr + uint32_t(c * (kCH / 8) + 2 * i) * C::BIAS_CG_BYTES,
                     C::BIAS_CG_BYTES, 128, kLayoutNone);
                 umma_ss(tS + uint32_t(16 * i), bdesc, ident_desc, idesc_bias, 1u);
+              }
+              if constexpr (MASK == kMaskAnalytic) {
+                // shifted-window mask: one MMA per masked axis adds the penalty where the
+                // query and key sit on different sides of that axis' roll seam
+                const uint64_t kf = smem_desc(maskb_addr + uint32_t(c * kCH / 8) * 128u,
+                                              (NPAD / 8) * 128, 128, kLayoutNone);
+#pragma unroll
+                for (int a = 0; a < 3; ++a) {
+                  if ((am >> a) & 1u) {
+                    const uint64_t qf = smem_desc(maska_addr + uint32_t(a) * (kBM / 8) * 256u,
+                                                  (kBM / 8) * 128, 128, kLayoutNone);
+                    umma_ss(tS, qf, kf, idesc_f16(kBM, width, BF16, false), 1u);
+                  }
+                }
               }
               umma_commit(bar(w, kSF));
               if (c > 0 && !issue_pv(c - 1, v_addr)) ok = false;
@@ -624,7 +674,25 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
           }
         }
       }
-      fence_proxy_async_shared();  // bias tile -> tensor-core (async proxy) reads
+      if constexpr (MASK == kMaskAnalytic) {
+        // Query features of the mask MMA for this query tile, one [128 x 16] tile per axis a:
+        // A_a[r][2a] = code_a(row), A_a[r][2a + 1] = 1 - code_a(row), 0 elsewhere and in rows
+        // past N; same core-matrix layout as the bias tile.
+        const uint16_t one = BF16 ? 0x3F80u : 0x3C00u;
+        uint16_t* ma = reinterpret_cast<uint16_t*>(maska_s);
+        for (int e = tid_sm; e < 3 * kBM * 16; e += kSmThreads) {
+          const int a = e / (kBM * 16), r = (e / 16) % kBM, k = e % 16;
+          const int grow = mt * kBM + r;
+          uint16_t val = 0;
+          if (grow < p.N && (k >> 1) == a) {
+            const uint32_t bit = (token_code(p, grow) >> a) & 1u;
+            val = ((k & 1) ? 1u - bit : bit) ? one : uint16_t(0);
+          }
+          ma[(a * (kBM / 8) * 256 + (k >> 3) * (kBM / 8) * 128 + (r >> 3) * 128 + (r & 7) * 16 +
+              (k & 7) * 2) / 2] = val;
+        }
+      }
+      fence_proxy_async_shared();  // bias / mask tiles -> tensor-core (async proxy) reads
       named_bar_sync(1, kSmThreads);
       if (tid_sm == 0) mbar_arrive(bias_ready);
       if (!ok) continue;
@@ -632,30 +700,19 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
       const int qrow = mt * kBM + row;
       const bool valid = qrow < p.N;
       const bool warp_live = (mt * kBM + quarter * 32) < p.N;  // uniform per warp
-      uint32_t code_i = 0;
-      if constexpr (MASK == kMaskAnalytic) code_i = valid ? token_code(p, qrow) : 0u;
 
       for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k_tile) {
         if (int(k_tile % kNumWG) != w) continue;
         // ---- per-tile mask state
         bool use_dense = false;
         const uint16_t* mrow = nullptr;
-        uint32_t am = 0;
         if constexpr (MASK == kMaskDense) {
           use_dense = (p.boundary == nullptr) || (p.boundary[b] != 0);
           const int mw = b % p.mask_windows;
           mrow = p.mask + (size_t(mw) * p.N + (valid ? qrow : 0)) * p.N;
         }
-        if constexpr (MASK == kMaskAnalytic) {
-          const int wi = b % (p.nwd * p.nwh * p.nww);
-          const int iw = wi % p.nww, t = wi / p.nww;
-          const int ih = t % p.nwh, id = t / p.nwh;
-          am = uint32_t(p.ssd != 0 && id == p.nwd - 1) |
-               (uint32_t(p.ssh != 0 && ih == p.nwh - 1) << 1) |
-               (uint32_t(p.ssw != 0 && iw == p.nww - 1) << 2);
-        }
         // Reference maximum of this row (log2 domain).  P = 2^(x - m_ref) is kept
-        // <= 2^8: m_ref moves up only when a chunk exceeds it by more than 8, and
+        // <= 2^15: m_ref moves up only when a chunk exceeds it by more than 15, and
         // then the O accumulator (with the row sums) is rescaled in TMEM first.
         float m_ref = kNegInf;
 
@@ -727,26 +784,14 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
               }
             }
           }
-          if constexpr (MASK == kMaskAnalytic) {
-            if (am != 0) {
-              uint64_t pen = 0;
+          // chunk maximum: eight independent max3 chains, then a 3-level tree
+          float mq[8];
 #pragma unroll
-              for (int a = 0; a < 3; ++a) {
-                if ((am >> a) & 1u) {
-                  pen |= planes[a * C::NCH + c] ^ (((code_i >> a) & 1u) ? ~uint64_t(0) : uint64_t(0));
-                }
-              }
+          for (int q = 0; q < 8; ++q) mq[q] = kNegInf;
 #pragma unroll
-              for (int j = 0; j < W; ++j) {
-                if ((pen >> j) & 1u) v[j] = kNegInf;
-              }
-            }
-          }
-          // chunk maximum: four independent max3 chains, then a 3-op tree
-          float mq[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
-#pragma unroll
-          for (int j = 0; j < W; j += 2) mq[(j >> 1) & 3] = max3(mq[(j >> 1) & 3], v[j], v[j + 1]);
-          const float mv = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+          for (int j = 0; j < W; j += 2) mq[(j >> 1) & 7] = max3(mq[(j >> 1) & 7], v[j], v[j + 1]);
+          const float mv = fmaxf(fmaxf(max3(mq[0], mq[1], mq[2]), max3(mq[3], mq[4], mq[5])),
+                                 fmaxf(mq[6], mq[7]));
           const float mc = mv * c1.x;  // chunk maximum in the log2 domain
           const bool need = mc > m_ref + kRescaleLog2;  // m_ref = -inf: any finite mc
           const float new_ref = need ? mc : m_ref;
@@ -877,15 +922,16 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 4D map {head_dim, N, H, B} over q/k/v with a 128-row box and 32-byte swizzle.
-int make_qkv_map(CUtensorMap* map, const void* base, const AttnArgs& a) {
+// 4D map {head_dim, N, H, B} over q/k/v: boxes of one 16-channel atom x box_rows rows
+// (128 for Q, the K/V box height of the chosen key padding for K and V), 32-byte swizzle.
+int make_qkv_map(CUtensorMap* map, const void* base, const AttnArgs& a, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return set_error(kErrCuda, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[4] = {cuuint64_t(a.head_dim), cuuint64_t(a.N), cuuint64_t(a.H),
                               cuuint64_t(a.B)};
   const cuuint64_t strides[3] = {cuuint64_t(a.qkv_stride_n) * 2, cuuint64_t(a.qkv_stride_h) * 2,
                                  cuuint64_t(a.qkv_stride_b) * 2};
-  const cuuint32_t box[4] = {cuuint32_t(kAtom), 128u, 1u, 1u};  // one 16-channel atom
+  const cuuint32_t box[4] = {cuuint32_t(kAtom), cuuint32_t(box_rows), 1u, 1u};
   const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   const CUtensorMapDataType dt =
       a.dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -984,20 +1030,29 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
       if (a.shift[i] < 0 || a.shift[i] >= a.win[i])
         return set_error(kErrInvalid, "analytic mask shift must satisfy 0 <= shift < window");
   }
-  // The tensor-core kernel: fp16 / bf16, head_dim 16 or 32, N <= 384, q/k/v/out on
+  // The tensor-core kernel: fp16 / bf16, head_dim 16 or 32, N <= 352, q/k/v/out on
   // 16-byte boundaries with 16-byte row strides (TMA); everything else runs the
   // fp32 SIMT kernel (attention_simt.cu).
   const bool tensor_path =
-      a.dtype != kF32 && (a.head_dim == 16 || a.head_dim == 32) && a.N <= 384 &&
+      a.dtype != kF32 && (a.head_dim == 16 || a.head_dim == 32) && a.N <= 352 &&
       aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
       (a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 == 0 &&
       (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 == 0;
   if (!tensor_path) return launch_window_attention_simt(a, stream);
 
+  const int n32 = int((a.N + 31) / 32) * 32;
+  const int npad = n32 <= 64 ? 64 : n32 <= 128 ? 128 : n32 <= 224 ? 224 : 352;
+  int kv_rows = 128;
+  switch (npad) {
+    case 64: kv_rows = Cfg<64, 16>::KVB; break;
+    case 128: kv_rows = Cfg<128, 16>::KVB; break;
+    case 224: kv_rows = Cfg<224, 16>::KVB; break;
+    default: kv_rows = Cfg<352, 16>::KVB; break;
+  }
   CUtensorMap tq, tk, tv;
-  if (int e = make_qkv_map(&tq, a.q, a)) return e;
-  if (int e = make_qkv_map(&tk, a.k, a)) return e;
-  if (int e = make_qkv_map(&tv, a.v, a)) return e;
+  if (int e = make_qkv_map(&tq, a.q, a, kBM)) return e;
+  if (int e = make_qkv_map(&tk, a.k, a, kv_rows)) return e;
+  if (int e = make_qkv_map(&tv, a.v, a, kv_rows)) return e;
 
   KParams kp{};
   kp.bias = static_cast<const uint16_t*>(a.bias);
@@ -1036,12 +1091,10 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
     kp.wsd = kp.wsh = kp.wsw = 1;
   }
 
-  const int n32 = int((a.N + 31) / 32) * 32;
   if (n32 <= 64) return dispatch_npad<64>(a, tq, tk, tv, kp, stream);
   if (n32 <= 128) return dispatch_npad<128>(a, tq, tk, tv, kp, stream);
   if (n32 <= 224) return dispatch_npad<224>(a, tq, tk, tv, kp, stream);
-  if (n32 <= 352) return dispatch_npad<352>(a, tq, tk, tv, kp, stream);
-  return dispatch_npad<384>(a, tq, tk, tv, kp, stream);
+  return dispatch_npad<352>(a, tq, tk, tv, kp, stream);
 }
 
 int read_device_error(bool clear) {

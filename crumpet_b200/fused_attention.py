@@ -16,7 +16,7 @@ compatibility and ignored: the tile shapes are fixed by the kernels' designs.
 
 Inputs: float16, bfloat16 or float32; head_dim a power of two from 16 to 256 (the
 reference's Triton kernel takes power-of-two head dims >= 16); any N >= 1.  float16
-/ bfloat16 with head_dim 16 or 32 and N <= 384 run the tcgen05 tensor-core kernel;
+/ bfloat16 with head_dim 16 or 32 and N <= 352 run the tcgen05 tensor-core kernel;
 the rest runs an fp32 SIMT kernel (float32 arithmetic throughout).
 """
 

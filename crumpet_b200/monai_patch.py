@@ -23,7 +23,7 @@ Same contract as the reference patch (torch-ext/crumpet/monai_patch.py:235-275):
   Linear (reference :117-198), falling back to the module's own eager forward
   where the reference does (training, attention dropout, head_dim < 16) and for
   head dims that are not a power of two up to 256 (the reference's Triton kernel
-  cannot compile those); fp16 / bf16 head_dim 16 / 32 windows of up to 384 tokens
+  cannot compile those); fp16 / bf16 head_dim 16 / 32 windows of up to 352 tokens
   run the tcgen05 kernel, the rest (fp32 activations included) the fp32 SIMT one;
 * ``SwinTransformer.proj_out`` (not patched by the reference; only when the
   module has it): the hidden-state LayerNorm of every stage output runs as one

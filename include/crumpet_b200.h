@@ -117,7 +117,7 @@ CRUMPET_API int crumpet_compute_attn_mask_3d(void* output, int dtype, int64_t D,
  * boundary[b] != 0 (the others are treated as unmasked); when it is NULL and a
  * mask is given, every window reads its mask.  dtype: F32, F16 or BF16 (all
  * tensors share it); head_dim 16, 32, 64, 128 or 256; any N >= 1.  F16 / BF16
- * with head_dim 16 or 32, N <= 384 and 16-byte aligned tensors run the tcgen05
+ * with head_dim 16 or 32, N <= 352 and 16-byte aligned tensors run the tcgen05
  * tensor-core kernel; every other call runs an fp32 SIMT kernel.
  * Replaces crumpet.fused_attention.fused_swin_attention
  *   (torch-ext/crumpet/fused_attention.py:149-226; kernel :48-146), which the
