@@ -256,7 +256,7 @@ def attention_stages(device, ref, timed) -> list:
     against the reference's Triton kernel on the same windows: exps, times, ratio."""
     import torch
 
-    from crumpet_b200.fused_attention import swin_window_attention_qkv
+    from crumpet_b200.fused_attention import attention_bias_tiles, swin_window_attention_qkv
 
     rows = []
     # (padded edge, heads, window, shift): 48^3 -> 49, 24^3 -> 28, 12^3 -> 14, 6^3
@@ -271,10 +271,14 @@ def attention_stages(device, ref, timed) -> list:
         rel = (coords[:, :, None] - coords[:, None, :]) + 6
         index = (rel[0] * 169 + rel[1] * 13 + rel[2]).to(device)
         ws, ss = (w,) * 3, (sh,) * 3
-        ms = timed(lambda: swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25),
-                   iters=10)
+        # the patched network builds each module's bias tiles once and passes them
+        tiles = attention_bias_tiles(table, index, N, 0.25, torch.float16)
+        ms = timed(lambda: swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25,
+                                                     bias_tiles=tiles), iters=10)
+        ms_gather = timed(lambda: swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25),
+                          iters=10)
         row = {"stage_windows": f"{edge}^3 padded, {B} windows x {H} heads, N={N}",
-               "exps": B * H * N * N, "ms": ms,
+               "exps": B * H * N * N, "ms": ms, "ms_bias_gathered_per_cta": ms_gather,
                "sfu_frac": B * H * N * N / ms / 1e6 / (16 * 148 * 1965e-3)}
         if ref is not None and N in ref.kernels:
             q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).contiguous() for i in range(3))

@@ -45,6 +45,8 @@ _OP_NAMES = (
     "fused_unshift_unpartition_3d_backward",
     "fused_swin_attention",
     "swin_window_attention_qkv",
+    "attention_bias_tiles",
+    "swin_window_attention_qkv_tiles",
     "norm_shift_partition_3d",
     "unshift_unpartition_crop_3d",
     "unshift_unpartition_crop_norm_3d",

@@ -99,6 +99,14 @@ def capi() -> ctypes.CDLL:
         lib.crumpet_swin_window_attention_qkv.argtypes = (
             [vp, vp, vp, i32, i64, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
         lib.crumpet_swin_window_attention_qkv.restype = i32
+        lib.crumpet_attention_bias_tiles_bytes.argtypes = [i64, i64]
+        lib.crumpet_attention_bias_tiles_bytes.restype = i64
+        lib.crumpet_attention_bias_tiles.argtypes = [vp, vp, i32, i64, vp, i64, i32, i64, i64,
+                                                     ctypes.c_float, vp]
+        lib.crumpet_attention_bias_tiles.restype = i32
+        lib.crumpet_swin_window_attention_qkv_tiles.argtypes = (
+            [vp, vp, vp] + [i64] * 9 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
+        lib.crumpet_swin_window_attention_qkv_tiles.restype = i32
         lib.crumpet_norm_shift_partition_3d.argtypes = (
             [vp, i32, vp, i32, vp, vp, ctypes.c_float] + [i64] * 11 + [vp])
         lib.crumpet_norm_shift_partition_3d.restype = i32

@@ -129,6 +129,7 @@ struct KParams {
   const void* table;
   const long long* index;
   long long table_rows;  // index values outside [0, table_rows) are flagged, not read
+  const uint8_t* bias_tiles;  // prebuilt bias tiles [H * MT][BIAS_BYTES], or null
   int index_stride;
   int bias_from_table;
   int table_f32;
@@ -277,6 +278,105 @@ __device__ __forceinline__ uint32_t window_last_axes(const KParams& p, int b) {
   const int ih = t % p.nwh, id = t / p.nwh;
   return uint32_t(p.ssd != 0 && id == p.nwd - 1) | (uint32_t(p.ssh != 0 && ih == p.nwh - 1) << 1) |
          (uint32_t(p.ssw != 0 && iw == p.nww - 1) << 2);
+}
+
+// Relative-position bias tile of one (head h, query tile mt) for the bias MMA, written
+// to dst (shared or global memory) as the UMMA K-major no-swizzle operand image:
+// elem(elem(bias) / scale) -- rounded to the element type first, as the reference's
+// .to(dtype) -- at rows < N and columns < N; -30000 in padded key columns (their
+// scores drop out of the softmax: 2^(-30000 scale log2 e) is 0); 0 in padded query
+// rows.  Core matrix (row group rg, column group cg) at cg * (kBM / 8) * 128 + rg * 128.
+// Each item is 8 consecutive columns of one row (one 16-byte core-matrix row); two
+// items per thread are in flight.  Threads tid = 0 .. nthreads-1 share the work.
+template <int NPAD, bool BF16>
+__device__ __forceinline__ void build_bias_tile(const KParams& p, int h, int mt, int tid,
+                                                int nthreads, uint8_t* dst) {
+  constexpr int BIAS_CG = (kBM / 8) * 128;
+  constexpr int kItems = kBM * (NPAD / 8);
+  constexpr int kBatch = 2;
+  const float inv_scale = 1.f / p.scale;
+  const uint16_t pad_val = f32_to_elem<BF16>(-30000.f);
+  for (int i0 = tid; i0 < kItems; i0 += kBatch * nthreads) {
+    float vals[kBatch][8];
+    long long idx[kBatch][8];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int item = i0 + u * nthreads;
+      const int r = item % kBM, cg = item / kBM;
+      const int grow = mt * kBM + r;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int col = cg * 8 + e;
+        const bool in = item < kItems && grow < p.N && col < p.N;
+        idx[u][e] = -1;
+        vals[u][e] = 0.f;
+        if (in) {
+          if (p.bias_from_table) {
+            // -1 marks "not gathered" below, so a stored -1 is mapped to another
+            // out-of-range value to be flagged like any other
+            const long long v = p.index[(long long)grow * p.index_stride + col];
+            idx[u][e] = v == -1 ? -2 : v;
+          } else {
+            vals[u][e] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
+          }
+        }
+      }
+    }
+    if (p.bias_from_table) {
+      // An index value outside the table would read past it: flag it in the
+      // device error word (bit 2) and take the bias as 0 instead.
+      bool bad = false;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (idx[u][e] != -1 && (idx[u][e] < 0 || idx[u][e] >= p.table_rows)) {
+            bad = true;
+            idx[u][e] = -1;
+          }
+        }
+      }
+      if (bad) atomicOr(&g_device_error, 2);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (idx[u][e] >= 0) {
+            vals[u][e] =
+                p.table_f32
+                    ? static_cast<const float*>(p.table)[idx[u][e] * p.H + h]
+                    : to_f32<BF16>(
+                          static_cast<const uint16_t*>(p.table)[idx[u][e] * p.H + h]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int item = i0 + u * nthreads;
+      if (item >= kItems) continue;
+      const int r = item % kBM, cg = item / kBM;
+      const int grow = mt * kBM + r;
+      uint32_t wv[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        uint32_t pair = 0;
+#pragma unroll
+        for (int z = 0; z < 2; ++z) {
+          const int col = cg * 8 + e + z;
+          uint16_t v16;
+          if (grow >= p.N) v16 = 0;
+          else if (col >= p.N) v16 = pad_val;
+          else v16 = f32_to_elem<BF16>(to_f32<BF16>(f32_to_elem<BF16>(vals[u][e + z])) * inv_scale);
+          pair |= uint32_t(v16) << (16 * z);
+        }
+        wv[e / 2] = pair;
+      }
+      *reinterpret_cast<uint4*>(dst + cg * BIAS_CG + 16 * r) =
+          make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+
 }
 
 template <int NPAD, int HD, bool BF16, int MASK>
@@ -581,98 +681,18 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     for (int pi = 0; pi < sc.pair_count; ++pi) {
       const int pair = sc.pair_begin + pi * sc.pair_step;
       const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
-      // Relative-position bias tile of this (head, query tile) for the bias MMA:
-      // elem(elem(bias) / scale) -- rounded to the element type first, as the
-      // reference's .to(dtype) -- at rows < N and columns < N; -30000 in padded
-      // key columns (their scores drop out of the softmax: 2^(-30000 scale log2 e)
-      // is 0); 0 in padded query rows.  Each item is 8 consecutive columns of one
-      // row (one 16-byte core-matrix row); two items per thread are in flight.
+      // Relative-position bias tile of this (head, query tile) for the bias MMA: copied
+      // from prebuilt tiles when the caller has them, else gathered here.
       named_bar_sync(1, kSmThreads);
-      {
-        constexpr int kItems = kBM * (NPAD / 8);
-        constexpr int kBatch = 2;
-        const float inv_scale = 1.f / p.scale;
-        const uint16_t pad_val = f32_to_elem<BF16>(-30000.f);
-        for (int i0 = tid_sm; i0 < kItems; i0 += kBatch * kSmThreads) {
-          float vals[kBatch][8];
-          long long idx[kBatch][8];
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            const int item = i0 + u * kSmThreads;
-            const int r = item % kBM, cg = item / kBM;
-            const int grow = mt * kBM + r;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int col = cg * 8 + e;
-              const bool in = item < kItems && grow < p.N && col < p.N;
-              idx[u][e] = -1;
-              vals[u][e] = 0.f;
-              if (in) {
-                if (p.bias_from_table) {
-                  // -1 marks "not gathered" below, so a stored -1 is mapped to another
-                  // out-of-range value to be flagged like any other
-                  const long long v = p.index[(long long)grow * p.index_stride + col];
-                  idx[u][e] = v == -1 ? -2 : v;
-                } else {
-                  vals[u][e] = to_f32<BF16>(p.bias[(size_t(h) * p.N + grow) * p.N + col]);
-                }
-              }
-            }
-          }
-          if (p.bias_from_table) {
-            // An index value outside the table would read past it: flag it in the
-            // device error word (bit 2) and take the bias as 0 instead.
-            bool bad = false;
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (idx[u][e] != -1 && (idx[u][e] < 0 || idx[u][e] >= p.table_rows)) {
-                  bad = true;
-                  idx[u][e] = -1;
-                }
-              }
-            }
-            if (bad) atomicOr(&g_device_error, 2);
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (idx[u][e] >= 0) {
-                  vals[u][e] =
-                      p.table_f32
-                          ? static_cast<const float*>(p.table)[idx[u][e] * p.H + h]
-                          : to_f32<BF16>(
-                                static_cast<const uint16_t*>(p.table)[idx[u][e] * p.H + h]);
-                }
-              }
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            const int item = i0 + u * kSmThreads;
-            if (item >= kItems) continue;
-            const int r = item % kBM, cg = item / kBM;
-            const int grow = mt * kBM + r;
-            uint32_t wv[4];
-#pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              uint32_t pair = 0;
-#pragma unroll
-              for (int z = 0; z < 2; ++z) {
-                const int col = cg * 8 + e + z;
-                uint16_t v16;
-                if (grow >= p.N) v16 = 0;
-                else if (col >= p.N) v16 = pad_val;
-                else v16 = f32_to_elem<BF16>(to_f32<BF16>(f32_to_elem<BF16>(vals[u][e + z])) * inv_scale);
-                pair |= uint32_t(v16) << (16 * z);
-              }
-              wv[e / 2] = pair;
-            }
-            *reinterpret_cast<uint4*>(bias_s + cg * C::BIAS_CG_BYTES + 16 * r) =
-                make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          }
-        }
+      if (p.bias_tiles != nullptr) {
+        // the tile was built once for this module (attention_bias_tiles): copy it
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.bias_tiles + size_t(pair) * size_t(C::BIAS_BYTES));
+        uint4* dst = reinterpret_cast<uint4*>(bias_s);
+#pragma unroll 4
+        for (int i = tid_sm; i < C::BIAS_BYTES / 16; i += kSmThreads) dst[i] = ldg_stream(src + i);
+      } else {
+        build_bias_tile<NPAD, BF16>(p, h, mt, tid_sm, kSmThreads, bias_s);
       }
       if constexpr (MASK == kMaskAnalytic) {
         // Query features of the mask MMA for this query tile, one [128 x 16] tile per axis a:
@@ -902,6 +922,16 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   }
 }
 
+// Prebuilt bias tiles: block `pair` (= h * MT + mt) writes the tile the attention kernel
+// would gather for that (head, query tile), in the same shared-memory image.
+template <int NPAD, bool BF16>
+__global__ void __launch_bounds__(256) bias_tile_kernel(const KParams p, uint8_t* tiles) {
+  const int pair = blockIdx.x;
+  const int h = pair / p.MT, mt = pair - h * p.MT;
+  build_bias_tile<NPAD, BF16>(p, h, mt, threadIdx.x, blockDim.x,
+                              tiles + size_t(pair) * size_t(Cfg<NPAD, 16>::BIAS_BYTES));
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -1015,11 +1045,14 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.B > 0x7fffffff || a.H > 0xffff || a.N > 0xffffff)
     return set_error(kErrInvalid, "B, H or N too large");
   if (!a.q || !a.k || !a.v || !a.out) return set_error(kErrInvalid, "null tensor pointer");
-  if (a.bias_from_table ? (!a.table || !a.index) : !a.bias)
+  const bool gather = a.bias_from_table && !a.bias_tiles;
+  if (a.bias_tiles ? false : (a.bias_from_table ? (!a.table || !a.index) : !a.bias))
     return set_error(kErrInvalid, "null bias pointer");
-  if (a.bias_from_table && a.index_stride < a.N)
+  if (a.bias_tiles && (reinterpret_cast<uintptr_t>(a.bias_tiles) & 15u))
+    return set_error(kErrInvalid, "bias tiles must be 16-byte aligned");
+  if (gather && a.index_stride < a.N)
     return set_error(kErrInvalid, "relative position index is smaller than N x N");
-  if (a.bias_from_table && a.table_rows < 1)
+  if (gather && a.table_rows < 1)
     return set_error(kErrInvalid, "relative position bias table has no rows");
   if (a.mask && a.mask_windows < 1) return set_error(kErrInvalid, "mask_windows must be >= 1");
   if (a.analytic) {
@@ -1038,7 +1071,13 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
       aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
       (a.qkv_stride_n | a.qkv_stride_h | a.qkv_stride_b) % 8 == 0 &&
       (a.out_stride_n | a.out_stride_h | a.out_stride_b) % 8 == 0;
-  if (!tensor_path) return launch_window_attention_simt(a, stream);
+  if (!tensor_path) {
+    if (a.bias_tiles)
+      return set_error(kErrUnsupported,
+                       "prebuilt bias tiles apply to fp16 / bf16 head_dim 16 or 32 windows of at "
+                       "most 352 tokens with 16-byte aligned tensors");
+    return launch_window_attention_simt(a, stream);
+  }
 
   const int n32 = int((a.N + 31) / 32) * 32;
   const int npad = n32 <= 64 ? 64 : n32 <= 128 ? 128 : n32 <= 224 ? 224 : 352;
@@ -1060,6 +1099,7 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   kp.index = reinterpret_cast<const long long*>(a.index);
   kp.index_stride = int(a.index_stride);
   kp.table_rows = a.table_rows;
+  kp.bias_tiles = static_cast<const uint8_t*>(a.bias_tiles);
   kp.bias_from_table = a.bias_from_table ? 1 : 0;
   kp.table_f32 = a.table_f32 ? 1 : 0;
   kp.mask = static_cast<const uint16_t*>(a.mask);
@@ -1095,6 +1135,62 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream) {
   if (n32 <= 128) return dispatch_npad<128>(a, tq, tk, tv, kp, stream);
   if (n32 <= 224) return dispatch_npad<224>(a, tq, tk, tv, kp, stream);
   return dispatch_npad<352>(a, tq, tk, tv, kp, stream);
+}
+
+namespace {
+int npad_for(int64_t N) {
+  const int64_t n32 = (N + 31) / 32 * 32;
+  return n32 <= 64 ? 64 : n32 <= 128 ? 128 : n32 <= 224 ? 224 : 352;
+}
+int64_t bias_tile_bytes(int npad) { return int64_t(npad / 8) * (kBM / 8) * 128 * 2; }
+template <int NPAD>
+int launch_bias_tiles_npad(uint8_t* tiles, const KParams& kp, int dtype, cudaStream_t stream) {
+  if (dtype == kBF16)
+    bias_tile_kernel<NPAD, true><<<kp.P, 256, 0, stream>>>(kp, tiles);
+  else
+    bias_tile_kernel<NPAD, false><<<kp.P, 256, 0, stream>>>(kp, tiles);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "bias tile launch");
+  return kOk;
+}
+}  // namespace
+
+int64_t attention_bias_tiles_bytes(int64_t H, int64_t N) {
+  if (H < 1 || N < 1 || N > 352) return 0;
+  return H * ((N + kBM - 1) / kBM) * bias_tile_bytes(npad_for(N));
+}
+
+int launch_attention_bias_tiles(void* tiles, const AttnArgs& a, cudaStream_t stream) {
+  if (a.dtype != kF16 && a.dtype != kBF16)
+    return set_error(kErrUnsupported, "bias tiles are built for float16 or bfloat16");
+  if (a.N < 1 || a.N > 352 || a.H < 1 || a.H > 0xffff)
+    return set_error(kErrUnsupported, "bias tiles need 1 <= N <= 352 and 1 <= H");
+  if (!(a.scale > 0.f) || !(a.scale < 1e30f))
+    return set_error(kErrUnsupported, "bias tiles need a finite scale > 0");
+  if (!tiles || !a.table || !a.index) return set_error(kErrInvalid, "null tensor pointer");
+  if (reinterpret_cast<uintptr_t>(tiles) & 15u)
+    return set_error(kErrInvalid, "bias tiles must be 16-byte aligned");
+  if (a.index_stride < a.N) return set_error(kErrInvalid, "relative position index is smaller than N x N");
+  if (a.table_rows < 1) return set_error(kErrInvalid, "relative position bias table has no rows");
+  KParams kp{};
+  kp.table = a.table;
+  kp.table_f32 = a.table_f32 ? 1 : 0;
+  kp.table_rows = a.table_rows;
+  kp.index = reinterpret_cast<const long long*>(a.index);
+  kp.index_stride = int(a.index_stride);
+  kp.bias_from_table = 1;
+  kp.H = int(a.H);
+  kp.N = int(a.N);
+  kp.MT = int((a.N + kBM - 1) / kBM);
+  kp.P = kp.H * kp.MT;
+  kp.scale = a.scale;
+  uint8_t* t = static_cast<uint8_t*>(tiles);
+  switch (npad_for(a.N)) {
+    case 64: return launch_bias_tiles_npad<64>(t, kp, a.dtype, stream);
+    case 128: return launch_bias_tiles_npad<128>(t, kp, a.dtype, stream);
+    case 224: return launch_bias_tiles_npad<224>(t, kp, a.dtype, stream);
+    default: return launch_bias_tiles_npad<352>(t, kp, a.dtype, stream);
+  }
 }
 
 int read_device_error(bool clear) {

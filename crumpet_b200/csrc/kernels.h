@@ -103,6 +103,7 @@ struct AttnArgs {
   const void* table;       // [T, H] fp32 (table_f32) or the element type
   bool table_f32;
   int64_t table_rows;      // T: index values outside [0, T) are flagged, not read
+  const void* bias_tiles;  // prebuilt bias tiles (attention_bias_tiles) or nullptr
   const int64_t* index;    // [>=N, index_stride] relative position index, sliced [:N, :N]
   int64_t index_stride;
   const void* mask;        // [mask_windows, N, N] contiguous or nullptr
@@ -118,6 +119,12 @@ struct AttnArgs {
 };
 
 int launch_window_attention(const AttnArgs& a, cudaStream_t stream);
+
+// Prebuilt bias tiles for the tensor-core attention kernel: the per-(head, query tile)
+// bias operand images it would otherwise gather from table + index in every CTA
+// (reads table, table_f32, table_rows, index, index_stride, H, N, scale, dtype).
+int64_t attention_bias_tiles_bytes(int64_t H, int64_t N);
+int launch_attention_bias_tiles(void* tiles, const AttnArgs& a, cudaStream_t stream);
 
 // The fp32 SIMT attention kernel (attention_simt.cu) for what the tensor-core kernel does
 // not take: float32 q/k/v, head_dim 64..256, N > 384, unaligned operands.  Arguments are

@@ -210,6 +210,59 @@ void swin_window_attention_qkv(at::Tensor& out, const at::Tensor& qkv, const at:
       shift_size[2], dtype_code(qkv), B, H, N, Dh, static_cast<float>(scale), cur_stream(qkv)));
 }
 
+void attention_bias_tiles(at::Tensor& tiles, const at::Tensor& table, const at::Tensor& index,
+                          int64_t N, double scale, at::ScalarType dtype) {
+  check_cuda_contig(tiles, "tiles");
+  check_cuda_contig(table, "relative_position_bias_table");
+  check_cuda_contig(index, "relative_position_index");
+  same_device(tiles, table, "relative_position_bias_table");
+  same_device(tiles, index, "relative_position_index");
+  TORCH_CHECK(tiles.scalar_type() == at::kByte, "tiles must be a uint8 tensor");
+  TORCH_CHECK(table.dim() == 2, "relative_position_bias_table must be [T, H]");
+  TORCH_CHECK(dtype == at::kHalf || dtype == at::kBFloat16, "bias tiles are float16 or bfloat16");
+  TORCH_CHECK(table.scalar_type() == at::kFloat || table.scalar_type() == dtype,
+              "relative_position_bias_table must be float32 or the tiles' dtype");
+  TORCH_CHECK(index.scalar_type() == at::kLong && index.dim() == 2 && index.size(0) >= N &&
+                  index.size(1) >= N,
+              "relative_position_index must be int64 [>=N, >=N]");
+  const int64_t H = table.size(1);
+  TORCH_CHECK(tiles.numel() == crumpet_attention_bias_tiles_bytes(H, N),
+              "tiles must hold crumpet_attention_bias_tiles_bytes(H, N) bytes");
+  const c10::cuda::CUDAGuard guard(tiles.device());
+  const int code = dtype == at::kHalf ? CRUMPET_DTYPE_F16 : CRUMPET_DTYPE_BF16;
+  check_rc(crumpet_attention_bias_tiles(tiles.data_ptr(), table.data_ptr(),
+                                        table.scalar_type() == at::kFloat ? 1 : 0, table.size(0),
+                                        index.data_ptr<int64_t>(), index.size(1), code, H, N,
+                                        static_cast<float>(scale), cur_stream(tiles)));
+}
+
+void swin_window_attention_qkv_tiles(at::Tensor& out, const at::Tensor& qkv,
+                                     const at::Tensor& tiles, at::IntArrayRef num_windows,
+                                     at::IntArrayRef window_size, at::IntArrayRef shift_size,
+                                     double scale) {
+  check_cuda_contig(out, "out");
+  check_cuda_contig(qkv, "qkv");
+  check_cuda_contig(tiles, "bias_tiles");
+  TORCH_CHECK(qkv.dim() == 5 && qkv.size(2) == 3, "qkv must have shape [B, N, 3, H, head_dim]");
+  const int64_t B = qkv.size(0), N = qkv.size(1), H = qkv.size(3), Dh = qkv.size(4);
+  TORCH_CHECK(out.dim() == 3 && out.size(0) == B && out.size(1) == N && out.size(2) == H * Dh,
+              "out must have shape [B, N, H * head_dim]");
+  TORCH_CHECK(out.scalar_type() == qkv.scalar_type(), "out and qkv dtypes differ");
+  TORCH_CHECK(tiles.scalar_type() == at::kByte &&
+                  tiles.numel() == crumpet_attention_bias_tiles_bytes(H, N),
+              "bias_tiles must be the uint8 tiles built for these H and N");
+  TORCH_CHECK(num_windows.size() == 3 && window_size.size() == 3 && shift_size.size() == 3,
+              "num_windows, window_size and shift_size take three values");
+  same_device(qkv, out, "out");
+  same_device(qkv, tiles, "bias_tiles");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  check_rc(crumpet_swin_window_attention_qkv_tiles(
+      out.data_ptr(), qkv.data_ptr(), tiles.data_ptr(), num_windows[0], num_windows[1],
+      num_windows[2], window_size[0], window_size[1], window_size[2], shift_size[0],
+      shift_size[1], shift_size[2], dtype_code(qkv), B, H, N, Dh, static_cast<float>(scale),
+      cur_stream(qkv)));
+}
+
 int64_t ceil_to(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 void norm_shift_partition_3d(at::Tensor& output, const at::Tensor& x, const at::Tensor& weight,
@@ -512,6 +565,14 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "Tensor? mask, Tensor? boundary, float scale) -> ()",
       kTags);
   ops.def(
+      "attention_bias_tiles(Tensor! tiles, Tensor table, Tensor index, int N, float scale, "
+      "ScalarType dtype) -> ()",
+      kTags);
+  ops.def(
+      "swin_window_attention_qkv_tiles(Tensor! out, Tensor qkv, Tensor bias_tiles, "
+      "int[] num_windows, int[] window_size, int[] shift_size, float scale) -> ()",
+      kTags);
+  ops.def(
       "swin_window_attention_qkv(Tensor! out, Tensor qkv, Tensor table, Tensor index, "
       "int[] num_windows, int[] window_size, int[] shift_size, float scale) -> ()",
       kTags);
@@ -555,6 +616,8 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("fused_unshift_unpartition_3d_backward", &fused_unshift_unpartition_3d_backward);
   ops.impl("fused_swin_attention", &fused_swin_attention);
   ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
+  ops.impl("attention_bias_tiles", &attention_bias_tiles);
+  ops.impl("swin_window_attention_qkv_tiles", &swin_window_attention_qkv_tiles);
   ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
   ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);

@@ -98,6 +98,34 @@ def fused_swin_attention(
     return out
 
 
+def tensor_core_attention(dtype: torch.dtype, N: int, head_dim: int) -> bool:
+    """Whether the tcgen05 kernel runs these windows (else the fp32 SIMT kernel)."""
+    return dtype in (torch.float16, torch.bfloat16) and head_dim in (16, 32) and 1 <= N <= 352
+
+
+def attention_bias_tiles(relative_position_bias_table: torch.Tensor,
+                         relative_position_index: torch.Tensor, N: int, scale: float,
+                         dtype: torch.dtype) -> torch.Tensor:
+    """The tensor-core kernel's relative-position bias operands for windows of N tokens,
+    built once: one tile per (head, 128-row query tile), gathered from
+    ``table[index[:N, :N]]`` and divided by ``scale`` in ``dtype``.  Pass the result as
+    ``bias_tiles`` to :func:`swin_window_attention_qkv` with the same N, scale and dtype;
+    rebuild it when the table changes."""
+    table = relative_position_bias_table.detach()
+    if table.dtype not in (torch.float32, dtype):
+        table = table.float()
+    H = int(table.shape[1])
+    nbytes = int(_native.capi().crumpet_attention_bias_tiles_bytes(H, int(N)))
+    if nbytes <= 0 or dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("bias tiles exist for float16 / bfloat16 windows of 1 to 352 tokens")
+    tiles = torch.empty(nbytes, dtype=torch.uint8, device=table.device)
+    _native.require().attention_bias_tiles(tiles, table.contiguous(),
+                                           relative_position_index.contiguous(), int(N),
+                                           float(scale), dtype)
+    _prof.count("attention_bias_tiles")
+    return tiles
+
+
 def swin_window_attention_qkv(
     qkv: torch.Tensor,
     relative_position_bias_table: torch.Tensor,
@@ -106,6 +134,7 @@ def swin_window_attention_qkv(
     window_size=None,
     shift_size=(0, 0, 0),
     scale: float | None = None,
+    bias_tiles: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Window attention straight from the packed qkv Linear output.
 
@@ -117,6 +146,8 @@ def swin_window_attention_qkv(
     is ``b % prod(num_windows)``).  This is the whole body of MONAI's
     ``WindowAttention.forward`` between its two Linears
     (torch-ext/crumpet/monai_patch.py:152-196 does the same with eager glue).
+    ``bias_tiles`` (from :func:`attention_bias_tiles`, tensor-core windows only) replaces
+    the per-CTA gather with a copy of the prebuilt operands.
     """
     if not qkv.is_cuda:
         raise RuntimeError("swin_window_attention_qkv runs on CUDA tensors only")
@@ -150,15 +181,20 @@ def swin_window_attention_qkv(
             "flops": 4 * B * H * N * N * D,
             "exps": B * H * N * N,
         })
-    ops.swin_window_attention_qkv(out, qkv.contiguous(), table.contiguous(),
-                                  relative_position_index.contiguous(), list(num_windows),
-                                  list(window_size), list(shift_size), float(scale))
+    if bias_tiles is not None and tensor_core_attention(qkv.dtype, N, D):
+        ops.swin_window_attention_qkv_tiles(out, qkv.contiguous(), bias_tiles, list(num_windows),
+                                            list(window_size), list(shift_size), float(scale))
+    else:
+        ops.swin_window_attention_qkv(out, qkv.contiguous(), table.contiguous(),
+                                      relative_position_index.contiguous(), list(num_windows),
+                                      list(window_size), list(shift_size), float(scale))
     _prof.count("swin_window_attention_qkv")
     _prof.kernel_end(token)
     return out
 
 
-__all__ = ["fused_swin_attention", "swin_window_attention_qkv", "head_dim_supported"]
+__all__ = ["fused_swin_attention", "swin_window_attention_qkv", "attention_bias_tiles",
+           "head_dim_supported", "tensor_core_attention"]
 
 
 def window_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:

@@ -71,9 +71,11 @@ from .block_fusion import (
     unshift_unpartition_crop_norm_3d,
 )
 from .fused_attention import (
+    attention_bias_tiles,
     fused_swin_attention,
     head_dim_supported,
     swin_window_attention_qkv,
+    tensor_core_attention,
     window_linear,
     window_linear_supported,
 )
@@ -260,6 +262,26 @@ def _linear(mod, x: torch.Tensor) -> torch.Tensor:
     return mod(x)
 
 
+_TILES_ATTR = "_crumpet_bias_tiles"
+
+
+def _bias_tiles(attn, n: int, head_dim: int, dtype: torch.dtype):
+    """The module's prebuilt bias operands for windows of n tokens (see
+    ``attention_bias_tiles``), cached on the module and rebuilt when the table or index
+    tensor, its in-place version, n, the dtype or the scale changes; None where the
+    tensor-core kernel does not run these windows (it then gathers the bias itself)."""
+    if not tensor_core_attention(dtype, n, head_dim):
+        return None
+    table, index = attn.relative_position_bias_table, attn.relative_position_index
+    key = (table.data_ptr(), table._version, index.data_ptr(), index._version, n, dtype,
+           float(attn.scale), table.device)
+    cached = getattr(attn, _TILES_ATTR, None)
+    if cached is None or cached[0] != key:
+        cached = (key, attention_bias_tiles(table, index, n, attn.scale, dtype))
+        object.__setattr__(attn, _TILES_ATTR, cached)
+    return cached[1]
+
+
 def _patched_window_attention_forward(original):
     @functools.wraps(original)
     def forward(self, x, mask):
@@ -283,7 +305,8 @@ def _patched_window_attention_forward(original):
             num_windows, window_size, shift_size = geometry or ((1, 1, 1), (n, 1, 1), (0, 0, 0))
             out = swin_window_attention_qkv(
                 qkv.view(b, n, 3, heads, head_dim), self.relative_position_bias_table,
-                self.relative_position_index, num_windows, window_size, shift_size, self.scale)
+                self.relative_position_index, num_windows, window_size, shift_size, self.scale,
+                bias_tiles=_bias_tiles(self, n, head_dim, qkv.dtype))
             return self.proj_drop(_linear(self.proj, out))
         # A mask from elsewhere: dense mask path.
         qkv = qkv.reshape(b, n, 3, heads, head_dim).permute(2, 0, 3, 1, 4)

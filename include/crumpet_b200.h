@@ -160,6 +160,35 @@ CRUMPET_API int crumpet_swin_window_attention_qkv(
     int64_t N, int64_t head_dim, float scale, void* stream);
 
 /*
+ * Prebuilt relative-position bias operands for the attention kernel.  The tensor-core
+ * kernel adds the bias through the tensor cores from a per-(head, query tile) operand
+ * image in shared memory, which crumpet_swin_window_attention_qkv gathers from the
+ * table and index in every CTA.  With eval weights fixed, a caller can build the
+ * images once (they depend on table, index, N, H, dtype and scale only) and pass them
+ * to crumpet_swin_window_attention_qkv_tiles, whose CTAs then copy them in.
+ *   crumpet_attention_bias_tiles_bytes: the buffer size for H heads and windows of N
+ *     tokens, 0 when 1 <= N <= 352 does not hold (the tensor-core kernel's domain).
+ *   crumpet_attention_bias_tiles: builds them into `tiles` (16-byte aligned, that many
+ *     bytes); table, index and their checks as for crumpet_swin_window_attention_qkv
+ *     (index values outside [0, table_rows) set bit 2 of crumpet_device_status).
+ *   crumpet_swin_window_attention_qkv_tiles: crumpet_swin_window_attention_qkv with the
+ *     bias from tiles built for the same H, N, dtype and scale (not checked: tiles of
+ *     other parameters give wrong outputs).  dtype F16 or BF16, head_dim 16 or 32,
+ *     N <= 352, 16-byte aligned tensors; other calls return CRUMPET_ERR_UNSUPPORTED.
+ * No reference counterpart: the reference re-gathers the bias with torch on every
+ * call (torch-ext/crumpet/monai_patch.py:160-162).
+ */
+CRUMPET_API int64_t crumpet_attention_bias_tiles_bytes(int64_t H, int64_t N);
+CRUMPET_API int crumpet_attention_bias_tiles(void* tiles, const void* bias_table, int table_f32,
+                                             int64_t table_rows, const int64_t* rel_index,
+                                             int64_t index_stride, int dtype, int64_t H,
+                                             int64_t N, float scale, void* stream);
+CRUMPET_API int crumpet_swin_window_attention_qkv_tiles(
+    void* out, const void* qkv, const void* bias_tiles, int64_t nw_d, int64_t nw_h, int64_t nw_w,
+    int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w, int dtype,
+    int64_t B, int64_t H, int64_t N, int64_t head_dim, float scale, void* stream);
+
+/*
  * LayerNorm, zero padding, cyclic roll by -ss and window partition in one pass:
  * the first half of a Swin block's attention branch.
  *   x      [B, D, H, W, C]  (in_dtype), any D/H/W (not window multiples)

@@ -161,3 +161,72 @@ def test_out_of_range_index_is_flagged_not_read(cuda_device):
     # the same call with the valid index leaves the word clear
     swin_window_attention_qkv(qkv, table, index, nw, ws, ss, 0.25)
     crumpet.check_device_status()
+
+
+TILE_CASES = [c for c in CASES if c[7] != "float32" and c[0] != "shift_n64_h2"] + [
+    ("stage2_n343_h12_b8", (14, 14, 14), (7, 7, 7), (3, 3, 3), 12, 8, (7, 7, 7), "float16"),
+]
+
+
+@pytest.mark.parametrize("case", TILE_CASES, ids=[c[0] for c in TILE_CASES])
+def test_prebuilt_bias_tiles_equal_the_gather(case, cuda_device):
+    """The per-module bias operands built once give bit-identical outputs to the per-CTA
+    gather (same operand image, same kernel arithmetic)."""
+    from crumpet_b200.fused_attention import attention_bias_tiles
+
+    (qkv, table, index, nw, ws, ss), _ = make_case(case, cuda_device)
+    B, N, _, H, D = qkv.shape
+    scale = D ** -0.5
+    tiles = attention_bias_tiles(table, index, N, scale, qkv.dtype)
+    gathered = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, scale)
+    tiled = swin_window_attention_qkv(qkv, table, index, nw, ws, ss, scale, bias_tiles=tiles)
+    torch.cuda.synchronize()
+    assert torch.equal(tiled, gathered)
+    # through the C ABI
+    out = torch.empty_like(tiled)
+    rc = _ops.capi().crumpet_swin_window_attention_qkv_tiles(
+        ptr(out), ptr(qkv), ptr(tiles), *nw, *ws, *ss, DTYPE_CODE[qkv.dtype], B, H, N, D, scale,
+        stream_ptr())
+    assert rc == 0, _ops.last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(out, gathered)
+    assert _ops.capi().crumpet_device_status(1) == 0
+
+
+def test_bias_tile_cache_follows_the_table(cuda_device):
+    """The patched WindowAttention caches its bias tiles and rebuilds them when the
+    table changes in place (as load_state_dict does)."""
+    import crumpet_b200 as crumpet
+    from crumpet_b200 import monai_patch, swin_unetr
+
+    torch.manual_seed(0)
+    attn = swin_unetr.WindowAttention(48, 3, (7, 7, 7), qkv_bias=True).to(cuda_device).eval()
+    x = torch.randn((8, 343, 48), device=cuda_device).half()
+    crumpet.patch_monai_swin_unetr(swin_unetr)
+    try:
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.float16):
+            first = attn(x, None)
+            tiles = getattr(attn, monai_patch._TILES_ATTR)[1]
+            again = attn(x, None)
+            assert getattr(attn, monai_patch._TILES_ATTR)[1] is tiles  # reused
+            attn.relative_position_bias_table.add_(0.5)
+            changed = attn(x, None)
+            assert getattr(attn, monai_patch._TILES_ATTR)[1] is not tiles
+    finally:
+        crumpet.unpatch_monai_swin_unetr()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.float16):
+        eager = attn(x, None)
+    assert torch.equal(first, again)
+    assert not torch.equal(first, changed)
+    assert (changed.float() - eager.float()).abs().max().item() < 2e-2
+
+
+def test_bias_tiles_reject_the_simt_domain(cuda_device):
+    from crumpet_b200.fused_attention import attention_bias_tiles
+
+    table = torch.randn((13 ** 3, 2), device=cuda_device)
+    index = torch.from_numpy(OA.relative_position_index((7, 7, 7))).long().to(cuda_device)
+    with pytest.raises(ValueError, match="352"):
+        attention_bias_tiles(table, index, 512, 0.25, torch.float16)
+    with pytest.raises(ValueError):
+        attention_bias_tiles(table, index, 343, 0.25, torch.float32)
