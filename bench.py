@@ -111,13 +111,24 @@ class ClockSampler:
         self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
 
     def __enter__(self):
+        if not self.gpu_ids:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={','.join(str(i) for i in self.gpu_ids)}",
-                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: a timed region shorter than a second (a few
+        # multi-GPU steps) would otherwise end before its first sample
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.tmp.flush()
+            if Path(self.tmp.name).stat().st_size > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):

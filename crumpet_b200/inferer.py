@@ -154,9 +154,22 @@ class SlidingWindowInferer:
 
     def my_batches(self, spatial) -> list[list[tuple[int, int, int]]]:
         """This rank's ROI batches: a contiguous range of the ROI grid (ranks differ by at
-        most one ROI, and a batch's ROIs stay spatially adjacent), cut into sw_batch."""
+        most one ROI, and a batch's ROIs stay spatially adjacent), cut into the fewest
+        batches of at most sw_batch ROIs, as equal in size as possible (50 ROIs in batches
+        of 8 run as 8 + 6 x 7 rather than 6 x 8 + 2: a two-ROI batch leaves the GPU idle
+        for much of its forward).  The ROI order, and so the order of the additions into
+        each voxel, does not depend on where the batches are cut."""
         mine = list(self.plan(spatial)[self.rank].rois)
-        return [mine[i:i + self.sw_batch] for i in range(0, len(mine), self.sw_batch)]
+        if not mine:
+            return []
+        count = -(-len(mine) // self.sw_batch)
+        small, extra = divmod(len(mine), count)
+        out, i = [], 0
+        for k in range(count):
+            size = small + (1 if k < extra else 0)
+            out.append(mine[i:i + size])
+            i += size
+        return out
 
     def _count_map(self, spatial, device) -> torch.Tensor:
         key = (tuple(spatial), device)

@@ -75,15 +75,17 @@ def test_sliding_window_patched_vs_eager(cuda_device):
 def test_sliding_window_cuda_graphs_match_eager_bit_for_bit(cuda_device):
     """CUDA-graph mode replays the same kernels on the same data: logits and labels equal
     the eager patched run's exactly, over two volumes in a row (the second replays the
-    graphs captured for the first) and a ragged last batch (6 ROIs in batches of 4: a
-    second graph for batches of 2), and each replay counts its crumpet_b200 launches."""
+    graphs captured for the first) and unequal batches (10 ROIs in batches of at most 4
+    run as 4 + 3 + 3: a graph per batch size), and each replay counts its crumpet_b200
+    launches."""
     torch.manual_seed(0)
     model = swin_unetr.SwinUNETR(1, 14, 48).to(cuda_device).eval()
-    vols = [torch.rand((1, 1, 96, 144, 160), device=cuda_device) for _ in range(2)]
+    vols = [torch.rand((1, 1, 96, 144, 288), device=cuda_device) for _ in range(2)]
     eager = SlidingWindowInferer(model, (96, 96, 96), 4, 0.5, 14, torch.float16)
     graphed = SlidingWindowInferer(model, (96, 96, 96), 4, 0.5, 14, torch.float16,
                                    cuda_graphs=True)
-    assert len(graphed.rois((96, 144, 160))) == 6
+    assert len(graphed.rois((96, 144, 288))) == 10
+    assert [len(b) for b in graphed.my_batches((96, 144, 288))] == [4, 3, 3]
     crumpet.patch_monai_swin_unetr(swin_unetr)
     try:
         for vol in vols:
@@ -94,9 +96,9 @@ def test_sliding_window_cuda_graphs_match_eager_bit_for_bit(cuda_device):
             got_seg = graphed.segment(vol)
             assert torch.equal(got_logits, want_logits)
             assert torch.equal(got_seg, want_seg)
-            # 8 attention launches per forward, one forward per batch of 4 and of 2
-            assert n1 - n0 == 2 * 8
-        assert sorted(k[0] for k in graphed._graphs) == [2, 4]
+            # 8 attention launches per forward, one forward per batch
+            assert n1 - n0 == 3 * 8
+        assert sorted(k[0] for k in graphed._graphs) == [3, 4]
     finally:
         crumpet.unpatch_monai_swin_unetr()
     # unpatched: the captured graphs still hold the patched forward until reset

@@ -121,6 +121,10 @@ def test_roi_sharding_partitions_the_batches(world):
     assert seen == roi_grid((512, 512, 224), (96,) * 3, 0.5)
     assert max(map(len, per_rank)) - min(map(len, per_rank)) <= 1
     assert all(len(b) <= 8 for i in inf for b in i.my_batches((512, 512, 224)))
+    # the fewest batches, as equal as possible (no two-ROI tail batch at 8 ranks)
+    for i in inf:
+        sizes = [len(b) for b in i.my_batches((512, 512, 224))]
+        assert len(sizes) == -(-sum(sizes) // 8) and max(sizes) - min(sizes) <= 1
 
 
 def test_sliding_window_eager_cpu_matches_single_forward():
