@@ -184,28 +184,33 @@ __device__ __forceinline__ float2 token_stats(const float (&v)[G][8], uint32_t v
   return make_float2(mean, rsqrtf(group_sum<L>(q.x + q.y) * inv_c + eps));
 }
 
-// y = (v - mean) * rstd * gamma + beta for one 8-channel group, in packed pairs
-// (each lane of a pair rounds exactly as the scalar expression would).
-__device__ __forceinline__ void normalize8(const float (&v)[8], float2 st,
-                                           const float* __restrict__ gamma8,
-                                           const float* __restrict__ beta8, float (&y)[8]) {
-  const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma8));
-  const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma8) + 1);
-  const float4 ba = __ldg(reinterpret_cast<const float4*>(beta8));
-  const float4 bb = __ldg(reinterpret_cast<const float4*>(beta8) + 1);
-  const float2 gm[4] = {make_float2(ga.x, ga.y), make_float2(ga.z, ga.w), make_float2(gb.x, gb.y),
-                        make_float2(gb.z, gb.w)};
-  const float2 bt[4] = {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
-                        make_float2(bb.z, bb.w)};
-  const float2 nm = make_float2(-st.x, -st.x), rs = make_float2(st.y, st.y);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __fmul2_rn(__fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), nm), rs);
-    const float2 r = __ffma2_rn(t, gm[i], bt[i]);
-    y[2 * i] = r.x;
-    y[2 * i + 1] = r.y;
+// gamma and beta of one 8-channel group, loaded once and applied to several tokens:
+// y = (v - mean) * rstd * gamma + beta in packed pairs (each lane of a pair rounds
+// exactly as the scalar expression would).
+struct Affine8 {
+  float2 gm[4], bt[4];
+  static __device__ __forceinline__ Affine8 load(const float* __restrict__ gamma8,
+                                                 const float* __restrict__ beta8) {
+    const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma8));
+    const float4 gb = __ldg(reinterpret_cast<const float4*>(gamma8) + 1);
+    const float4 ba = __ldg(reinterpret_cast<const float4*>(beta8));
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(beta8) + 1);
+    return Affine8{{make_float2(ga.x, ga.y), make_float2(ga.z, ga.w), make_float2(gb.x, gb.y),
+                    make_float2(gb.z, gb.w)},
+                   {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
+                    make_float2(bb.z, bb.w)}};
   }
-}
+  __device__ __forceinline__ void apply(const float (&v)[8], float2 st, float (&y)[8]) const {
+    const float2 nm = make_float2(-st.x, -st.x), rs = make_float2(st.y, st.y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __fmul2_rn(__fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), nm), rs);
+      const float2 r = __ffma2_rn(t, gm[i], bt[i]);
+      y[2 * i] = r.x;
+      y[2 * i + 1] = r.y;
+    }
+  }
+};
 
 // The index math of a lane group's NT tokens (first + j * stride) is
 // done once per token -- by lane j of the group for token j -- and broadcast to the
@@ -260,6 +265,8 @@ norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
     }
   }
   const float inv_c = 1.f / float(g.C);
+  // one token at a time: keeping a second token's fp32 values live for a shared gamma /
+  // beta load costs registers (80 instead of 64) and resident blocks, and is slower here
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
     const uint32_t token = first + j * kGroups;
@@ -282,7 +289,7 @@ norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
       if (grp >= g.groups) continue;
       float y[8];
       if (inside[j]) {
-        normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
+        Affine8::load(gamma + grp * 8, beta + grp * 8).apply(v[k], st, y);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = 0.f;  // F.pad after the norm: zeros
@@ -420,35 +427,40 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
     }
   }
   const float inv_c = 1.f / float(g.C);
+  float v[kTokensPerGroup][kGroupsPerLane][8];
+  float2 st[kTokensPerGroup];
 #pragma unroll
   for (int j = 0; j < kTokensPerGroup; ++j) {
     const uint32_t token = first + j * kGroups;
-    float v[kGroupsPerLane][8];
     uint32_t valid = 0;
 #pragma unroll
     for (int k = 0; k < kGroupsPerLane; ++k) {
       const uint32_t grp = sub + k * L;
       if (live[j] && grp < g.groups) {
-        Io<T>::to_float(rw[j][k], v[k]);
+        Io<T>::to_float(rw[j][k], v[j][k]);
         if (residual) {
           float r[8];
           Io<T>::to_float(rr[j][k], r);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[k][e] = round_to<T>(r[e] + v[k][e]);
+          for (int e = 0; e < 8; ++e) v[j][k][e] = round_to<T>(r[e] + v[j][k][e]);
         }
-        Io<T>::store8(out + uint64_t(token) * g.C + grp * 8, v[k]);
+        Io<T>::store8(out + uint64_t(token) * g.C + grp * 8, v[j][k]);
         valid |= 1u << k;
       }
     }
-    const float2 st = token_stats<L>(v, valid, inv_c, g.eps);
-    if (!live[j]) continue;
+    st[j] = token_stats<L>(v[j], valid, inv_c, g.eps);
+  }
 #pragma unroll
-    for (int k = 0; k < kGroupsPerLane; ++k) {
-      const uint32_t grp = sub + k * L;
-      if (grp >= g.groups) continue;
+  for (int k = 0; k < kGroupsPerLane; ++k) {
+    const uint32_t grp = sub + k * L;
+    if (grp >= g.groups) continue;
+    const Affine8 ab = Affine8::load(gamma + grp * 8, beta + grp * 8);
+#pragma unroll
+    for (int j = 0; j < kTokensPerGroup; ++j) {
+      if (!live[j]) continue;
       float y[8];
-      normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
-      Io<TN>::store8(normed + uint64_t(token) * g.C + grp * 8, y);
+      ab.apply(v[j][k], st[j], y);
+      Io<TN>::store8(normed + uint64_t(first + j * kGroups) * g.C + grp * 8, y);
     }
   }
 }
@@ -514,31 +526,34 @@ patch_merge_norm_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
     }
   }
   const float inv_c = 1.f / float(8 * g.C);
+  float v[NT][G][8];
+  float2 st[NT];
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
-    const uint32_t token = first + j * kGroups;
-    float v[G][8];
     uint32_t valid = 0;
 #pragma unroll
     for (int k = 0; k < G; ++k) {
       if ((inb[j] >> k) & 1u) {
-        Io<TIn>::to_float(raw[j][k], v[k]);
+        Io<TIn>::to_float(raw[j][k], v[j][k]);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[k][e] = 0.f;  // padding rows (and unused groups)
+        for (int e = 0; e < 8; ++e) v[j][k][e] = 0.f;  // padding rows (and unused groups)
       }
       if (sub + k * L < g.groups) valid |= 1u << k;
     }
-    const float2 st = token_stats<L>(v, valid, inv_c, g.eps);
-    if (!live[j]) continue;
-    TOut* dst = out + uint64_t(token) * (8 * g.C);
+    st[j] = token_stats<L>(v[j], valid, inv_c, g.eps);
+  }
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const uint32_t grp = sub + k * L;
-      if (grp >= g.groups) continue;
+  for (int k = 0; k < G; ++k) {
+    const uint32_t grp = sub + k * L;
+    if (grp >= g.groups) continue;
+    const Affine8 ab = Affine8::load(gamma + grp * 8, beta + grp * 8);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      if (!live[j]) continue;
       float y[8];
-      normalize8(v[k], st, gamma + grp * 8, beta + grp * 8, y);
-      Io<TOut>::store8(dst + grp * 8, y);
+      ab.apply(v[j][k], st[j], y);
+      Io<TOut>::store8(out + uint64_t(first + j * kGroups) * (8 * g.C) + grp * 8, y);
     }
   }
 }
