@@ -99,7 +99,11 @@ def build_model(device):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples during the timed region.
+
+    Every 500 ms: each query stalls the GPUs' work briefly.  On two B200s the timed
+    region ran 6.5 % slower than the same steps without the sampler (the end-to-end
+    region) when sampling every 100 ms, 1.8 % slower at 500 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -116,7 +120,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={','.join(str(i) for i in self.gpu_ids)}",
-                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "100"],
+                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "500"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
