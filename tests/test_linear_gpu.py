@@ -13,10 +13,11 @@ from helpers import DTYPE_CODE, ptr, stream_ptr
 
 pytestmark = pytest.mark.gpu
 
-# (M, K, N): stage-1 qkv at full size (2744 windows x 343 tokens of an 8-ROI batch), stage-1
-# proj with a partial last tile, a single partial tile, stage-2 proj, the largest supported N
-CASES = [(941192, 48, 144), (1000, 48, 48), (77, 48, 144), (5000, 96, 96), (3000, 48, 256),
-         (2048, 96, 160)]
+# (M, K, N): stage-1 qkv and proj at full size (2744 windows x 343 tokens of an 8-ROI batch),
+# stage-1 proj with a partial last tile, a single partial tile, stage-2 proj, the largest
+# supported N, K = 96 at its largest N
+CASES = [(941192, 48, 144), (941192, 48, 48), (1000, 48, 48), (77, 48, 144), (5000, 96, 96),
+         (3000, 48, 256), (2048, 96, 160)]
 IDS = [f"M{m}_K{k}_N{n}" for m, k, n in CASES]
 
 
