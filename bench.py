@@ -99,11 +99,11 @@ def build_model(device):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region.
+    """nvidia-smi clock / throttle-reason samples during the timed region, every 200 ms.
 
-    Every 500 ms: each query stalls the GPUs' work briefly.  On two B200s the timed
-    region ran 6.5 % slower than the same steps without the sampler (the end-to-end
-    region) when sampling every 100 ms, 1.8 % slower at 500 ms."""
+    On two B200s the same steps ran 882-885 ms with and without a sampler (every GPU from
+    one process, each rank its own GPU, NVML from a thread, 500 or 2000 ms): sampling does
+    not slow the timed work."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -120,7 +120,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={','.join(str(i) for i in self.gpu_ids)}",
-                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "500"],
+                 f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=self.tmp, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -706,9 +706,11 @@ def main() -> None:
 
     # ---- timed region 1: volume resident in HBM
     launches0 = profiling.total_launches()
-    barrier()
-    torch.cuda.synchronize()
+    # rank 0 starts the sampler (and waits for its first sample) before the barrier, so
+    # every rank's clock starts together
     with ClockSampler(visible_gpu_ids(world) if rank == 0 else []) as clocks:
+        barrier()
+        torch.cuda.synchronize()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
