@@ -200,6 +200,17 @@ struct Affine8 {
                    {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
                     make_float2(bb.z, bb.w)}};
   }
+  // the same from a shared-memory copy of gamma / beta
+  static __device__ __forceinline__ Affine8 load_shared(const float* gamma8, const float* beta8) {
+    const float4 ga = reinterpret_cast<const float4*>(gamma8)[0];
+    const float4 gb = reinterpret_cast<const float4*>(gamma8)[1];
+    const float4 ba = reinterpret_cast<const float4*>(beta8)[0];
+    const float4 bb = reinterpret_cast<const float4*>(beta8)[1];
+    return Affine8{{make_float2(ga.x, ga.y), make_float2(ga.z, ga.w), make_float2(gb.x, gb.y),
+                    make_float2(gb.z, gb.w)},
+                   {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
+                    make_float2(bb.z, bb.w)}};
+  }
   __device__ __forceinline__ void apply(const float (&v)[8], float2 st, float (&y)[8]) const {
     const float2 nm = make_float2(-st.x, -st.x), rs = make_float2(st.y, st.y);
 #pragma unroll
@@ -211,6 +222,21 @@ struct Affine8 {
     }
   }
 };
+
+// gamma and beta of `n` channels copied into shared memory (gb[0..n) and gb[cap..cap+n)) by
+// the whole block: the normalise step then reads them with short-latency shared loads
+// instead of L1 hits on its critical path (norm + partition 32.8 -> 30.3 us, crop + norm2
+// 53.2 -> 52.2 us at stage 1; patch merging, whose blocks cover only 32 tokens of 8C
+// channels, is faster without it).  All threads of the block must call this.
+__device__ __forceinline__ void stage_affine(float* gb, uint32_t cap,
+                                             const float* __restrict__ gamma,
+                                             const float* __restrict__ beta, uint32_t n) {
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    gb[i] = __ldg(gamma + i);
+    gb[cap + i] = __ldg(beta + i);
+  }
+  __syncthreads();
+}
 
 // The index math of a lane group's NT tokens (first + j * stride) is
 // done once per token -- by lane j of the group for token j -- and broadcast to the
@@ -249,6 +275,8 @@ norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
                             const BlockGeom g) {
   constexpr uint32_t kGroups = kThreads / L;  // lane groups per block
   const uint32_t sub = threadIdx.x % L;
+  __shared__ __align__(16) float gb_s[2 * kMaxC];
+  stage_affine(gb_s, kMaxC, gamma, beta, g.C);
   const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
   uint64_t src[kTokensPerGroup];
   bool inside[kTokensPerGroup];
@@ -289,7 +317,7 @@ norm_shift_partition_kernel(TOut* __restrict__ out, const TIn* __restrict__ x,
       if (grp >= g.groups) continue;
       float y[8];
       if (inside[j]) {
-        Affine8::load(gamma + grp * 8, beta + grp * 8).apply(v[k], st, y);
+        Affine8::load_shared(gb_s + grp * 8, gb_s + kMaxC + grp * 8).apply(v[k], st, y);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = 0.f;  // F.pad after the norm: zeros
@@ -390,6 +418,8 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
                          const BlockGeom g) {
   constexpr uint32_t kGroups = kThreads / L;
   const uint32_t sub = threadIdx.x % L;
+  __shared__ __align__(16) float gb_s[2 * kMaxC];
+  stage_affine(gb_s, kMaxC, gamma, beta, g.C);
   const uint32_t first = blockIdx.x * (kGroups * kTokensPerGroup) + threadIdx.x / L;
   uint64_t src[kTokensPerGroup];
   bool live[kTokensPerGroup];
@@ -454,7 +484,7 @@ unshift_crop_norm_kernel(T* __restrict__ out, TN* __restrict__ normed,
   for (int k = 0; k < kGroupsPerLane; ++k) {
     const uint32_t grp = sub + k * L;
     if (grp >= g.groups) continue;
-    const Affine8 ab = Affine8::load(gamma + grp * 8, beta + grp * 8);
+    const Affine8 ab = Affine8::load_shared(gb_s + grp * 8, gb_s + kMaxC + grp * 8);
 #pragma unroll
     for (int j = 0; j < kTokensPerGroup; ++j) {
       if (!live[j]) continue;
