@@ -29,7 +29,7 @@ namespace crumpet {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;  // 256 and 512 measured slower for the LayerNorm kernels
 // LayerNorm kernel work split: a token's C channels are 8-channel groups spread
 // over L lanes (L a power of two, the smallest with L * kGroupsPerLane >= C/8),
 // kGroupsPerLane groups per lane, and each L-lane group normalises
