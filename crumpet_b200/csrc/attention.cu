@@ -1142,7 +1142,9 @@ int npad_for(int64_t N) {
   const int64_t n32 = (N + 31) / 32 * 32;
   return n32 <= 64 ? 64 : n32 <= 128 ? 128 : n32 <= 224 ? 224 : 352;
 }
-int64_t bias_tile_bytes(int npad) { return int64_t(npad / 8) * (kBM / 8) * 128 * 2; }
+// one (head, query tile) tile: NPAD / 8 column groups of kBM / 8 core matrices of 8 x 8
+// 16-bit elements (128 bytes) -- Cfg<NPAD, HD>::BIAS_BYTES, the stride the kernels use
+int64_t bias_tile_bytes(int npad) { return int64_t(npad / 8) * (kBM / 8) * 128; }
 template <int NPAD>
 int launch_bias_tiles_npad(uint8_t* tiles, const KParams& kp, int dtype, cudaStream_t stream) {
   if (dtype == kBF16)
@@ -1154,6 +1156,10 @@ int launch_bias_tiles_npad(uint8_t* tiles, const KParams& kp, int dtype, cudaStr
   return kOk;
 }
 }  // namespace
+
+static_assert(Cfg<352, 16>::BIAS_BYTES == (352 / 8) * (kBM / 8) * 128 &&
+                  Cfg<224, 16>::BIAS_BYTES == (224 / 8) * (kBM / 8) * 128,
+              "bias tile size on the host and in the kernels");
 
 int64_t attention_bias_tiles_bytes(int64_t H, int64_t N) {
   if (H < 1 || N < 1 || N > 352) return 0;
