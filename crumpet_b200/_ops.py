@@ -107,6 +107,9 @@ def capi() -> ctypes.CDLL:
         lib.crumpet_swin_window_attention_qkv_tiles.argtypes = (
             [vp, vp, vp] + [i64] * 9 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
         lib.crumpet_swin_window_attention_qkv_tiles.restype = i32
+        lib.crumpet_swin_window_attention_qkv_static_tiles.argtypes = (
+            [vp, vp, vp, i32, i64, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
+        lib.crumpet_swin_window_attention_qkv_static_tiles.restype = i32
         lib.crumpet_norm_shift_partition_3d.argtypes = (
             [vp, i32, vp, i32, vp, vp, ctypes.c_float] + [i64] * 11 + [vp])
         lib.crumpet_norm_shift_partition_3d.restype = i32

@@ -1199,6 +1199,56 @@ int launch_attention_bias_tiles(void* tiles, const AttnArgs& a, cudaStream_t str
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Bias tiles in a fixed device buffer, for callers that cannot allocate device memory
+// (crumpet_swin_window_attention_qkv_static_tiles).  The buffer is part of the library
+// image: every GPU that loads the library holds kStaticTileBytes until the process exits.
+// Its name is only a host-side stand-in for the device copy, so host code passes the
+// device address, looked up once per device with that device current.
+constexpr size_t kStaticTileBytes = size_t(4) << 20;
+static __device__ __align__(256) uint8_t g_static_bias_tiles[kStaticTileBytes];
+
+namespace {
+constexpr int kMaxStaticDevices = 64;
+
+int static_tiles_address(void** out) {
+  static std::mutex mu;
+  static void* addr[kMaxStaticDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxStaticDevices)
+    return set_error(kErrUnsupported, "static bias tiles: device ordinal above 63");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_bias_tiles);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaGetSymbolAddress(static bias tiles)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return kOk;
+}
+}  // namespace
+
+int launch_window_attention_static_tiles(const AttnArgs& a, cudaStream_t stream) {
+  const int64_t need = attention_bias_tiles_bytes(a.H, a.N);
+  if (need <= 0)
+    return set_error(kErrUnsupported, "static bias tiles need 1 <= N <= 352 and H >= 1");
+  if (uint64_t(need) > kStaticTileBytes)
+    return set_error(kErrUnsupported,
+                     "static bias tiles: H x ceil(N / 128) tiles exceed the 4 MiB buffer "
+                     "(at most 46 tiles at N = 343, 73 at N = 216)");
+  void* tiles = nullptr;
+  if (int rc = static_tiles_address(&tiles)) return rc;
+  // every byte of the `need` bytes the attention kernel reads is rewritten here, so the
+  // previous call's contents never show through
+  if (int rc = launch_attention_bias_tiles(tiles, a, stream)) return rc;
+  AttnArgs t = a;
+  t.bias_tiles = tiles;
+  return launch_window_attention(t, stream);
+}
+
 int read_device_error(bool clear) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;

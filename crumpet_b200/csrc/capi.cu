@@ -200,6 +200,49 @@ int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bi
   return launch_window_attention(a, static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_swin_window_attention_qkv_static_tiles(
+    void* out, const void* qkv, const void* bias_table, int table_f32, int64_t table_rows,
+    const int64_t* rel_index, int64_t index_stride, int64_t nw_d, int64_t nw_h, int64_t nw_w,
+    int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w,
+    int dtype, int64_t B, int64_t H, int64_t N, int64_t head_dim, float scale, void* stream) {
+  AttnArgs a{};
+  const int64_t hd = H * head_dim;
+  const int64_t esize = dtype == kF32 ? 4 : 2;
+  a.q = qkv;
+  a.k = static_cast<const char*>(qkv) + hd * esize;
+  a.v = static_cast<const char*>(qkv) + 2 * hd * esize;
+  a.qkv_stride_n = 3 * hd;
+  a.qkv_stride_h = head_dim;
+  a.qkv_stride_b = N * 3 * hd;
+  a.out = out;
+  a.out_stride_n = hd;
+  a.out_stride_h = head_dim;
+  a.out_stride_b = N * hd;
+  a.bias_from_table = true;
+  a.table = bias_table;
+  a.table_f32 = table_f32 != 0;
+  a.table_rows = table_rows;
+  a.index = rel_index;
+  a.index_stride = index_stride;
+  a.analytic = (ss_d | ss_h | ss_w) != 0;
+  a.nwin[0] = nw_d;
+  a.nwin[1] = nw_h;
+  a.nwin[2] = nw_w;
+  a.win[0] = ws_d;
+  a.win[1] = ws_h;
+  a.win[2] = ws_w;
+  a.shift[0] = ss_d;
+  a.shift[1] = ss_h;
+  a.shift[2] = ss_w;
+  a.B = B;
+  a.H = H;
+  a.N = N;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.dtype = dtype;
+  return launch_window_attention_static_tiles(a, static_cast<cudaStream_t>(stream));
+}
+
 int64_t crumpet_attention_bias_tiles_bytes(int64_t H, int64_t N) {
   return attention_bias_tiles_bytes(H, N);
 }

@@ -125,6 +125,9 @@ int launch_window_attention(const AttnArgs& a, cudaStream_t stream);
 // (reads table, table_f32, table_rows, index, index_stride, H, N, scale, dtype).
 int64_t attention_bias_tiles_bytes(int64_t H, int64_t N);
 int launch_attention_bias_tiles(void* tiles, const AttnArgs& a, cudaStream_t stream);
+// launch_attention_bias_tiles into a fixed 4 MiB device buffer of the library, then the
+// attention with those tiles: no device allocation by anyone.
+int launch_window_attention_static_tiles(const AttnArgs& a, cudaStream_t stream);
 
 // The fp32 SIMT attention kernel (attention_simt.cu) for what the tensor-core kernel does
 // not take: float32 q/k/v, head_dim 64..256, N > 384, unaligned operands.  Arguments are

@@ -189,6 +189,32 @@ CRUMPET_API int crumpet_swin_window_attention_qkv_tiles(
     int64_t B, int64_t H, int64_t N, int64_t head_dim, float scale, void* stream);
 
 /*
+ * crumpet_swin_window_attention_qkv_static_tiles: the packed-qkv window attention
+ * (arguments as crumpet_swin_window_attention_qkv; domain and results as
+ * crumpet_swin_window_attention_qkv_tiles, with the tiles built from table and index
+ * as crumpet_attention_bias_tiles builds them) for a
+ * caller that cannot allocate device memory: one that runs where cudaMalloc is not
+ * allowed or not wanted (an allocator-less runtime, a host that hands over only the
+ * buffers it owns, a path that must not touch the device heap).  It still passes its
+ * own qkv, table, index and output.  The bias tiles go into a buffer that is part of
+ * the library image, 4 MiB on every GPU that loads the library, held until exit:
+ * crumpet_attention_bias_tiles_bytes(H, N) must not exceed 4 MiB (at most 46 (head,
+ * query tile) tiles at N = 343, 73 at N = 216), else CRUMPET_ERR_UNSUPPORTED.
+ * Each call rebuilds every tile it reads, so nothing depends on an earlier call.
+ * All calls on a GPU share that one buffer: calls that can overlap on the GPU (other
+ * streams, other host threads) race on it; calls on one stream are ordered.
+ * The first call on a device looks up the buffer's device address (with that device
+ * current) and keeps it; make that first call before capturing a stream.
+ * It allocates nothing itself, and nothing it calls does.  No counterpart in the
+ * reference, which allocates its outputs and intermediates through torch.
+ */
+CRUMPET_API int crumpet_swin_window_attention_qkv_static_tiles(
+    void* out, const void* qkv, const void* bias_table, int table_f32, int64_t table_rows,
+    const int64_t* rel_index, int64_t index_stride, int64_t nw_d, int64_t nw_h, int64_t nw_w,
+    int64_t ws_d, int64_t ws_h, int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w,
+    int dtype, int64_t B, int64_t H, int64_t N, int64_t head_dim, float scale, void* stream);
+
+/*
  * LayerNorm, zero padding, cyclic roll by -ss and window partition in one pass:
  * the first half of a Swin block's attention branch.
  *   x      [B, D, H, W, C]  (in_dtype), any D/H/W (not window multiples)
