@@ -25,7 +25,8 @@ import torch
 
 from . import _ops as _native
 from . import profiling as _prof
-from .cache import clear_mask_cache, get_or_compute_mask, make_mask_key, mask_cache_info
+from .cache import (clear_mask_cache, get_or_compute_mask, make_mask_key, mask_cache_info,
+                    remember_mask_geometry)
 from .reference import (
     compute_attn_mask_3d_reference,
     unfused_shift_partition_3d_reference,
@@ -44,6 +45,7 @@ _OP_NAMES = (
     "fused_unshift_unpartition_3d",
     "fused_unshift_unpartition_3d_backward",
     "fused_swin_attention",
+    "fused_swin_attention_shifted",
     "swin_window_attention_qkv",
     "attention_bias_tiles",
     "swin_window_attention_qkv_tiles",
@@ -182,6 +184,10 @@ def compute_attn_mask_3d(
         with _nvtx("crumpet.compute_attn_mask_3d"):
             _native.require().compute_attn_mask_3d(out, *g.dims, *g.window, *g.shift)
             _prof.count("compute_attn_mask_3d")
+        # fused_swin_attention recognises this mask (while nobody writes to it) and adds
+        # it on chip from the window geometry
+        remember_mask_geometry(out, tuple(d // w for d, w in zip(g.dims, g.window)),
+                               g.window, g.shift)
         return out
 
     return get_or_compute_mask(make_mask_key(*g.dims, g.window, g.shift, dtype, dev), compute)

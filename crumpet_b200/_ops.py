@@ -96,6 +96,9 @@ def capi() -> ctypes.CDLL:
             vp, vp, vp, vp, vp, vp, i64, vp, i32, i64, i64, i64, i64, ctypes.c_float, vp,
         ]
         lib.crumpet_fused_swin_attention.restype = i32
+        lib.crumpet_fused_swin_attention_shifted.argtypes = (
+            [vp, vp, vp, vp, vp, vp, i32] + [i64] * 13 + [ctypes.c_float, vp])
+        lib.crumpet_fused_swin_attention_shifted.restype = i32
         lib.crumpet_swin_window_attention_qkv.argtypes = (
             [vp, vp, vp, i32, i64, vp] + [i64] * 10 + [i32] + [i64] * 4 + [ctypes.c_float, vp])
         lib.crumpet_swin_window_attention_qkv.restype = i32

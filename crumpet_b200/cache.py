@@ -14,6 +14,7 @@ thread-safe (callers hold the GIL, as every op wrapper does).
 from __future__ import annotations
 
 import os
+import weakref
 from collections import OrderedDict
 from typing import Callable
 
@@ -126,3 +127,31 @@ def get_or_compute_mask(key: MaskKey, compute: Callable[[], torch.Tensor]) -> to
     value = compute()
     _LRU.insert(key, value)
     return value
+
+
+# Window geometry of the masks compute_attn_mask_3d built, so fused_swin_attention can add
+# such a mask on chip instead of reading it: id(mask) -> (weak reference, torch version
+# counter at creation, (windows per axis, window, shift)).  A mask modified in place since
+# (its version counter moved on) or a copy of it is not recognised and is read as given.
+_GEOMETRY: dict[int, tuple[weakref.ref, int, tuple]] = {}
+
+
+def remember_mask_geometry(mask: torch.Tensor, num_windows, window, shift) -> None:
+    key = id(mask)
+
+    def forget(_ref, key=key):
+        entry = _GEOMETRY.get(key)
+        if entry is not None and entry[0] is _ref:
+            del _GEOMETRY[key]
+
+    ref = weakref.ref(mask, forget)
+    _GEOMETRY[key] = (ref, mask._version, (tuple(num_windows), tuple(window), tuple(shift)))
+
+
+def mask_geometry(mask: torch.Tensor):
+    """(windows per axis, window, shift) of a mask compute_attn_mask_3d built and nobody
+    has written to since, else None."""
+    entry = _GEOMETRY.get(id(mask))
+    if entry is None or entry[0]() is not mask or entry[1] != mask._version:
+        return None
+    return entry[2]

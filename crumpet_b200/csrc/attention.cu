@@ -604,7 +604,12 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
             const uint32_t sb = smem_u32(smem + st * C::STAGE_BYTES);
             // axes on which this window is the last one of a shifted grid
             uint32_t am = 0;
-            if constexpr (MASK == kMaskAnalytic) am = window_last_axes(p, b);
+            if constexpr (MASK == kMaskAnalytic) {
+              am = window_last_axes(p, b);
+              // boundary flags, when the caller gives them, switch the mask off for the
+              // windows they leave unflagged (as they do for a dense mask)
+              if (p.boundary != nullptr && p.boundary[b] == 0) am = 0;
+            }
             const uint32_t q_addr = sb;
             const uint32_t k_addr = sb + C::Q_BYTES;
             const uint32_t v_addr = sb + C::Q_BYTES + C::KV_BYTES;

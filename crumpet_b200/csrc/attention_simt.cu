@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) window_attention_simt_kernel(const S
                                    (long long)(b % p.mask_windows) * p.N * p.N
                              : nullptr;
   uint32_t last_axes = 0;
-  if (p.analytic) {
+  if (p.analytic && (p.boundary == nullptr || p.boundary[b] != 0)) {
     const int wi = b % (p.nwd * p.nwh * p.nww);
     const int iw = wi % p.nww, t = wi / p.nww;
     const int ih = t % p.nwh, id = t / p.nwh;

@@ -155,6 +155,45 @@ int crumpet_fused_swin_attention(void* out, const void* q, const void* k, const 
   return launch_window_attention(a, static_cast<cudaStream_t>(stream));
 }
 
+int crumpet_fused_swin_attention_shifted(void* out, const void* q, const void* k,
+                                         const void* v, const void* rel_bias,
+                                         const uint8_t* boundary, int dtype, int64_t B,
+                                         int64_t H, int64_t N, int64_t head_dim, int64_t nw_d,
+                                         int64_t nw_h, int64_t nw_w, int64_t ws_d, int64_t ws_h,
+                                         int64_t ws_w, int64_t ss_d, int64_t ss_h, int64_t ss_w,
+                                         float scale, void* stream) {
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.qkv_stride_n = head_dim;
+  a.qkv_stride_h = N * head_dim;
+  a.qkv_stride_b = H * N * head_dim;
+  a.out = out;
+  a.out_stride_n = head_dim;
+  a.out_stride_h = N * head_dim;
+  a.out_stride_b = H * N * head_dim;
+  a.bias = rel_bias;
+  a.boundary = boundary;
+  a.analytic = (ss_d | ss_h | ss_w) != 0;
+  a.nwin[0] = nw_d;
+  a.nwin[1] = nw_h;
+  a.nwin[2] = nw_w;
+  a.win[0] = ws_d;
+  a.win[1] = ws_h;
+  a.win[2] = ws_w;
+  a.shift[0] = ss_d;
+  a.shift[1] = ss_h;
+  a.shift[2] = ss_w;
+  a.B = B;
+  a.H = H;
+  a.N = N;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.dtype = dtype;
+  return launch_window_attention(a, static_cast<cudaStream_t>(stream));
+}
+
 int crumpet_swin_window_attention_qkv(void* out, const void* qkv, const void* bias_table,
                                       int table_f32, int64_t table_rows, const int64_t* rel_index,
                                       int64_t index_stride, int64_t nw_d, int64_t nw_h,

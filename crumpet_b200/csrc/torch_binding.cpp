@@ -236,6 +236,51 @@ void attention_bias_tiles(at::Tensor& tiles, const at::Tensor& table, const at::
                                         static_cast<float>(scale), cur_stream(tiles)));
 }
 
+// fused_swin_attention with the shifted-window mask of a window grid computed on chip
+// (crumpet_fused_swin_attention_shifted) in place of a dense mask tensor.
+void fused_swin_attention_shifted(at::Tensor& out, const at::Tensor& q, const at::Tensor& k,
+                                  const at::Tensor& v, const at::Tensor& rel_bias,
+                                  const c10::optional<at::Tensor>& boundary,
+                                  at::IntArrayRef num_windows, at::IntArrayRef window_size,
+                                  at::IntArrayRef shift_size, double scale) {
+  check_cuda_contig(out, "out");
+  check_cuda_contig(q, "q");
+  check_cuda_contig(k, "k");
+  check_cuda_contig(v, "v");
+  check_cuda_contig(rel_bias, "relative_position_bias");
+  TORCH_CHECK(q.dim() == 4 && q.sizes() == k.sizes() && q.sizes() == v.sizes() &&
+                  q.sizes() == out.sizes(),
+              "q, k, v and out must share the shape [B, H, N, head_dim]");
+  const int64_t B = q.size(0), H = q.size(1), N = q.size(2), Dh = q.size(3);
+  TORCH_CHECK(rel_bias.dim() == 3 && rel_bias.size(0) == H && rel_bias.size(1) == N &&
+                  rel_bias.size(2) == N,
+              "relative_position_bias must have shape [H, N, N]");
+  const auto st = q.scalar_type();
+  TORCH_CHECK(k.scalar_type() == st && v.scalar_type() == st && out.scalar_type() == st &&
+                  rel_bias.scalar_type() == st,
+              "q, k, v, out and relative_position_bias must share one dtype");
+  TORCH_CHECK(num_windows.size() == 3 && window_size.size() == 3 && shift_size.size() == 3,
+              "num_windows, window_size and shift_size take three values");
+  same_device(q, k, "k");
+  same_device(q, v, "v");
+  same_device(q, out, "out");
+  same_device(q, rel_bias, "relative_position_bias");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const uint8_t* bnd = nullptr;
+  if (boundary.has_value() && boundary->defined()) {
+    check_cuda_contig(*boundary, "boundary");
+    same_device(q, *boundary, "boundary");
+    TORCH_CHECK(boundary->scalar_type() == at::kByte && boundary->numel() == B,
+                "boundary must be a uint8 tensor of B elements");
+    bnd = boundary->data_ptr<uint8_t>();
+  }
+  check_rc(crumpet_fused_swin_attention_shifted(
+      out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), rel_bias.data_ptr(), bnd,
+      dtype_code(q), B, H, N, Dh, num_windows[0], num_windows[1], num_windows[2],
+      window_size[0], window_size[1], window_size[2], shift_size[0], shift_size[1],
+      shift_size[2], static_cast<float>(scale), cur_stream(q)));
+}
+
 void swin_window_attention_qkv_tiles(at::Tensor& out, const at::Tensor& qkv,
                                      const at::Tensor& tiles, at::IntArrayRef num_windows,
                                      at::IntArrayRef window_size, at::IntArrayRef shift_size,
@@ -565,6 +610,11 @@ TORCH_LIBRARY(crumpet_ops, ops) {
       "Tensor? mask, Tensor? boundary, float scale) -> ()",
       kTags);
   ops.def(
+      "fused_swin_attention_shifted(Tensor! out, Tensor q, Tensor k, Tensor v, Tensor rel_bias, "
+      "Tensor? boundary, int[] num_windows, int[] window_size, int[] shift_size, float scale) "
+      "-> ()",
+      kTags);
+  ops.def(
       "attention_bias_tiles(Tensor! tiles, Tensor table, Tensor index, int N, float scale, "
       "ScalarType dtype) -> ()",
       kTags);
@@ -618,6 +668,7 @@ TORCH_LIBRARY_IMPL(crumpet_ops, CUDA, ops) {
   ops.impl("swin_window_attention_qkv", &swin_window_attention_qkv);
   ops.impl("attention_bias_tiles", &attention_bias_tiles);
   ops.impl("swin_window_attention_qkv_tiles", &swin_window_attention_qkv_tiles);
+  ops.impl("fused_swin_attention_shifted", &fused_swin_attention_shifted);
   ops.impl("norm_shift_partition_3d", &norm_shift_partition_3d);
   ops.impl("unshift_unpartition_crop_3d", &unshift_unpartition_crop_3d);
   ops.impl("unshift_unpartition_crop_norm_3d", &unshift_unpartition_crop_norm_3d);

@@ -26,6 +26,7 @@ import torch
 
 from . import _ops as _native
 from . import profiling as _prof
+from .cache import mask_geometry
 
 _ATTN_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -68,12 +69,21 @@ def fused_swin_attention(
     bias = relative_position_bias.to(q.dtype).contiguous()
     mask_t = None
     bnd = None
+    geometry = None
     if mask is not None:
         if mask.ndim != 3 or tuple(mask.shape[1:]) != (N, N):
             raise ValueError(f"mask must have shape [num_windows, {N}, {N}]")
         if B % int(mask.shape[0]) != 0:
             raise ValueError(f"mask shape {int(mask.shape[0])} incompatible with B={B}")
-        mask_t = mask.to(q.dtype).contiguous()
+        # A mask that compute_attn_mask_3d built (and nobody has written to since) is the
+        # shifted-window mask of a known window grid: the kernel adds it on chip instead of
+        # reading its rows (the same values, up to fp32 rounding)
+        geometry = mask_geometry(mask)
+        if geometry is not None:
+            nw, win, _ = geometry
+            if nw[0] * nw[1] * nw[2] != int(mask.shape[0]) or win[0] * win[1] * win[2] != N:
+                geometry = None
+        mask_t = None if geometry is not None else mask.to(q.dtype).contiguous()
         if boundary is not None:
             bnd = boundary if boundary.dtype == torch.uint8 else boundary.to(torch.uint8)
             bnd = bnd.contiguous()
@@ -83,7 +93,7 @@ def fused_swin_attention(
     token = None
     if _prof._active:
         esize = q.element_size()
-        masked = 0 if mask_t is None else (B if bnd is None else bnd)
+        masked = 0 if mask_t is None else (B if bnd is None else bnd)  # rows read from HBM
         token = _prof.kernel_begin("fused_swin_attention", {
             # algorithmic bytes: q, k, v, out, the bias once, plus the mask rows
             # of masked windows (resolved when the timer is summarised)
@@ -92,7 +102,11 @@ def fused_swin_attention(
             "flops": 4 * B * H * N * N * D,
             "exps": B * H * N * N,
         })
-    ops.fused_swin_attention(out, q, k, v, bias, mask_t, bnd, float(scale))
+    if geometry is not None:
+        ops.fused_swin_attention_shifted(out, q, k, v, bias, bnd, list(geometry[0]),
+                                         list(geometry[1]), list(geometry[2]), float(scale))
+    else:
+        ops.fused_swin_attention(out, q, k, v, bias, mask_t, bnd, float(scale))
     _prof.count("fused_swin_attention")
     _prof.kernel_end(token)
     return out

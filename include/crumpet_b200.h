@@ -129,6 +129,27 @@ CRUMPET_API int crumpet_fused_swin_attention(void* out, const void* q, const voi
                                  int64_t N, int64_t head_dim, float scale, void* stream);
 
 /*
+ * crumpet_fused_swin_attention with, in place of a dense mask tensor, the shifted-window
+ * mask that crumpet_compute_attn_mask_3d builds for the window grid
+ *   nw_* windows per axis of one batch entry (window b is b % (nw_d*nw_h*nw_w)),
+ *   ws_* window size (ws_d*ws_h*ws_w == N), ss_* cyclic shift (all 0: no mask),
+ * computed on chip instead of read from memory (-100 where two tokens of a window come
+ * from different roll regions).  boundary: uint8 [B] or NULL, as for
+ * crumpet_fused_swin_attention: windows with boundary[b] == 0 are treated as unmasked.
+ * The same function as crumpet_fused_swin_attention given that mask tensor, up to fp32
+ * rounding, without the mask's HBM reads (645 MB at a 98^3 grid of 7^3 windows).  No
+ * reference counterpart: the reference reads the mask tensor
+ * (torch-ext/crumpet/fused_attention.py:123-129); crumpet_b200.fused_swin_attention
+ * routes here when the mask it is given is one that compute_attn_mask_3d returned and
+ * that has not been modified since.
+ */
+CRUMPET_API int crumpet_fused_swin_attention_shifted(
+    void* out, const void* q, const void* k, const void* v, const void* rel_bias,
+    const uint8_t* boundary, int dtype, int64_t B, int64_t H, int64_t N, int64_t head_dim,
+    int64_t nw_d, int64_t nw_h, int64_t nw_w, int64_t ws_d, int64_t ws_h, int64_t ws_w,
+    int64_t ss_d, int64_t ss_h, int64_t ss_w, float scale, void* stream);
+
+/*
  * Fused window attention straight from the packed qkv Linear output, with the
  * relative-position bias gathered in-kernel and the shifted-window mask
  * computed on chip -- the whole body of MONAI's WindowAttention.forward
