@@ -136,7 +136,19 @@ def get_or_compute_mask(key: MaskKey, compute: Callable[[], torch.Tensor]) -> to
 _GEOMETRY: dict[int, tuple[weakref.ref, int, tuple]] = {}
 
 
+def _version(t: torch.Tensor):
+    # inference tensors keep no version counter: writes to them cannot be seen, so they
+    # are never recognised
+    try:
+        return t._version
+    except RuntimeError:
+        return None
+
+
 def remember_mask_geometry(mask: torch.Tensor, num_windows, window, shift) -> None:
+    version = _version(mask)
+    if version is None:
+        return
     key = id(mask)
 
     def forget(_ref, key=key):
@@ -145,13 +157,13 @@ def remember_mask_geometry(mask: torch.Tensor, num_windows, window, shift) -> No
             del _GEOMETRY[key]
 
     ref = weakref.ref(mask, forget)
-    _GEOMETRY[key] = (ref, mask._version, (tuple(num_windows), tuple(window), tuple(shift)))
+    _GEOMETRY[key] = (ref, version, (tuple(num_windows), tuple(window), tuple(shift)))
 
 
 def mask_geometry(mask: torch.Tensor):
     """(windows per axis, window, shift) of a mask compute_attn_mask_3d built and nobody
     has written to since, else None."""
     entry = _GEOMETRY.get(id(mask))
-    if entry is None or entry[0]() is not mask or entry[1] != mask._version:
+    if entry is None or entry[0]() is not mask or entry[1] != _version(mask):
         return None
     return entry[2]

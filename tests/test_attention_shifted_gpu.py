@@ -109,3 +109,17 @@ def test_shifted_entry_through_the_c_abi(cuda_device):
     want = crumpet.fused_swin_attention(q, k, v, bias, mask.clone(), None)
     torch.cuda.synchronize()
     assert (out.float() - want.float()).abs().max().item() <= TOL[torch.float16]
+
+
+def test_masks_built_in_inference_mode_are_read(cuda_device):
+    # inference tensors keep no version counter, so such a mask is always read as given
+    try:
+        with torch.inference_mode():
+            q, k, v, bias, mask = _inputs(cuda_device, (10, 10, 10), (5, 5, 5), (2, 2, 2), 2, 1,
+                                          torch.float16, seed=3)
+            assert mask_geometry(mask) is None
+            got = crumpet.fused_swin_attention(q, k, v, bias, mask, None)
+            want = crumpet.fused_swin_attention(q, k, v, bias, mask.clone(), None)
+        assert torch.equal(got, want)
+    finally:
+        crumpet.clear_mask_cache()

@@ -30,3 +30,10 @@ def test_registry_forgets_collected_masks():
     del m
     gc.collect()
     assert key not in cache._GEOMETRY
+
+
+def test_inference_tensors_are_never_recognised():
+    with torch.inference_mode():
+        m = torch.zeros(8, 343, 343)
+    remember_mask_geometry(m, (2, 2, 2), (7, 7, 7), (3, 3, 3))  # must not raise
+    assert mask_geometry(m) is None
