@@ -163,6 +163,8 @@ def remember_mask_geometry(mask: torch.Tensor, num_windows, window, shift) -> No
 def mask_geometry(mask: torch.Tensor):
     """(windows per axis, window, shift) of a mask compute_attn_mask_3d built and nobody
     has written to since, else None."""
+    if torch.compiler.is_compiling():
+        return None  # traced code keeps the plain mask-reading call
     entry = _GEOMETRY.get(id(mask))
     if entry is None or entry[0]() is not mask or entry[1] != _version(mask):
         return None
