@@ -71,9 +71,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 15.f;  // P = 2^(x - m_ref) stays <= 2^15 (fp16 max 65504)
 constexpr float kLog2e = 1.4426950408889634f;
 // every kPolyEvery-th pair of exponentials is computed on the FMA pipe (poly_ex2x2); at
-// stage 0, 1 in 8 shortened the kernel by 1.5-2 %, 1 in 4 left it unchanged and 1 in 2
-// lengthened it by 6 % (0 puts every exponential on the SFU)
-constexpr int kPolyEvery = 8;
+// stage 0 (ncu medians against all on the SFU) 1 in 6 shortened the kernel by 1.5 %, 1 in 8
+// by 1.1 %, 1 in 4 left it unchanged and 1 in 2 lengthened it by 6 % (0: all on the SFU)
+constexpr int kPolyEvery = 6;
 
 // Per (padded key count, head dim) layout.  A head dim of 32 is two 16-channel
 // atoms: Q, K and V are loaded as one TMA box per atom into separate regions, QK^T
