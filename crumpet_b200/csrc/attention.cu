@@ -191,7 +191,8 @@ __device__ __forceinline__ float fast_ex2(float x) {
 
 // 2^x for a pair of scores on the FMA pipe instead of the MUFU unit, so the softmax's
 // exponentials are not all queued on the SFU: x is clamped to [-125, +inf) (P stays at most
-// 2^15 here, and anything below 2^-125 rounds to 0 in the 16-bit P), split as x = n + f with
+// 2^15 here; below the clamp an fp16 P rounds to 0, while a bf16 P keeps 2^-125, about 1e-38
+// of the row's largest term, where the SFU gives 0), split as x = n + f with
 // n the nearest integer (the 1.5 * 2^23 rounding constant) and f in [-0.5, 0.5], 2^f taken
 // from a cubic fitted for this kernel (minimax by Lawson-reweighted least squares on
 // Chebyshev nodes; relative error below 7.5e-5 on [-0.5, 0.5], under half a 16-bit ulp),
