@@ -67,6 +67,7 @@ constexpr int kSmThreads = kNumWG * 4 * 32;            // softmax threads (one p
 constexpr int kThreads = kCtrlWarps * 32 + kSmThreads;  // 512
 constexpr int kRowBytes = kAtom * 2;  // one atom row: 16 channels of fp16/bf16
 constexpr int kBarsPerWG = 9;
+constexpr int kSchedWords = 7;  // the CTA's work list in shared memory (store_sched)
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 15.f;  // P = 2^(x - m_ref) stays <= 2^15 (fp16 max 65504)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -121,7 +122,8 @@ struct Cfg {
   static constexpr int IDENT_BYTES = 512;             // 16x16 identity, UMMA B operand
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BIAS_BYTES + ONES_BYTES +
                                     IDENT_BYTES + MASKA_BYTES + MASKB_BYTES +
-                                    (2 * STAGES + kNumWG * kBarsPerWG + 1) * 8 + 64 + 4 * STAGES;
+                                    (2 * STAGES + kNumWG * kBarsPerWG + 1) * 8 + 64 + 4 * STAGES +
+                                    4 * kSchedWords;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
@@ -153,23 +155,73 @@ struct KParams {
   int stall_loads;
 };
 
-// Work list of one CTA: `pair_count` (head, query-tile) pairs starting at
-// pair_begin with stride pair_step; inside each pair the windows
-// win_begin, win_begin + win_step, ...  Tile k of the CTA (in that order) goes to WG k % kNumWG.
+// Work list of one CTA: `pair_count` (head, query-tile) pairs starting at pair_begin
+// with stride pair_step; inside each pair the windows lo, lo + win_step, ... below hi
+// (pair_windows).  Tile k of the CTA (in that order) goes to WG k % kNumWG.
 struct Sched {
-  int pair_begin, pair_step, pair_count, win_begin, win_step;
+  int pair_begin, pair_step, pair_count;
+  int win_begin, win_step;   // every pair but the first and last: win_begin .. B - 1
+  int first_begin, last_end;  // the first pair starts at first_begin, the last ends at last_end
 };
 
-__device__ __forceinline__ Sched make_sched(int P) {
+// The CTA keeps its Sched in shared memory (kSchedWords words) and reads it at pair
+// boundaries only, so none of it stays live in registers through the tile loops.
+
+__device__ __forceinline__ void store_sched(int* dst, const Sched& s) {
+  dst[0] = s.pair_begin;
+  dst[1] = s.pair_step;
+  dst[2] = s.pair_count;
+  dst[3] = s.win_begin;
+  dst[4] = s.win_step;
+  dst[5] = s.first_begin;
+  dst[6] = s.last_end;
+}
+
+__device__ __forceinline__ int sched_pairs(const volatile int* s) { return s[2]; }
+
+// pair pi of the CTA: its index and its windows lo, lo + step, ... below hi
+__device__ __forceinline__ void pair_windows(const volatile int* s, int pi, int B, int& pair,
+                                             int& lo, int& hi, int& step) {
+  pair = s[0] + pi * s[1];
+  lo = pi == 0 ? s[5] : s[3];
+  hi = pi == s[2] - 1 ? s[6] : B;
+  step = s[4];
+}
+
+// With P <= G pairs, S = G / P CTAs share each pair's windows (window b goes to CTA b % S
+// of the pair, so the CTAs of one head's query tiles walk the same windows in step and
+// meet its K/V rows in L2).  When the bias tiles are prebuilt (`helpers`), the X = G - P * S
+// CTAs left over take the last e windows of every pair, split evenly in pair order.  A
+// helper's share spans about P / X + 1 pairs, and each pair it starts costs a bias-tile copy
+// and a pipeline refill, counted as 6 tiles, so e is the largest value with
+//   P e / X + 6 (P / X + 1) <= (B - e) / S,
+// i.e. e = (X B - 6 S (P + X)) / (P S + X): the helpers finish no later than the sharing
+// CTAs, which now walk B - e windows.  (A bias tile gathered in the kernel costs several
+// times that copy, so without prebuilt tiles the leftover CTAs stay idle.)  With P > G
+// each CTA takes whole pairs c, c + G, ...
+__device__ __forceinline__ Sched make_sched(int P, int B, bool helpers) {
   const int G = gridDim.x, c = blockIdx.x;
-  Sched s{0, 1, 0, 0, 1};
+  Sched s{0, 1, 0, 0, 1, 0, B};
   if (P <= G) {
-    const int S = G / P;
+    const int S = G / P, X = G - P * S;
+    const int64_t room = int64_t(X) * B - int64_t(6) * S * (P + X);
+    const int e = (helpers && room > 0) ? int(room / (int64_t(P) * S + X)) : 0;
     if (c < P * S) {
       s.pair_begin = c / S;
       s.pair_count = 1;
-      s.win_begin = c % S;
       s.win_step = S;
+      s.first_begin = c % S;
+      s.last_end = B - e;
+    } else if (e > 0) {
+      const int64_t items = int64_t(P) * e, j = c - P * S;
+      const int t0 = int(j * items / X), t1 = int((j + 1) * items / X);
+      if (t1 > t0) {
+        s.pair_begin = t0 / e;
+        s.pair_count = (t1 - 1) / e - t0 / e + 1;
+        s.win_begin = B - e;
+        s.first_begin = B - e + t0 % e;
+        s.last_end = B - e + (t1 - 1) % e + 1;
+      }
     }
   } else {
     s.pair_begin = c;
@@ -431,11 +483,15 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
   // the TMA warp to announce tile k in this word, which implies the previous
   // phase has completed, and only then waits on the barrier's parity.
   volatile int* stage_tile = abort_flag + 1;
+  volatile int* sched_s = stage_tile + kStages;  // this CTA's Sched (store_sched)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const Sched sc = make_sched(p.P);
-  if (sc.pair_count == 0) return;  // uniform for the CTA
+  {
+    const Sched sc = make_sched(p.P, p.B, p.bias_tiles != nullptr);
+    if (sc.pair_count == 0) return;  // uniform for the CTA
+    if (threadIdx.x == 0) store_sched(const_cast<int*>(sched_s), sc);
+  }
 
   // Barriers: the stage ring [load_full x kStages][load_empty x kStages], then per WG
   //           [s_full][s_empty][p_full][p_empty][o_full][o_empty][drain]
@@ -521,10 +577,11 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         tma_prefetch_map(&tv);
         uint32_t k = 0;
         bool ok = true;
-        for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
-          const int pair = sc.pair_begin + pi * sc.pair_step;
+        for (int pi = 0; pi < sched_pairs(sched_s) && ok; ++pi) {
+          int pair, lo, hi, step;
+          pair_windows(sched_s, pi, p.B, pair, lo, hi, step);
           const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
-          for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k) {
+          for (int b = lo; b < hi && ok; b += step, ++k) {
             const int st = int(k % kStages);
             const uint32_t ph = (k / kStages) & 1u;
             if (!mbar_wait(load_empty + st, ph ^ 1u, abort_flag)) {
@@ -612,12 +669,15 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
         const uint64_t ident_desc = smem_desc(smem_u32(ident_s), 256, 128, kLayoutNone);
         constexpr uint32_t idesc_bias = idesc_f16(kBM, 16, BF16, false);
         uint32_t k = 0;
-        for (int pi = 0; pi < sc.pair_count && ok; ++pi) {
+        for (int pi = 0; pi < sched_pairs(sched_s) && ok; ++pi) {
           if (!mbar_wait(bias_ready, uint32_t(pi) & 1u, abort_flag)) {
             ok = false;
             break;
           }
-          for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k) {
+          int pair, lo, hi, step;
+          pair_windows(sched_s, pi, p.B, pair, lo, hi, step);
+          (void)pair;
+          for (int b = lo; b < hi && ok; b += step, ++k) {
             if (int(k % kNumWG) != w) continue;
             const int st = int(k % kStages);
             const uint32_t ph = (k / kStages) & 1u;
@@ -709,8 +769,10 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
     uint32_t k_tile = 0;  // tile index within the CTA (shared numbering with the TMA/MMA warps)
     bool ok = true;
 
-    for (int pi = 0; pi < sc.pair_count; ++pi) {
-      const int pair = sc.pair_begin + pi * sc.pair_step;
+    const int npairs = sched_pairs(sched_s);
+    for (int pi = 0; pi < npairs; ++pi) {
+      int pair, lo, hi, step;
+      pair_windows(sched_s, pi, p.B, pair, lo, hi, step);
       const int h = pair / p.MT, mt = pair - (pair / p.MT) * p.MT;
       // Relative-position bias tile of this (head, query tile) for the bias MMA: copied
       // from prebuilt tiles when the caller has them, else gathered here.
@@ -752,7 +814,7 @@ window_attention_kernel(const __grid_constant__ CUtensorMap tq,
       const bool valid = qrow < p.N;
       const bool warp_live = (mt * kBM + quarter * 32) < p.N;  // uniform per warp
 
-      for (int b = sc.win_begin; b < p.B && ok; b += sc.win_step, ++k_tile) {
+      for (int b = lo; b < hi && ok; b += step, ++k_tile) {
         if (int(k_tile % kNumWG) != w) continue;
         // ---- per-tile mask state
         bool use_dense = false;
