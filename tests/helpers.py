@@ -24,6 +24,27 @@ def header_functions() -> list[str]:
     return re.findall(r"CRUMPET_API\s+[\w\s\*]+?\b(crumpet_\w+)\s*\(", text)
 
 
+def header_prototypes() -> dict[str, tuple[str, list[str]]]:
+    """name -> (return type, parameter types) of every function include/crumpet_b200.h
+    declares, comments stripped and parameter names dropped."""
+    text = (ROOT / "include" / "crumpet_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", " ", text)
+    protos = {}
+    for ret, name, params in re.findall(
+            r"CRUMPET_API\s+([\w\s\*]+?)\s*\b(crumpet_\w+)\s*\(([^)]*)\)\s*;", text):
+        types = []
+        for param in params.split(","):
+            param = " ".join(param.split())
+            if param in ("", "void"):
+                continue
+            # drop the parameter name: the last identifier, unless the type ends in '*'
+            m = re.fullmatch(r"(.*?[\s\*])(\w+)", param)
+            types.append(" ".join(m.group(1).split()) if m else param)
+        protos[name] = (" ".join(ret.split()), types)
+    return protos
+
+
 def ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 

@@ -412,3 +412,33 @@ def test_loader_reload_is_idempotent():
     crumpet._register_fake_impls()
     crumpet._register_fake_impls()
     assert _ops.available()
+
+
+def _ctype_of(c_type: str):
+    """The ctypes class a C parameter or return type of the header must be bound as."""
+    if c_type.replace(" ", "") == "constchar*":
+        return ctypes.c_char_p
+    if "*" in c_type:
+        return ctypes.c_void_p
+    base = c_type.replace("const ", "").strip()
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float}[base]
+
+
+def test_ctypes_bindings_match_the_header():
+    """Every function of include/crumpet_b200.h is bound in _ops.capi() with exactly the
+    header's parameter list and return type (a wrong count or width would pass garbage to
+    the kernels without any error)."""
+    from helpers import header_prototypes
+
+    protos = header_prototypes()
+    assert set(protos) == set(header_functions())
+    lib = _ops.capi()
+    for name, (ret, params) in protos.items():
+        fn = getattr(lib, name)
+        assert fn.argtypes is not None, f"{name} has no argtypes"
+        want = [_ctype_of(t) for t in params]
+        got = list(fn.argtypes)
+        assert len(got) == len(want), (name, len(got), len(want))
+        for i, (g, w) in enumerate(zip(got, want)):
+            assert g is w, (name, i, params[i], g, w)
+        assert fn.restype is _ctype_of(ret), (name, ret, fn.restype)
