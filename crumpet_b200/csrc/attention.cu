@@ -166,7 +166,6 @@ struct Sched {
 
 // The CTA keeps its Sched in shared memory (kSchedWords words) and reads it at pair
 // boundaries only, so none of it stays live in registers through the tile loops.
-
 __device__ __forceinline__ void store_sched(int* dst, const Sched& s) {
   dst[0] = s.pair_begin;
   dst[1] = s.pair_step;
